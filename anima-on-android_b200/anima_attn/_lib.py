@@ -1,0 +1,91 @@
+"""ctypes binding of libanima_attn.so (include/anima_rt.h, include/anima_attn.h).
+
+The shared library is built in-tree by ``build.py`` next to this file.  There is no
+fallback: if the library is missing or does not load, importing the package raises.
+"""
+from __future__ import annotations
+
+import ctypes as ct
+import os
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "libanima_attn.so")
+
+# status codes and flags (anima_attn.h)
+OK, ERR_ARG, ERR_SHAPE, ERR_CUDA, ERR_TIMEOUT, ERR_UNSUPPORTED, ERR_NOMEM = 0, -1, -2, -3, -4, -5, -6
+DTYPE_F32, DTYPE_BF16, DTYPE_F16 = 0, 1, 2
+FLAG_QNORM, FLAG_KNORM, FLAG_ROPE, FLAG_MASK, FLAG_CAUSAL = 0x1, 0x2, 0x4, 0x8, 0x10
+
+ERR_NAMES = {OK: "ok", ERR_ARG: "bad argument", ERR_SHAPE: "unsupported shape",
+             ERR_CUDA: "CUDA error", ERR_TIMEOUT: "device-side wait timed out",
+             ERR_UNSUPPORTED: "unsupported device", ERR_NOMEM: "out of device memory"}
+
+_P = ct.c_void_p
+_I64x3 = ct.c_int64 * 3
+
+
+class PrologueArgs(ct.Structure):
+    _fields_ = [("q", _P), ("k", _P), ("v", _P), ("in_dtype", ct.c_int),
+                ("q_stride", _I64x3), ("k_stride", _I64x3), ("v_stride", _I64x3),
+                ("B", ct.c_int), ("H", ct.c_int), ("S_q", ct.c_int), ("S_kv", ct.c_int),
+                ("D", ct.c_int), ("q_norm_w", _P), ("k_norm_w", _P), ("eps", ct.c_float),
+                ("rope_freqs", _P), ("flags", ct.c_uint), ("q_out", _P), ("k_out", _P),
+                ("v_out", _P), ("op_dtype", ct.c_int)]
+
+
+class AttnArgs(ct.Structure):
+    _fields_ = [("q", _P), ("k", _P), ("v", _P), ("op_dtype", ct.c_int), ("out", _P),
+                ("out_dtype", ct.c_int), ("out_stride", _I64x3), ("B", ct.c_int),
+                ("H", ct.c_int), ("S_q", ct.c_int), ("S_kv", ct.c_int), ("D", ct.c_int),
+                ("scale", ct.c_float), ("flags", ct.c_uint), ("kv_valid_len", _P)]
+
+
+# Every symbol the headers declare, with its ctypes signature.
+SIGNATURES = {
+    # include/anima_rt.h -- argtypes as the reference binds them (anima_rt_ops.py:11-34)
+    "anima_rt_init": ([], ct.c_bool),
+    "anima_rt_destroy": ([], None),
+    "anima_rt_run_sdpa_flash": ([_P] * 4 + [ct.c_int] * 4 + [ct.c_float, ct.c_bool], ct.c_bool),
+    "anima_rt_run_sdpa": ([_P] * 4 + [ct.c_int] * 4 + [ct.c_float, ct.c_bool], ct.c_bool),
+    "anima_rt_run_rmsnorm": ([_P, _P, _P, ct.c_int, ct.c_int, ct.c_float], ct.c_bool),
+    "anima_rt_run_rope": ([_P, _P, _P, ct.c_int, ct.c_int, ct.c_int], ct.c_bool),
+    "anima_rt_run_attention": ([_P] * 8 + [ct.c_int] * 5 + [ct.c_float, ct.c_float, ct.c_uint],
+                               ct.c_bool),
+    "anima_rt_last_error": ([], ct.c_char_p),
+    # include/anima_attn.h
+    "anima_attn_prologue": ([ct.POINTER(PrologueArgs), _P], ct.c_int),
+    "anima_attn_fwd": ([ct.POINTER(AttnArgs), _P], ct.c_int),
+    "anima_attn_status": ([_P, ct.c_int], ct.c_int),
+    "anima_attn_device_info": ([ct.POINTER(ct.c_int), ct.POINTER(ct.c_int)], ct.c_int),
+    "anima_attn_version": ([], ct.c_char_p),
+}
+
+
+def load(path: str = LIB_PATH) -> ct.CDLL:
+    if not os.path.exists(path):
+        raise ImportError(
+            f"{path} is missing: build the CUDA library first "
+            "(python -c 'import __graft_entry__ as g; g.build()' from the repository root)")
+    lib = ct.CDLL(path)
+    for name, (args, res) in SIGNATURES.items():
+        fn = getattr(lib, name)
+        fn.argtypes = args
+        fn.restype = res
+    return lib
+
+
+lib = load()
+
+
+class AnimaError(RuntimeError):
+    pass
+
+
+def check(rc: int, what: str) -> None:
+    if rc != OK:
+        raise AnimaError(f"{what} failed: {ERR_NAMES.get(rc, rc)}")
+
+
+def last_error() -> str:
+    s = lib.anima_rt_last_error()
+    return s.decode() if s else ""

@@ -1,0 +1,207 @@
+"""Torch-tensor front end of the B200 attention library.
+
+All tensors are CUDA tensors on the current device; every call is enqueued on the
+current torch stream and returns without synchronising.  The kernels run in
+libanima_attn.so (sm_100a); there is no PyTorch or CPU fallback.
+
+Layouts follow the reference call sites:
+  * projections q/k/v as produced by ``rearrange(t, "b s (h d) -> b s h d")``
+    (src/predict2.py:177-180, anima_rt/scripts/numpy_dit.py:283): [B, S, H, D];
+  * operands of the attention core: [B*H, S, D] 16-bit (the anima_rt [BH, S, D]
+    layout, anima_rt/src/anima_rt.cpp:142-145);
+  * output [B, S, H, D] (what the o-proj consumes, numpy_dit.py:294) or [B, H, S, D]
+    (what F.scaled_dot_product_attention returns, predict2.py:25-29).
+"""
+from __future__ import annotations
+
+import ctypes as ct
+import math
+from typing import Optional
+
+import torch
+
+from . import _lib as L
+
+_TORCH_DT = {torch.float32: L.DTYPE_F32, torch.bfloat16: L.DTYPE_BF16, torch.float16: L.DTYPE_F16}
+
+
+def _stream() -> int:
+    return torch.cuda.current_stream().cuda_stream
+
+
+def _ptr(t: Optional[torch.Tensor]):
+    return None if t is None else ct.c_void_p(t.data_ptr())
+
+
+def _check_cuda(*ts):
+    for t in ts:
+        if t is not None and not t.is_cuda:
+            raise ValueError("anima_attn ops take CUDA tensors")
+
+
+def _as_weight(w: Optional[torch.Tensor], device) -> Optional[torch.Tensor]:
+    if w is None:
+        return None
+    return w.detach().to(device=device, dtype=torch.float32).contiguous()
+
+
+def prologue(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
+             q_norm_w: Optional[torch.Tensor] = None, k_norm_w: Optional[torch.Tensor] = None,
+             rope_freqs: Optional[torch.Tensor] = None, eps: float = 1e-6,
+             norm_q: bool = True, norm_k: bool = True, op_dtype=torch.bfloat16,
+             out: Optional[tuple] = None):
+    """Fused per-head RMSNorm + 3D RoPE + cast + transpose, one HBM pass.
+
+    q [B, S_q, H, D], k/v [B, S_kv, H, D] (fp32/bf16/fp16, any strides with D
+    contiguous) -> (q, k, v) [B*H, S, D] in ``op_dtype``.  ``norm_q``/``norm_k`` apply
+    RMSNorm (weights may be None = 1); ``rope_freqs`` [S, D/2, 2, 2] fp32 rotates q and k.
+    Replaces numpy_dit.py:285-291 / predict2.py:182-193.
+    """
+    _check_cuda(q, k, v)
+    B, Sq, H, D = q.shape
+    Skv = k.shape[1]
+    if k.shape != (B, Skv, H, D) or v.shape != k.shape:
+        raise ValueError("k and v must be [B, S_kv, H, D] matching q")
+    if q.dtype not in _TORCH_DT or k.dtype != q.dtype or v.dtype != q.dtype:
+        raise ValueError("q, k, v must share one of float32/bfloat16/float16")
+    for t in (q, k, v):
+        if t.stride(3) != 1:
+            raise ValueError("the head dimension must be contiguous")
+    dev = q.device
+    if out is None:
+        qo = torch.empty((B * H, Sq, D), device=dev, dtype=op_dtype)
+        ko = torch.empty((B * H, Skv, D), device=dev, dtype=op_dtype)
+        vo = torch.empty((B * H, Skv, D), device=dev, dtype=op_dtype)
+    else:
+        qo, ko, vo = out
+    qw, kw = _as_weight(q_norm_w, dev), _as_weight(k_norm_w, dev)
+    fr = None
+    flags = (L.FLAG_QNORM if norm_q else 0) | (L.FLAG_KNORM if norm_k else 0)
+    if rope_freqs is not None:
+        fr = rope_freqs.detach().to(device=dev, dtype=torch.float32).reshape(-1).contiguous()
+        if fr.numel() != Sq * D * 2:
+            raise ValueError("rope_freqs must hold [S_q, D/2, 2, 2] values")
+        flags |= L.FLAG_ROPE
+    a = L.PrologueArgs()
+    a.q, a.k, a.v = _ptr(q), _ptr(k), _ptr(v)
+    a.in_dtype = _TORCH_DT[q.dtype]
+    for name, t in (("q_stride", q), ("k_stride", k), ("v_stride", v)):
+        getattr(a, name)[:] = [t.stride(0), t.stride(1), t.stride(2)]
+    a.B, a.H, a.S_q, a.S_kv, a.D = B, H, Sq, Skv, D
+    a.q_norm_w, a.k_norm_w = _ptr(qw), _ptr(kw)
+    a.eps = float(eps)
+    a.rope_freqs = _ptr(fr)
+    a.flags = flags
+    a.q_out, a.k_out, a.v_out = _ptr(qo), _ptr(ko), _ptr(vo)
+    a.op_dtype = _TORCH_DT[op_dtype]
+    # qw/kw/fr may be freed on return: the caching allocator hands their blocks only to
+    # work enqueued later on this stream, which runs after the kernel.
+    L.check(L.lib.anima_attn_prologue(ct.byref(a), ct.c_void_p(_stream())), "anima_attn_prologue")
+    return qo, ko, vo
+
+
+def attention_core(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, B: int, H: int,
+                   scale: Optional[float] = None, kv_valid_len: Optional[torch.Tensor] = None,
+                   causal: bool = False, out: Optional[torch.Tensor] = None,
+                   out_layout: str = "bshd", out_dtype=torch.float32) -> torch.Tensor:
+    """tcgen05 flash attention on 16-bit head-major operands.
+
+    q [B*H, S_q, 128], k/v [B*H, S_kv, 128] contiguous bf16/fp16.  Returns (or fills)
+    ``out`` in ``out_layout`` "bshd" [B, S_q, H, D] or "bhsd" [B, H, S_q, D].
+    ``kv_valid_len`` int32 [B] masks keys >= kv_valid_len[b] (cross-attention padding).
+    """
+    _check_cuda(q, k, v)
+    BH, Sq, D = q.shape
+    Skv = k.shape[1]
+    if BH != B * H or k.shape != (BH, Skv, D) or v.shape != k.shape:
+        raise ValueError("operands must be [B*H, S, D]")
+    if q.dtype not in (torch.bfloat16, torch.float16) or k.dtype != q.dtype or v.dtype != q.dtype:
+        raise ValueError("operands must be bfloat16 or float16")
+    if not (q.is_contiguous() and k.is_contiguous() and v.is_contiguous()):
+        raise ValueError("operands must be contiguous")
+    if out is None:
+        shape = (B, Sq, H, D) if out_layout == "bshd" else (B, H, Sq, D)
+        out = torch.empty(shape, device=q.device, dtype=out_dtype)
+    if out_layout == "bshd":
+        st = (out.stride(0), out.stride(2), out.stride(1))
+    elif out_layout == "bhsd":
+        st = (out.stride(0), out.stride(1), out.stride(2))
+    else:
+        raise ValueError("out_layout must be 'bshd' or 'bhsd'")
+    if out.stride(3) != 1:
+        raise ValueError("output head dimension must be contiguous")
+    flags = L.FLAG_CAUSAL if causal else 0
+    vl = None
+    if kv_valid_len is not None:
+        vl = kv_valid_len.to(device=q.device, dtype=torch.int32).contiguous()
+        if vl.numel() != B:
+            raise ValueError("kv_valid_len must have B entries")
+        flags |= L.FLAG_MASK
+    a = L.AttnArgs()
+    a.q, a.k, a.v = _ptr(q), _ptr(k), _ptr(v)
+    a.op_dtype = _TORCH_DT[q.dtype]
+    a.out = _ptr(out)
+    a.out_dtype = _TORCH_DT[out.dtype]
+    a.out_stride[:] = list(st)
+    a.B, a.H, a.S_q, a.S_kv, a.D = B, H, Sq, Skv, D
+    a.scale = float(1.0 / math.sqrt(D) if scale is None else scale)
+    a.flags = flags
+    a.kv_valid_len = _ptr(vl)
+    L.check(L.lib.anima_attn_fwd(ct.byref(a), ct.c_void_p(_stream())), "anima_attn_fwd")
+    return out
+
+
+def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
+              q_norm_w: Optional[torch.Tensor] = None, k_norm_w: Optional[torch.Tensor] = None,
+              rope_freqs: Optional[torch.Tensor] = None,
+              kv_valid_len: Optional[torch.Tensor] = None, norm_q: bool = True,
+              norm_k: bool = True, causal: bool = False, scale: Optional[float] = None,
+              eps: float = 1e-6, out_dtype=torch.float32, op_dtype=torch.bfloat16,
+              workspace: Optional[tuple] = None, out: Optional[torch.Tensor] = None):
+    """The attention of one DiT block from projections to o-proj input.
+
+    q [B, S_q, H, D], k/v [B, S_kv, H, D] pre-norm projections -> [B, S_q, H, D]:
+    q/k RMSNorm, RoPE (self-attention), SDPA with optional key-padding mask.  This is
+    NumpyAttention.forward between the projection and o-proj GEMMs
+    (numpy_dit.py:285-294) and predict2 Attention.compute_qkv's norm/RoPE plus
+    torch_attention_op (predict2.py:182-193, 61-88).
+    """
+    B, Sq, H, D = q.shape
+    qh, kh, vh = prologue(q, k, v, q_norm_w, k_norm_w, rope_freqs, eps, norm_q, norm_k,
+                          op_dtype, out=workspace)
+    return attention_core(qh, kh, vh, B, H, scale, kv_valid_len, causal, out=out,
+                          out_layout="bshd", out_dtype=out_dtype)
+
+
+def sdpa(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, scale: Optional[float] = None,
+         is_causal: bool = False, op_dtype=torch.bfloat16) -> torch.Tensor:
+    """F.scaled_dot_product_attention on [B, H, S, D] tensors (predict2.py:25-29).
+
+    Returns [B, H, S_q, D] in q's dtype (fp32 for fp32 inputs)."""
+    B, H, Sq, D = q.shape
+    Skv = k.shape[2]
+    # [B, H, S, D] viewed as [B, S, H, D] with swapped strides: the prologue reads any
+    # strides, so no transpose copy is made.
+    qv, kv, vv = (t.transpose(1, 2) for t in (q, k, v))
+    if q.dtype not in _TORCH_DT:
+        raise ValueError("unsupported dtype")
+    qh, kh, vh = prologue(qv, kv, vv, norm_q=False, norm_k=False, op_dtype=op_dtype)
+    out_dtype = torch.bfloat16 if q.dtype == torch.bfloat16 else torch.float32
+    o = attention_core(qh, kh, vh, B, H, scale, None, is_causal, out_layout="bhsd",
+                       out_dtype=out_dtype)
+    return o if o.dtype == q.dtype else o.to(q.dtype)
+
+
+def status(reset: bool = True) -> int:
+    """Synchronise the current stream and return the device status word (0 = clean)."""
+    return L.lib.anima_attn_status(ct.c_void_p(_stream()), int(reset))
+
+
+def device_info():
+    sm, cc = ct.c_int(0), ct.c_int(0)
+    L.check(L.lib.anima_attn_device_info(ct.byref(sm), ct.byref(cc)), "anima_attn_device_info")
+    return sm.value, cc.value
+
+
+def version() -> str:
+    return L.lib.anima_attn_version().decode()

@@ -1,0 +1,417 @@
+// abi.cu -- the library's C ABI (include/anima_rt.h, include/anima_attn.h).
+//
+// Two layers:
+//  * anima_attn_*: device pointers + stream, asynchronous, int status codes.
+//  * anima_rt_*:   drop-in replacements of the reference runtime's extern "C" entries
+//    (anima_rt/src/anima_rt.cpp:11-173): fp32 host pointers, bool returns.  Each call
+//    copies its operands into a device workspace owned by the library, runs the
+//    kernels on the library's stream, copies the result back and synchronises.
+//    Calls are serialised by one mutex (one workspace); like the reference they are
+//    safe to call from several threads.
+#include <mutex>
+#include <string>
+
+#include "anima_rt.h"
+#include "common.cuh"
+
+namespace anima {
+int attn_fwd_launch(const AnimaAttnArgs* a, int* status, cudaStream_t st);
+int prologue_launch(const AnimaPrologueArgs* a, int sm_count, cudaStream_t st);
+int rmsnorm_launch(const float* x, const float* w, float* y, long long m, int d, float eps,
+                   int sm_count, cudaStream_t st);
+int rope_launch(const float* t, const float* f, float* out, int N, int S, int D, int sm_count,
+                cudaStream_t st);
+}  // namespace anima
+
+using namespace anima;
+
+namespace {
+
+thread_local std::string g_last_error;
+
+void set_error(const std::string& s) { g_last_error = s; }
+
+constexpr int kMaxDevices = 64;
+
+struct DeviceState {
+  bool ready = false;
+  int sm_count = 0;
+  int cc = 0;
+  int* status = nullptr;  // one int of device memory: first error a kernel recorded
+};
+DeviceState g_dev[kMaxDevices];
+std::mutex g_dev_mu;
+
+// Per-device bookkeeping for the current device; nullptr (with error set) on failure.
+DeviceState* current_device(int* rc) {
+  int dev = -1;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) {
+    cudaGetLastError();
+    *rc = ANIMA_ERR_CUDA;
+    set_error("no usable CUDA device");
+    return nullptr;
+  }
+  DeviceState& d = g_dev[dev];
+  if (d.ready) return &d;
+  std::lock_guard<std::mutex> lk(g_dev_mu);
+  if (!d.ready) {
+    int major = 0, minor = 0, sms = 0;
+    if (cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess ||
+        cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev) != cudaSuccess ||
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) {
+      cudaGetLastError();
+      *rc = ANIMA_ERR_CUDA;
+      set_error("cudaDeviceGetAttribute failed");
+      return nullptr;
+    }
+    if (major != 10) {
+      *rc = ANIMA_ERR_UNSUPPORTED;
+      set_error("anima_attn kernels are built for sm_100a (B200); device is sm_" +
+                std::to_string(major * 10 + minor));
+      return nullptr;
+    }
+    int* st = nullptr;
+    if (cudaMalloc(&st, sizeof(int)) != cudaSuccess || cudaMemset(st, 0, sizeof(int)) != cudaSuccess) {
+      cudaGetLastError();
+      *rc = ANIMA_ERR_NOMEM;
+      set_error("cannot allocate the device status word");
+      return nullptr;
+    }
+    d.sm_count = sms;
+    d.cc = major * 10 + minor;
+    d.status = st;
+    d.ready = true;
+  }
+  return &d;
+}
+
+const char* code_name(int rc) {
+  switch (rc) {
+    case ANIMA_OK: return "ok";
+    case ANIMA_ERR_ARG: return "bad argument";
+    case ANIMA_ERR_SHAPE: return "unsupported shape";
+    case ANIMA_ERR_CUDA: return "CUDA error";
+    case ANIMA_ERR_TIMEOUT: return "device-side wait timed out";
+    case ANIMA_ERR_UNSUPPORTED: return "unsupported device";
+    case ANIMA_ERR_NOMEM: return "out of device memory";
+  }
+  return "unknown error";
+}
+
+// ---------------------------------------------------------------- anima_rt state
+struct RtState {
+  bool inited = false;
+  cudaStream_t stream = nullptr;
+  void* ws = nullptr;
+  size_t ws_bytes = 0;
+  int device = -1;
+};
+RtState g_rt;
+std::recursive_mutex g_rt_mu;
+
+bool rt_fail(const std::string& what) {
+  set_error(what);
+  return false;
+}
+
+// Make sure the stream exists on the current device and the workspace holds `bytes`.
+bool rt_prepare(size_t bytes) {
+  int rc = ANIMA_OK;
+  if (!current_device(&rc)) return false;
+  int dev = -1;
+  cudaGetDevice(&dev);
+  if (g_rt.device != dev) {  // first use, or the caller switched devices
+    if (g_rt.ws) cudaFree(g_rt.ws);
+    if (g_rt.stream) cudaStreamDestroy(g_rt.stream);
+    g_rt.ws = nullptr;
+    g_rt.ws_bytes = 0;
+    g_rt.stream = nullptr;
+    if (cudaStreamCreateWithFlags(&g_rt.stream, cudaStreamNonBlocking) != cudaSuccess) {
+      cudaGetLastError();
+      return rt_fail("cudaStreamCreate failed");
+    }
+    g_rt.device = dev;
+  }
+  if (bytes > g_rt.ws_bytes) {
+    if (g_rt.ws) cudaFree(g_rt.ws);
+    g_rt.ws = nullptr;
+    g_rt.ws_bytes = 0;
+    if (cudaMalloc(&g_rt.ws, bytes) != cudaSuccess) {
+      cudaGetLastError();
+      return rt_fail("cudaMalloc of " + std::to_string(bytes) + " bytes failed");
+    }
+    g_rt.ws_bytes = bytes;
+  }
+  return true;
+}
+
+size_t align_up(size_t x) { return (x + 255) & ~size_t(255); }
+
+bool rt_check(cudaError_t e, const char* what) {
+  if (e == cudaSuccess) return true;
+  cudaGetLastError();
+  return rt_fail(std::string(what) + ": " + cudaGetErrorString(e));
+}
+
+bool rt_finish(const char* what) {
+  if (!rt_check(cudaStreamSynchronize(g_rt.stream), what)) return false;
+  int rc = ANIMA_OK;
+  DeviceState* d = current_device(&rc);
+  int code = 0;
+  if (!rt_check(cudaMemcpy(&code, d->status, sizeof(int), cudaMemcpyDeviceToHost), what))
+    return false;
+  if (code != 0) {
+    cudaMemset(d->status, 0, sizeof(int));
+    return rt_fail(std::string(what) + ": " + code_name(code));
+  }
+  return true;
+}
+
+// Shared body of anima_rt_run_sdpa_flash / anima_rt_run_sdpa / anima_rt_run_attention.
+bool rt_attention(const float* q, const float* k, const float* v, const float* q_w,
+                  const float* k_w, const float* freqs, const int* kv_valid, float* out,
+                  int B, int S_q, int S_kv, int H, int D, float eps, float scale,
+                  unsigned flags, const char* who) {
+  if (!q || !k || !v || !out) return rt_fail(std::string(who) + ": null pointer");
+  if (D != 128)
+    return rt_fail(std::string(who) + ": head size " + std::to_string(D) +
+                   " unsupported (the B200 kernels take D = 128)");
+  if (B <= 0 || H <= 0 || S_q <= 0 || S_kv <= 0)
+    return rt_fail(std::string(who) + ": empty or negative shape");
+  if ((flags & ANIMA_FLAG_ROPE) && (!freqs || S_q != S_kv))
+    return rt_fail(std::string(who) + ": RoPE needs freqs and S_q == S_kv");
+  std::lock_guard<std::recursive_mutex> lk(g_rt_mu);
+  const size_t nq = (size_t)B * S_q * H * D, nk = (size_t)B * S_kv * H * D;
+  size_t off = 0;
+  auto carve = [&](size_t bytes) { size_t o = off; off = align_up(off + bytes); return o; };
+  const size_t o_q = carve(nq * 4), o_k = carve(nk * 4), o_v = carve(nk * 4);
+  const size_t o_qb = carve(nq * 2), o_kb = carve(nk * 2), o_vb = carve(nk * 2);
+  const size_t o_out = carve(nq * 4);
+  const size_t o_w = carve(2 * D * 4);
+  const size_t o_f = carve(freqs ? (size_t)S_q * D * 2 * 4 : 0);
+  const size_t o_valid = carve(kv_valid ? (size_t)B * 4 : 0);
+  if (!rt_prepare(off)) return false;
+  char* ws = static_cast<char*>(g_rt.ws);
+  cudaStream_t st = g_rt.stream;
+  float *dq = (float*)(ws + o_q), *dk = (float*)(ws + o_k), *dv = (float*)(ws + o_v);
+  float* dout = (float*)(ws + o_out);
+  float* dw = (float*)(ws + o_w);
+  if (!rt_check(cudaMemcpyAsync(dq, q, nq * 4, cudaMemcpyHostToDevice, st), who) ||
+      !rt_check(cudaMemcpyAsync(dk, k, nk * 4, cudaMemcpyHostToDevice, st), who) ||
+      !rt_check(cudaMemcpyAsync(dv, v, nk * 4, cudaMemcpyHostToDevice, st), who))
+    return false;
+  if (q_w && !rt_check(cudaMemcpyAsync(dw, q_w, D * 4, cudaMemcpyHostToDevice, st), who))
+    return false;
+  if (k_w && !rt_check(cudaMemcpyAsync(dw + D, k_w, D * 4, cudaMemcpyHostToDevice, st), who))
+    return false;
+  if (freqs && !rt_check(cudaMemcpyAsync(ws + o_f, freqs, (size_t)S_q * D * 2 * 4,
+                                         cudaMemcpyHostToDevice, st), who))
+    return false;
+  if (kv_valid && !rt_check(cudaMemcpyAsync(ws + o_valid, kv_valid, (size_t)B * 4,
+                                            cudaMemcpyHostToDevice, st), who))
+    return false;
+
+  AnimaPrologueArgs pa = {};
+  pa.q = dq;
+  pa.k = dk;
+  pa.v = dv;
+  pa.in_dtype = ANIMA_DTYPE_F32;
+  const int64_t sq3[3] = {(int64_t)S_q * H * D, (int64_t)H * D, D};
+  const int64_t sk3[3] = {(int64_t)S_kv * H * D, (int64_t)H * D, D};
+  for (int i = 0; i < 3; ++i) {
+    pa.q_stride[i] = sq3[i];
+    pa.k_stride[i] = sk3[i];
+    pa.v_stride[i] = sk3[i];
+  }
+  pa.B = B;
+  pa.H = H;
+  pa.S_q = S_q;
+  pa.S_kv = S_kv;
+  pa.D = D;
+  pa.q_norm_w = q_w ? dw : nullptr;
+  pa.k_norm_w = k_w ? dw + D : nullptr;
+  pa.eps = eps;
+  pa.rope_freqs = freqs ? (const float*)(ws + o_f) : nullptr;
+  pa.flags = flags & (ANIMA_FLAG_QNORM | ANIMA_FLAG_KNORM | ANIMA_FLAG_ROPE);
+  pa.q_out = ws + o_qb;
+  pa.k_out = ws + o_kb;
+  pa.v_out = ws + o_vb;
+  pa.op_dtype = ANIMA_DTYPE_BF16;
+  int rc = anima_attn_prologue(&pa, st);
+  if (rc != ANIMA_OK) return rt_fail(std::string(who) + ": prologue: " + code_name(rc));
+
+  AnimaAttnArgs aa = {};
+  aa.q = ws + o_qb;
+  aa.k = ws + o_kb;
+  aa.v = ws + o_vb;
+  aa.op_dtype = ANIMA_DTYPE_BF16;
+  aa.out = dout;
+  aa.out_dtype = ANIMA_DTYPE_F32;
+  aa.out_stride[0] = (int64_t)S_q * H * D;  // [B, S_q, H, D]
+  aa.out_stride[1] = D;
+  aa.out_stride[2] = (int64_t)H * D;
+  aa.B = B;
+  aa.H = H;
+  aa.S_q = S_q;
+  aa.S_kv = S_kv;
+  aa.D = D;
+  aa.scale = scale;
+  aa.flags = (flags & ANIMA_FLAG_CAUSAL) | (kv_valid ? ANIMA_FLAG_MASK : 0u);
+  aa.kv_valid_len = kv_valid ? (const int*)(ws + o_valid) : nullptr;
+  rc = anima_attn_fwd(&aa, st);
+  if (rc != ANIMA_OK) return rt_fail(std::string(who) + ": attention: " + code_name(rc));
+  if (!rt_check(cudaMemcpyAsync(out, dout, nq * 4, cudaMemcpyDeviceToHost, st), who))
+    return false;
+  return rt_finish(who);
+}
+
+}  // namespace
+
+extern "C" {
+
+// ---------------------------------------------------------------- device-pointer ABI
+int anima_attn_prologue(const AnimaPrologueArgs* a, void* stream) {
+  if (!a) return ANIMA_ERR_ARG;
+  int rc = ANIMA_OK;
+  DeviceState* d = current_device(&rc);
+  if (!d) return rc;
+  rc = prologue_launch(a, d->sm_count, static_cast<cudaStream_t>(stream));
+  if (rc != ANIMA_OK) set_error(std::string("anima_attn_prologue: ") + code_name(rc));
+  return rc;
+}
+
+int anima_attn_fwd(const AnimaAttnArgs* a, void* stream) {
+  if (!a || !a->q || !a->k || !a->v || !a->out) return ANIMA_ERR_ARG;
+  if ((a->flags & ANIMA_FLAG_MASK) && !a->kv_valid_len) return ANIMA_ERR_ARG;
+  const int oe = a->out_dtype == ANIMA_DTYPE_F32 ? 4 : 8;  // elements per 16 bytes
+  for (int i = 0; i < 3; ++i)
+    if (a->out_stride[i] < 0 || a->out_stride[i] % oe) return ANIMA_ERR_ARG;
+  const uintptr_t al = reinterpret_cast<uintptr_t>(a->q) | reinterpret_cast<uintptr_t>(a->k) |
+                       reinterpret_cast<uintptr_t>(a->v) | reinterpret_cast<uintptr_t>(a->out);
+  if (al & 15u) return ANIMA_ERR_ARG;
+  int rc = ANIMA_OK;
+  DeviceState* d = current_device(&rc);
+  if (!d) return rc;
+  rc = attn_fwd_launch(a, d->status, static_cast<cudaStream_t>(stream));
+  if (rc != ANIMA_OK) set_error(std::string("anima_attn_fwd: ") + code_name(rc));
+  return rc;
+}
+
+int anima_attn_status(void* stream, int reset) {
+  int rc = ANIMA_OK;
+  DeviceState* d = current_device(&rc);
+  if (!d) return rc;
+  if (cudaStreamSynchronize(static_cast<cudaStream_t>(stream)) != cudaSuccess) {
+    cudaGetLastError();
+    return ANIMA_ERR_CUDA;
+  }
+  int code = 0;
+  if (cudaMemcpy(&code, d->status, sizeof(int), cudaMemcpyDeviceToHost) != cudaSuccess) {
+    cudaGetLastError();
+    return ANIMA_ERR_CUDA;
+  }
+  if (reset && code) cudaMemset(d->status, 0, sizeof(int));
+  return code;
+}
+
+int anima_attn_device_info(int* sm_count, int* cc) {
+  int rc = ANIMA_OK;
+  DeviceState* d = current_device(&rc);
+  if (!d) return rc;
+  if (sm_count) *sm_count = d->sm_count;
+  if (cc) *cc = d->cc;
+  return ANIMA_OK;
+}
+
+const char* anima_attn_version(void) {
+  return "anima_attn sm_100a: tcgen05 flash fwd (2x128-row Q tiles/CTA, 128-key tiles, "
+         "4-slot K/V ring, TMEM S/P/O), fused RMSNorm+RoPE prologue";
+}
+
+// ---------------------------------------------------------------- anima_rt drop-ins
+bool anima_rt_init(void) {
+  std::lock_guard<std::recursive_mutex> lk(g_rt_mu);
+  if (g_rt.inited) return true;
+  if (!rt_prepare(0)) return false;
+  g_rt.inited = true;
+  return true;
+}
+
+void anima_rt_destroy(void) {
+  std::lock_guard<std::recursive_mutex> lk(g_rt_mu);
+  if (g_rt.ws) cudaFree(g_rt.ws);
+  if (g_rt.stream) cudaStreamDestroy(g_rt.stream);
+  g_rt = RtState();
+}
+
+bool anima_rt_run_sdpa_flash(const float* Q, const float* K, const float* V, float* output,
+                             int BH, int S_q, int S_kv, int D, float scale, bool is_causal) {
+  // [BH, S, D] is [B, S, H, D] with B = BH and H = 1.
+  return rt_attention(Q, K, V, nullptr, nullptr, nullptr, nullptr, output, BH, S_q, S_kv, 1, D,
+                      0.f, scale, is_causal ? ANIMA_FLAG_CAUSAL : 0u, "anima_rt_run_sdpa_flash");
+}
+
+bool anima_rt_run_sdpa(const float* Q, const float* K, const float* V, float* output, int BH,
+                       int S_q, int S_kv, int D, float scale, bool is_causal) {
+  if (!g_rt.inited) return rt_fail("anima_rt_run_sdpa: anima_rt_init has not been called");
+  return rt_attention(Q, K, V, nullptr, nullptr, nullptr, nullptr, output, BH, S_q, S_kv, 1, D,
+                      0.f, scale, is_causal ? ANIMA_FLAG_CAUSAL : 0u, "anima_rt_run_sdpa");
+}
+
+bool anima_rt_run_attention(const float* q, const float* k, const float* v, const float* q_w,
+                            const float* k_w, const float* freqs, const int* kv_valid,
+                            float* out, int B, int S_q, int S_kv, int H, int D, float eps,
+                            float scale, unsigned flags) {
+  return rt_attention(q, k, v, q_w, k_w, freqs, kv_valid, out, B, S_q, S_kv, H, D, eps, scale,
+                      flags, "anima_rt_run_attention");
+}
+
+bool anima_rt_run_rmsnorm(const float* x, const float* w, float* out, int m, int d, float eps) {
+  if (!g_rt.inited) return rt_fail("anima_rt_run_rmsnorm: anima_rt_init has not been called");
+  if (!x || !out || m < 0 || d <= 0) return rt_fail("anima_rt_run_rmsnorm: bad arguments");
+  if (m == 0) return true;
+  std::lock_guard<std::recursive_mutex> lk(g_rt_mu);
+  const size_t n = (size_t)m * d;
+  const size_t o_x = 0, o_y = align_up(n * 4), o_w = o_y + align_up(n * 4);
+  if (!rt_prepare(o_w + align_up((size_t)d * 4))) return false;
+  char* ws = static_cast<char*>(g_rt.ws);
+  cudaStream_t st = g_rt.stream;
+  const char* who = "anima_rt_run_rmsnorm";
+  if (!rt_check(cudaMemcpyAsync(ws + o_x, x, n * 4, cudaMemcpyHostToDevice, st), who)) return false;
+  if (w && !rt_check(cudaMemcpyAsync(ws + o_w, w, (size_t)d * 4, cudaMemcpyHostToDevice, st), who))
+    return false;
+  int rc = ANIMA_OK;
+  DeviceState* dev = current_device(&rc);
+  rc = rmsnorm_launch((const float*)(ws + o_x), w ? (const float*)(ws + o_w) : nullptr,
+                      (float*)(ws + o_y), m, d, eps, dev->sm_count, st);
+  if (rc != ANIMA_OK) return rt_fail(std::string(who) + ": " + code_name(rc));
+  if (!rt_check(cudaMemcpyAsync(out, ws + o_y, n * 4, cudaMemcpyDeviceToHost, st), who)) return false;
+  return rt_finish(who);
+}
+
+bool anima_rt_run_rope(const float* t, const float* freqs, float* out, int N, int S, int D) {
+  const char* who = "anima_rt_run_rope";
+  if (!t || !freqs || !out || N < 0 || S < 0 || D <= 0 || (D & 1))
+    return rt_fail(std::string(who) + ": bad arguments");
+  if (N == 0 || S == 0) return true;
+  std::lock_guard<std::recursive_mutex> lk(g_rt_mu);
+  const size_t n = (size_t)N * S * D, nf = (size_t)S * D * 2;
+  const size_t o_t = 0, o_o = align_up(n * 4), o_f = o_o + align_up(n * 4);
+  if (!rt_prepare(o_f + align_up(nf * 4))) return false;
+  char* ws = static_cast<char*>(g_rt.ws);
+  cudaStream_t st = g_rt.stream;
+  if (!rt_check(cudaMemcpyAsync(ws + o_t, t, n * 4, cudaMemcpyHostToDevice, st), who) ||
+      !rt_check(cudaMemcpyAsync(ws + o_f, freqs, nf * 4, cudaMemcpyHostToDevice, st), who))
+    return false;
+  int rc = ANIMA_OK;
+  DeviceState* dev = current_device(&rc);
+  rc = rope_launch((const float*)(ws + o_t), (const float*)(ws + o_f), (float*)(ws + o_o), N, S,
+                   D, dev->sm_count, st);
+  if (rc != ANIMA_OK) return rt_fail(std::string(who) + ": " + code_name(rc));
+  if (!rt_check(cudaMemcpyAsync(out, ws + o_o, n * 4, cudaMemcpyDeviceToHost, st), who)) return false;
+  return rt_finish(who);
+}
+
+const char* anima_rt_last_error(void) { return g_last_error.c_str(); }
+
+}  // extern "C"

@@ -1,0 +1,125 @@
+/*
+ * anima_attn.h -- device-pointer C ABI of the B200 attention library.
+ *
+ * These entries serve PyTorch / CUDA callers that already hold the projections on the
+ * GPU.  They replace, as one fused pipeline, the per-block attention sequence of the
+ * reference DiT:
+ *
+ *   q/k RMSNorm (D = 128, eps 1e-6)   anima_rt/scripts/numpy_dit.py:285-286,
+ *                                     src/predict2.py:185-186
+ *   3D RoPE, self-attention only      anima_rt/scripts/numpy_dit.py:288-289,
+ *                                     src/predict2.py:187-189, 31-38
+ *   [B,S,H,D] -> [B,H,S,D] transpose  anima_rt/scripts/numpy_dit.py:291
+ *   flash SDPA                        anima_rt/src/anima_rt.cpp:147-156
+ *   transpose back to [B,S,H*D]       anima_rt/scripts/numpy_dit.py:294
+ *
+ * No torch types cross this boundary: plain device pointers, element strides, sizes
+ * and a cudaStream_t passed as void*.  Every entry is asynchronous on that stream and
+ * returns ANIMA_OK or a negative code; none aborts.  Device-side waits are bounded
+ * (about one second); a kernel that gives up records ANIMA_ERR_TIMEOUT in the
+ * library's per-device status word (anima_attn_status) and returns.
+ */
+#ifndef ANIMA_ATTN_H_
+#define ANIMA_ATTN_H_
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum {
+  ANIMA_OK = 0,
+  ANIMA_ERR_ARG = -1,         /* null pointer, bad dtype, bad stride */
+  ANIMA_ERR_SHAPE = -2,       /* unsupported or inconsistent shape */
+  ANIMA_ERR_CUDA = -3,        /* a CUDA runtime/driver call failed */
+  ANIMA_ERR_TIMEOUT = -4,     /* a device-side wait ran out (see anima_attn_status) */
+  ANIMA_ERR_UNSUPPORTED = -5, /* device is not sm_100 */
+  ANIMA_ERR_NOMEM = -6
+};
+
+enum { ANIMA_DTYPE_F32 = 0, ANIMA_DTYPE_BF16 = 1, ANIMA_DTYPE_F16 = 2 };
+
+/* flags */
+#define ANIMA_FLAG_QNORM 0x1u  /* RMSNorm q rows with q_norm_w            */
+#define ANIMA_FLAG_KNORM 0x2u  /* RMSNorm k rows with k_norm_w            */
+#define ANIMA_FLAG_ROPE 0x4u   /* rotate q and k with rope_freqs          */
+#define ANIMA_FLAG_MASK 0x8u   /* key-padding mask from kv_valid_len[B]   */
+#define ANIMA_FLAG_CAUSAL 0x10u /* top-left causal mask (col <= row)      */
+
+/*
+ * Prologue: per-head RMSNorm + RoPE + cast, one HBM pass.
+ * Inputs q [B, S_q, H, D], k/v [B, S_kv, H, D] of dtype in_dtype, addressed by element
+ * strides (stride_b, stride_s, stride_h; the D axis must be contiguous).
+ * Outputs q_out [B*H, S_q, D], k_out/v_out [B*H, S_kv, D], contiguous, dtype op_dtype
+ * (BF16 or F16) -- the layout anima_attn_fwd reads.
+ * rope_freqs: fp32 [S_q, D/2, 2, 2] table (VideoRopePosition3DEmb layout); with
+ * ANIMA_FLAG_ROPE it rotates q and k (requires S_q == S_kv).
+ * q_norm_w / k_norm_w: fp32 [D]; NULL means weight 1.
+ */
+typedef struct AnimaPrologueArgs {
+  const void* q;
+  const void* k;
+  const void* v;
+  int in_dtype;
+  int64_t q_stride[3];
+  int64_t k_stride[3];
+  int64_t v_stride[3];
+  int B, H, S_q, S_kv, D;
+  const float* q_norm_w;
+  const float* k_norm_w;
+  float eps;
+  const float* rope_freqs;
+  unsigned flags;
+  void* q_out;
+  void* k_out;
+  void* v_out;
+  int op_dtype;
+} AnimaPrologueArgs;
+
+/*
+ * Attention core (tcgen05 / TMEM flash forward, sm_100a).
+ * q [B*H, S_q, D], k/v [B*H, S_kv, D] contiguous, dtype op_dtype (BF16 or F16), D = 128.
+ * out: element strides out_stride = {b, h, s}, D contiguous, dtype out_dtype (F32, BF16).
+ *   [B*H, S_q, D] (the anima_rt layout):   {H*S_q*D, S_q*D, D}
+ *   [B, S_q, H, D] (feeds the o-proj):     {S_q*H*D, D, H*D}
+ * kv_valid_len: device int32 [B], used with ANIMA_FLAG_MASK (keys >= valid are masked;
+ * a sample with 0 valid keys gets a zero output).
+ */
+typedef struct AnimaAttnArgs {
+  const void* q;
+  const void* k;
+  const void* v;
+  int op_dtype;
+  void* out;
+  int out_dtype;
+  int64_t out_stride[3];
+  int B, H, S_q, S_kv, D;
+  float scale;
+  unsigned flags;
+  const int* kv_valid_len;
+} AnimaAttnArgs;
+
+/* Replaces the norm/RoPE/transpose steps listed above (numpy_dit.py:285-291). */
+int anima_attn_prologue(const AnimaPrologueArgs* args, void* stream);
+
+/* Replaces anima::cpu::flash_attention (anima_rt/include/cpu/flash_attention.h:55-208)
+ * for device-resident operands. */
+int anima_attn_fwd(const AnimaAttnArgs* args, void* stream);
+
+/* Device status word of the current device: 0, or the first ANIMA_ERR_* a kernel
+ * recorded.  Synchronises `stream`; clears the word when reset != 0. */
+int anima_attn_status(void* stream, int reset);
+
+/* Number of streaming multiprocessors and compute capability of the current device
+ * (major*10 + minor); returns ANIMA_ERR_CUDA without a device. */
+int anima_attn_device_info(int* sm_count, int* cc);
+
+/* Library build identifier (kernel configuration), for logs. */
+const char* anima_attn_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* ANIMA_ATTN_H_ */

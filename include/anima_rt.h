@@ -1,0 +1,83 @@
+/*
+ * anima_rt.h -- drop-in replacement for the reference runtime's attention entry points.
+ *
+ * libanima_attn.so exports these symbols with the exact signatures, argument meaning,
+ * ownership and bool-return convention of riorgord/Anima-on-Android's
+ * anima_rt/src/anima_rt.cpp, so the reference's ctypes bindings
+ * (anima_rt/scripts/anima_rt_ops.py:11-34, scripts/phone_pipeline_nd.py:46-68) load it
+ * unchanged.  All pointers are caller-owned, contiguous fp32 HOST memory; each call
+ * copies its inputs to the current CUDA device, runs the B200 kernels, copies the
+ * result back and returns.  A call returns false (never aborts) on any CUDA error or
+ * unsupported shape; anima_rt_last_error() then describes why.
+ *
+ * Calls are serialised inside the library (one device workspace); concurrent callers
+ * are safe but do not overlap on the GPU.
+ */
+#ifndef ANIMA_RT_H_
+#define ANIMA_RT_H_
+
+#include <stdbool.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Replaces anima_rt_init (anima_rt/src/anima_rt.cpp:13-20).  Idempotent.  Selects the
+ * current CUDA device and creates the library's stream and workspace.  false when no
+ * CUDA device is usable. */
+bool anima_rt_init(void);
+
+/* Replaces anima_rt_destroy (anima_rt/src/anima_rt.cpp:166-171).  Frees the workspace;
+ * later calls that need init (rmsnorm, math sdpa) return false until anima_rt_init. */
+void anima_rt_destroy(void);
+
+/* Replaces anima_rt_run_sdpa_flash (anima_rt/src/anima_rt.cpp:147-156,
+ * anima_rt/include/cpu/flash_attention.h:55-208).
+ * Q [BH, S_q, D], K/V [BH, S_kv, D], output [BH, S_q, D], fp32.  Computes
+ * softmax(Q K^T * scale) V per head, top-left causal mask when is_causal.  Operands
+ * are rounded to bf16 for the tensor cores, accumulation and softmax are fp32.
+ * Supports D == 128 (the Anima head size); other D return false.  Like the reference
+ * it does not require anima_rt_init. */
+bool anima_rt_run_sdpa_flash(const float* Q, const float* K, const float* V, float* output,
+                             int BH, int S_q, int S_kv, int D, float scale, bool is_causal);
+
+/* Replaces anima_rt_run_sdpa (anima_rt/src/anima_rt.cpp:78-140).  The reference's math
+ * path scales both Q and K by `scale` (effective scale^2); this library computes the
+ * correct SDPA with `scale` applied once, identical to anima_rt_run_sdpa_flash.
+ * Returns false before anima_rt_init, as the reference does. */
+bool anima_rt_run_sdpa(const float* Q, const float* K, const float* V, float* output,
+                       int BH, int S_q, int S_kv, int D, float scale, bool is_causal);
+
+/* Replaces anima_rt_run_rmsnorm (anima_rt/src/anima_rt.cpp:45-50,
+ * anima_rt/include/cpu/rmsnorm_kernel.h:11-33): y = x / sqrt(mean(x^2) + eps) * w
+ * per row of x [m, d]; w may be NULL.  Returns false before anima_rt_init. */
+bool anima_rt_run_rmsnorm(const float* x, const float* w, float* out, int m, int d,
+                          float eps);
+
+/* Replaces anima_rt_run_rope (anima_rt/src/anima_rt.cpp:160-164,
+ * anima_rt/include/cpu/rope_kernel.h:30-62): t [N, S, D], freqs [S, D/2, 2, 2]
+ * ([cos, -sin, sin, cos] per pair), pairs (p, D/2 + p).  Bit-identical to the
+ * reference (no fused multiply-add). */
+bool anima_rt_run_rope(const float* t, const float* freqs, float* out, int N, int S, int D);
+
+/* Extension (no single reference counterpart): the whole per-block attention sequence
+ * of NumpyAttention.forward (anima_rt/scripts/numpy_dit.py:285-294) in one call --
+ * q/k RMSNorm (q_w / k_w may be NULL: weight 1; flags select which are applied),
+ * RoPE on q and k with freqs [S_q, D/2, 2, 2] (self-attention, S_q == S_kv), flash
+ * SDPA and the transposes.  q [B, S_q, H, D], k/v [B, S_kv, H, D], out [B, S_q, H, D],
+ * all fp32 host memory.  kv_valid (host int32 [B], may be NULL) masks keys >= kv_valid[b].
+ * flags: 1 = q norm, 2 = k norm, 4 = RoPE, 16 = causal (bit values of ANIMA_FLAG_*).
+ * Host buffers in page-locked memory make the copies run at full PCIe speed. */
+bool anima_rt_run_attention(const float* q, const float* k, const float* v, const float* q_w,
+                            const float* k_w, const float* freqs, const int* kv_valid,
+                            float* out, int B, int S_q, int S_kv, int H, int D, float eps,
+                            float scale, unsigned flags);
+
+/* Extension: text of the last failure on this thread ("" if none). */
+const char* anima_rt_last_error(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* ANIMA_RT_H_ */

@@ -1,0 +1,240 @@
+"""Parity of the B200 kernels with the reference (oracle + golden fixtures), on a GPU.
+
+Bar (north star): rel-L2 <= 5e-3 and max-abs <= 2e-2 per attention output against the
+reference's fp32 flash SDPA; the RoPE drop-in is bit-exact; the RMSNorm drop-in agrees
+to fp32 rounding (its sum is a tree, the reference's is sequential).
+"""
+import ctypes as ct
+
+import numpy as np
+import pytest
+
+from conftest import ATTN_MAX_ABS, ATTN_REL_L2, golden, max_abs, rel_l2
+
+pytestmark = pytest.mark.gpu
+
+torch = pytest.importorskip("torch")
+
+
+@pytest.fixture(scope="module")
+def aa():
+    import anima_attn
+    from anima_attn import _lib as L
+    torch.cuda.set_device(0)
+    assert L.lib.anima_rt_init()
+    return anima_attn
+
+
+@pytest.fixture(scope="module")
+def O():
+    from oracle import oracle
+    oracle.build(ref=False)
+    return oracle
+
+
+def _ok(got, ref, rel=ATTN_REL_L2, mx=ATTN_MAX_ABS):
+    r, m = rel_l2(got, ref), max_abs(got, ref)
+    assert np.isfinite(got).all()
+    assert r <= rel and m <= mx, f"rel-L2 {r:.3e} max-abs {m:.3e}"
+    return r, m
+
+
+def _dev(a):
+    return torch.from_numpy(np.ascontiguousarray(a)).cuda()
+
+
+# ------------------------------------------------------------------ drop-in C ABI
+@pytest.mark.parametrize("name", ["sdpa_square.npz", "sdpa_ragged.npz", "sdpa_causal.npz",
+                                  "sdpa_cross.npz"])
+def test_sdpa_flash_dropin_vs_reference_fixture(aa, name):
+    from anima_attn import _lib as L
+    g = golden(name)
+    q, k, v = g["q"], g["k"], g["v"]
+    bh, sq, d = q.shape
+    skv = k.shape[1]
+    out = np.zeros_like(g["out"])
+    ok = L.lib.anima_rt_run_sdpa_flash(q.ctypes.data, k.ctypes.data, v.ctypes.data,
+                                       out.ctypes.data, bh, sq, skv, d,
+                                       ct.c_float(1 / np.sqrt(d)), ct.c_bool(bool(g["causal"])))
+    assert ok, L.last_error()
+    _ok(out, g["out"])
+
+
+def test_rope_dropin_bit_exact(aa):
+    from anima_attn.compat import anima_rt_rope
+    g = golden("rope.npz")
+    assert np.array_equal(anima_rt_rope(g["t"], g["freqs"]), g["out_anima_rt"])
+
+
+def test_rmsnorm_dropin(aa):
+    from anima_attn.compat import NumpyRT
+    g = golden("rmsnorm.npz")
+    rt = NumpyRT({"blk.q_norm.weight": g["w"]})
+    got = rt.run_rmsnorm(g["x"].reshape(2, 32, 128), "blk.q_norm").reshape(64, 128)
+    assert max_abs(got, g["out_w"]) <= 2e-6
+    assert rel_l2(got, g["out_w"]) <= 1e-6
+
+
+def test_fused_host_entry_vs_reference_composition(aa):
+    from anima_attn.compat import NumpyRT
+    g = golden("prologue_sdpa.npz")
+    rt = NumpyRT({"b.q_norm.weight": g["q_w"], "b.k_norm.weight": g["k_w"]})
+    got = rt.run_attention(g["q"], g["k"], g["v"], "b", rope_emb=g["freqs"])
+    _ok(got, g["out"].transpose(0, 2, 1, 3))
+
+
+def test_numpyrt_run_sdpa_shapes(aa):
+    from anima_attn.compat import NumpyRT
+    g = golden("sdpa_ragged.npz")
+    rt = NumpyRT({})
+    got = rt.run_sdpa(g["q"][None], g["k"][None], g["v"][None])
+    _ok(got[0], g["out"])
+
+
+# ------------------------------------------------------------------ device path
+SHAPES = [  # (B, H, Sq, Skv, causal)
+    (1, 1, 1, 1, False), (1, 2, 7, 7, False), (1, 1, 64, 64, False), (1, 2, 127, 129, False),
+    (2, 2, 129, 127, False), (1, 3, 256, 256, False), (1, 1, 300, 1000, False),
+    (1, 1, 513, 200, False), (1, 2, 256, 256, True), (1, 1, 200, 333, True),
+]
+
+
+@pytest.mark.parametrize("B,H,Sq,Skv,causal", SHAPES)
+def test_attention_core_shapes(aa, O, B, H, Sq, Skv, causal):
+    rng = np.random.default_rng(B * 1000 + Sq * 7 + Skv)
+    q = rng.standard_normal((B, H, Sq, 128), dtype=np.float32)
+    k = rng.standard_normal((B, H, Skv, 128), dtype=np.float32)
+    v = rng.standard_normal((B, H, Skv, 128), dtype=np.float32)
+    ref = O.sdpa(q, k, v, causal=causal)
+    got = aa.sdpa(_dev(q), _dev(k), _dev(v), is_causal=causal)
+    torch.cuda.synchronize()
+    _ok(got.cpu().numpy(), ref)
+    assert aa.status() == 0
+
+
+@pytest.mark.parametrize("op_dtype", ["bf16", "f16"])
+@pytest.mark.parametrize("out_dtype,layout", [("f32", "bshd"), ("bf16", "bshd"), ("f32", "bhsd")])
+def test_operand_and_output_variants(aa, O, op_dtype, out_dtype, layout):
+    rng = np.random.default_rng(5)
+    B, H, S = 2, 3, 300
+    q, k, v = (rng.standard_normal((B, S, H, 128), dtype=np.float32) for _ in range(3))
+    qw = (1 + 0.1 * rng.standard_normal(128)).astype(np.float32)
+    kw = (1 + 0.1 * rng.standard_normal(128)).astype(np.float32)
+    tdt = {"bf16": torch.bfloat16, "f16": torch.float16, "f32": torch.float32}
+    qh, kh, vh = aa.prologue(_dev(q), _dev(k), _dev(v), _dev(qw), _dev(kw), op_dtype=tdt[op_dtype])
+    out = aa.attention_core(qh, kh, vh, B, H, out_layout=layout, out_dtype=tdt[out_dtype])
+    torch.cuda.synchronize()
+    rq, rk, rv = O.prologue(q, k, v, qw, kw)
+    ref = O.sdpa(rq, rk, rv)  # [B,H,S,D]
+    got = out.float().cpu().numpy()
+    if layout == "bshd":
+        got = got.transpose(0, 2, 1, 3)
+    tol = 8e-3 if out_dtype == "bf16" else ATTN_REL_L2  # bf16 output adds 2^-9 rounding
+    _ok(got, ref, rel=tol)
+
+
+def test_prologue_matches_oracle_to_operand_rounding(aa, O):
+    rng = np.random.default_rng(9)
+    B, H, side = 2, 4, 10
+    S = side * side
+    q, k, v = (rng.standard_normal((B, S, H, 128), dtype=np.float32) for _ in range(3))
+    qw = (1 + 0.1 * rng.standard_normal(128)).astype(np.float32)
+    kw = (1 + 0.1 * rng.standard_normal(128)).astype(np.float32)
+    fr = O.rope_freqs_3d(1, side, side)
+    qh, kh, vh = aa.prologue(_dev(q), _dev(k), _dev(v), _dev(qw), _dev(kw), _dev(fr),
+                             op_dtype=torch.float16)
+    torch.cuda.synchronize()
+    rq, rk, rv = O.prologue(q, k, v, qw, kw, fr)
+    for got, ref in ((qh, rq), (kh, rk), (vh, rv)):
+        g = got.float().cpu().numpy().reshape(ref.shape)
+        # fp16 rounding of the fp32 oracle value: |err| <= 2^-11 |x| (+ tree-sum ulps)
+        assert np.all(np.abs(g - ref) <= np.abs(ref) * 2.0 ** -10 + 1e-6)
+
+
+def test_masked_cross_attention(aa, O):
+    rng = np.random.default_rng(21)
+    B, H, Sq, Skv = 6, 2, 200, 512
+    q = rng.standard_normal((B, H, Sq, 128), dtype=np.float32)
+    k = rng.standard_normal((B, H, Skv, 128), dtype=np.float32)
+    v = rng.standard_normal((B, H, Skv, 128), dtype=np.float32)
+    valid = np.array([0, 1, 77, 128, 129, 512], dtype=np.int32)
+    ref = O.sdpa_varlen(q, k, v, valid, threads=4)
+    qh, kh, vh = (_dev(t).reshape(B * H, -1, 128).to(torch.bfloat16) for t in (q, k, v))
+    out = aa.attention_core(qh, kh, vh, B, H, kv_valid_len=_dev(valid), out_layout="bhsd")
+    torch.cuda.synchronize()
+    got = out.cpu().numpy()
+    assert not got[0].any()  # zero valid keys -> zero output, like the oracle
+    _ok(got, ref)
+
+
+# ------------------------------------------------------------------ BASELINE configs
+def test_config1_self_attention_256(aa, O):
+    rng = np.random.default_rng(0)
+    q, k, v = (rng.standard_normal((2, 16, 256, 128), dtype=np.float32) for _ in range(3))
+    ref = O.sdpa(q, k, v, threads=8)
+    got = aa.sdpa(_dev(q), _dev(k), _dev(v))
+    torch.cuda.synchronize()
+    _ok(got.cpu().numpy(), ref)
+
+
+def test_config2_prologue_self_attention_1024(aa, O):
+    rng = np.random.default_rng(1)
+    B, S, H = 2, 1024, 16
+    q, k, v = (rng.standard_normal((B, S, H, 128), dtype=np.float32) for _ in range(3))
+    qw = (1 + 0.1 * rng.standard_normal(128)).astype(np.float32)
+    kw = (1 + 0.1 * rng.standard_normal(128)).astype(np.float32)
+    fr = O.rope_freqs_3d(1, 32, 32)
+    out = aa.attention(_dev(q), _dev(k), _dev(v), _dev(qw), _dev(kw), _dev(fr))
+    torch.cuda.synchronize()
+    rq, rk, rv = O.prologue(q, k, v, qw, kw, fr)
+    ref = O.sdpa(rq, rk, rv, threads=8)
+    _ok(out.cpu().numpy().transpose(0, 2, 1, 3), ref)
+
+
+def test_config3_masked_cross_attention(aa, O):
+    rng = np.random.default_rng(2)
+    B, Sq, Skv, H = 2, 4096, 512, 16
+    q = rng.standard_normal((B, Sq, H, 128), dtype=np.float32)
+    ctx = rng.standard_normal((B, Skv, 1024), dtype=np.float32)
+    wk = (0.02 * rng.standard_normal((2048, 1024))).astype(np.float32)
+    wv = (0.02 * rng.standard_normal((2048, 1024))).astype(np.float32)
+    wk = torch.from_numpy(wk).bfloat16().float().numpy()
+    wv = torch.from_numpy(wv).bfloat16().float().numpy()
+    k = (ctx @ wk.T).reshape(B, Skv, H, 128).astype(np.float32)
+    v = (ctx @ wv.T).reshape(B, Skv, H, 128).astype(np.float32)
+    qw = (1 + 0.1 * rng.standard_normal(128)).astype(np.float32)
+    valid = rng.integers(32, 513, size=B).astype(np.int32)
+    out = aa.attention(_dev(q), _dev(k), _dev(v), _dev(qw), None, None,
+                       kv_valid_len=_dev(valid), norm_k=False)
+    torch.cuda.synchronize()
+    rq, rk, rv = O.prologue(q, k, v, qw, None)
+    ref = O.sdpa_varlen(rq, rk, rv, valid, threads=8)
+    _ok(out.cpu().numpy().transpose(0, 2, 1, 3), ref)
+
+
+@pytest.mark.parametrize("L", [4096, 16384])
+def test_long_sequence_rows_and_properties(aa, O, L):
+    """Config 5 sizes: sampled query rows against all keys (rows are independent, so
+    the sliced oracle is exact), plus size-independent properties of the full output."""
+    side = int(np.sqrt(L))
+    rng = np.random.default_rng(L)
+    B, H = 2, 16
+    q, k, v = (rng.standard_normal((B, L, H, 128), dtype=np.float32) for _ in range(3))
+    qw = (1 + 0.1 * rng.standard_normal(128)).astype(np.float32)
+    kw = (1 + 0.1 * rng.standard_normal(128)).astype(np.float32)
+    fr = O.rope_freqs_3d(1, side, side)
+    dq, dk, dv = _dev(q), _dev(k), _dev(v)
+    out = aa.attention(dq, dk, dv, _dev(qw), _dev(kw), _dev(fr))
+    torch.cuda.synchronize()
+    got = out.cpu().numpy()  # [B, L, H, D]
+    rq, rk, rv = O.prologue(q, k, v, qw, kw, fr)  # [B, H, L, D]
+    rows = np.sort(rng.choice(L, size=96, replace=False))
+    for (b, h) in [(0, 0), (1, 15), (1, 7)]:
+        ref = O.sdpa(rq[b, h][rows][None], rk[b, h][None], rv[b, h][None])[0]
+        _ok(got[b, rows, h], ref)
+    # rows of softmax sum to one: V = 1 gives an all-ones output
+    ones = torch.ones_like(dv)
+    o1 = aa.attention(dq, dk, ones, _dev(qw), _dev(kw), _dev(fr))
+    torch.cuda.synchronize()
+    assert np.abs(o1.cpu().numpy() - 1.0).max() < 1e-2
+    assert aa.status() == 0
