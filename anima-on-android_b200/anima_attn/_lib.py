@@ -9,7 +9,8 @@ import ctypes as ct
 import os
 
 HERE = os.path.dirname(os.path.abspath(__file__))
-LIB_PATH = os.path.join(HERE, "libanima_attn.so")
+# ANIMA_ATTN_LIB points at another build of the same library (e.g. a tuning variant).
+LIB_PATH = os.environ.get("ANIMA_ATTN_LIB", os.path.join(HERE, "libanima_attn.so"))
 
 # status codes and flags (anima_attn.h)
 OK, ERR_ARG, ERR_SHAPE, ERR_CUDA, ERR_TIMEOUT, ERR_UNSUPPORTED, ERR_NOMEM = 0, -1, -2, -3, -4, -5, -6

@@ -10,6 +10,7 @@
 //   warp 9     MMA issuer (one thread) + TMEM owner:
 //                S_i  = Q_i K_j^T          (SS form, both operands in shared memory)
 //                O_i += P_i V_j            (TS form, P read from tensor memory)
+//   warps 10-11 idle (they complete the third warpgroup, which donates its registers)
 //   warps 0-7  two softmax warpgroups, one per 128-row Q tile; thread = query row =
 //              TMEM lane.  Each reads its S row from TMEM, updates the running max
 //              and sum, writes P (16-bit) back over S, rescales its O row when the
@@ -37,9 +38,17 @@ constexpr int kPanel = 128 * 128;      // [128 rows][64 x 16-bit], 128B-swizzled
 constexpr int kTile = 2 * kPanel;      // [128 rows][128 x 16-bit] = 32 KB
 constexpr int kProducerWarp = 8;
 constexpr int kMmaWarp = 9;
-constexpr int kThreads = 320;
+constexpr int kThreads = 384;              // 3 warpgroups
+// Launch budget 384 x 168 registers; the control warpgroup gives registers back to the
+// two softmax warpgroups: 2*128*208 + 128*80 = 63488 <= 384*168.
+constexpr uint32_t kRegsSoftmax = 208;
+constexpr uint32_t kRegsControl = 80;
 constexpr uint32_t kTmemCols = 512;
 constexpr float kRescaleThreshold = 8.0f;  // log2 units
+#ifndef ANIMA_POLY_PER8
+#define ANIMA_POLY_PER8 2
+#endif
+constexpr int kPolyPer8 = ANIMA_POLY_PER8;  // of every 8 column pairs, polynomial exp2
 
 struct Smem {
   uint8_t q[kNT][kTile];
@@ -131,6 +140,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_after();
   const uint32_t tmem = sm.tmem_base;
 
+  if (warp >= 8) {
+    regs_dec<kRegsControl>();
   if (warp == kProducerWarp) {
     // ------------------------------------------------------------ TMA producer
     if (lane == 0) {
@@ -175,17 +186,16 @@ __global__ void __launch_bounds__(kThreads, 1)
       constexpr uint32_t ab = kOp == ANIMA_DTYPE_BF16 ? 1u : 0u;  // idesc: 0 f16, 1 bf16
       constexpr uint32_t idesc_qk = make_idesc_f16(ab, kBM, kBN, 0);
       constexpr uint32_t idesc_pv = make_idesc_f16(ab, kBM, kD, 1);
-      uint32_t q_base[kNT], kv_base[kStages];
-      for (int i = 0; i < kNT; ++i) q_base[i] = smem_u32(sm.q[i]);
-      for (int s = 0; s < kStages; ++s) kv_base[s] = smem_u32(sm.kv[s]);
+      const uint32_t q_base = smem_u32(sm.q[0]);    // tile i at + i * kTile
+      const uint32_t kv_base = smem_u32(sm.kv[0]);  // slot s at + s * kTile
 
       auto issue_qk = [&](int i, int slot) {
         const uint32_t d = tmem + i * 128;
 #pragma unroll
         for (int kk = 0; kk < kD / 16; ++kk) {
           const uint32_t off = (kk >> 2) * kPanel + (kk & 3) * 32;
-          umma_ss(d, sdesc_sw128(q_base[i] + off, 16, 1024),
-                  sdesc_sw128(kv_base[slot] + off, 16, 1024), idesc_qk, kk > 0);
+          umma_ss(d, sdesc_sw128(q_base + i * kTile + off, 16, 1024),
+                  sdesc_sw128(kv_base + slot * kTile + off, 16, 1024), idesc_qk, kk > 0);
         }
       };
       auto issue_pv = [&](int i, int slot, bool acc) {
@@ -193,7 +203,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t a = tmem + i * 128;
 #pragma unroll
         for (int kk = 0; kk < kBN / 16; ++kk) {
-          umma_ts(d, a + kk * 8, sdesc_sw128(kv_base[slot] + kk * 2048, kPanel, 1024),
+          umma_ts(d, a + kk * 8, sdesc_sw128(kv_base + slot * kTile + kk * 2048, kPanel, 1024),
                   idesc_pv, (acc || kk > 0) ? 1u : 0u);
         }
       };
@@ -251,7 +261,17 @@ __global__ void __launch_bounds__(kThreads, 1)
       drain_wait(&sm.mma_done, 0);
     }
     __syncwarp();
+  }
+    // Teardown of the control warpgroup: TMEM is released once every warp is done.
+    tc_fence_before();
+    __syncthreads();
+    if (warp == kMmaWarp) {
+      tc_fence_after();
+      tmem_dealloc(tmem, kTmemCols);
+    }
+    return;
   } else {
+    regs_inc<kRegsSoftmax>();
     // ------------------------------------------------------------ softmax / epilogue
     const int i = warp >> 2;            // query tile of this warpgroup
     const int quarter = warp & 3;       // TMEM lane quarter this warp may access
@@ -281,18 +301,25 @@ __global__ void __launch_bounds__(kThreads, 1)
 
       int lim = kv_len - j * kBN;
       if (causal) lim = min(lim, grow - j * kBN + 1);
-      if (lim < kBN) {
+      const bool full = lim >= kBN;
+      if (!full) {
 #pragma unroll
         for (int c = 0; c < 4; ++c)
 #pragma unroll
           for (int e = 0; e < 32; ++e)
             if (c * 32 + e >= lim) r[c][e] = __float_as_uint(-INFINITY);
       }
-      float mx = -INFINITY;
+#define SV(e) __uint_as_float(r[(e) >> 5][(e) & 31])
+      // Row max: 8 independent 3-input-max chains, then a small tree.
+      float acc[8];
 #pragma unroll
-      for (int c = 0; c < 4; ++c)
+      for (int k = 0; k < 8; ++k) acc[k] = fmaxf(SV(2 * k), SV(2 * k + 1));
 #pragma unroll
-        for (int e = 0; e < 32; ++e) mx = fmaxf(mx, __uint_as_float(r[c][e]));
+      for (int e = 16; e < 128; e += 16)
+#pragma unroll
+        for (int k = 0; k < 8; ++k) acc[k] = max3f(acc[k], SV(e + 2 * k), SV(e + 2 * k + 1));
+      const float mx = max3f(max3f(acc[0], acc[1], acc[2]), max3f(acc[3], acc[4], acc[5]),
+                             fmaxf(acc[6], acc[7]));
       const float m_tile = mx * sl2;
       float m_use = m, alpha = 1.f;
       if (m == -INFINITY) {
@@ -303,18 +330,42 @@ __global__ void __launch_bounds__(kThreads, 1)
         alpha = ex2_approx(m - m_tile);
       }
       const float neg_base = (m_use == -INFINITY) ? 0.f : -m_use;
-      float sum = 0.f;
+      const uint64_t scale2 = f2pack(sl2, sl2), base2 = f2pack(neg_base, neg_base);
+      uint64_t sum2[4];
+#pragma unroll
+      for (int k = 0; k < 4; ++k) sum2[k] = 0ull;
       uint32_t pk[2][32];
+      // P = 2^(s*scale*log2e - m): pairs of columns through the packed FMA pipe; in full
+      // tiles kPolyPer8 of every 8 pairs take the polynomial exp2, the rest MUFU ex2.
+      if (full) {
 #pragma unroll
-      for (int c = 0; c < 4; ++c)
-#pragma unroll
-        for (int e = 0; e < 32; e += 2) {
-          const float p0 = ex2_approx(fmaf(__uint_as_float(r[c][e]), sl2, neg_base));
-          const float p1 = ex2_approx(fmaf(__uint_as_float(r[c][e + 1]), sl2, neg_base));
-          sum += p0 + p1;
-          const int col = c * 16 + (e >> 1);
-          pk[col >> 5][col & 31] = pack2<kOp>(p0, p1);
+        for (int pr = 0; pr < 64; ++pr) {
+          float x0, x1;
+          f2unpack(fma2(f2pack(SV(2 * pr), SV(2 * pr + 1)), scale2, base2), x0, x1);
+          if ((pr & 7) < kPolyPer8) {
+            exp2_poly_pair(x0, x1);
+          } else {
+            x0 = ex2_approx(x0);
+            x1 = ex2_approx(x1);
+          }
+          sum2[pr & 3] = add2(sum2[pr & 3], f2pack(x0, x1));
+          pk[pr >> 5][pr & 31] = pack2<kOp>(x0, x1);
         }
+      } else {
+#pragma unroll
+        for (int pr = 0; pr < 64; ++pr) {
+          float x0, x1;
+          f2unpack(fma2(f2pack(SV(2 * pr), SV(2 * pr + 1)), scale2, base2), x0, x1);
+          x0 = ex2_approx(x0);
+          x1 = ex2_approx(x1);
+          sum2[pr & 3] = add2(sum2[pr & 3], f2pack(x0, x1));
+          pk[pr >> 5][pr & 31] = pack2<kOp>(x0, x1);
+        }
+      }
+#undef SV
+      float sa, sb;
+      f2unpack(add2(add2(sum2[0], sum2[1]), add2(sum2[2], sum2[3])), sa, sb);
+      const float sum = sa + sb;
       l = l * alpha + sum;
       tmem_st32(tS, pk[0]);
       tmem_st32(tS + 32, pk[1]);
@@ -379,13 +430,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
     }
-  }
-
-  tc_fence_before();
-  __syncthreads();
-  if (warp == kMmaWarp) {
-    tc_fence_after();
-    tmem_dealloc(tmem, kTmemCols);
+    tc_fence_before();
+    __syncthreads();  // pairs with the control warpgroup's teardown barrier
   }
 }
 

@@ -209,6 +209,70 @@ __device__ __forceinline__ float ex2_approx(float x) {
   return y;
 }
 
+// ---------------------------------------------------------------- register budget
+// Per-warpgroup register reconfiguration; every warp of the warpgroup executes it.
+template <uint32_t kRegs>
+__device__ __forceinline__ void regs_inc() {
+  asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kRegs));
+}
+template <uint32_t kRegs>
+__device__ __forceinline__ void regs_dec() {
+  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kRegs));
+}
+
+// ---------------------------------------------------------------- fp32 math helpers
+__device__ __forceinline__ float max3f(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
+// Two fp32 values in one 64-bit register pair, for the packed f32x2 instructions.
+__device__ __forceinline__ uint64_t f2pack(float a, float b) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
+  return r;
+}
+__device__ __forceinline__ void f2unpack(uint64_t r, float& a, float& b) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(r));
+}
+__device__ __forceinline__ uint64_t fma2(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+__device__ __forceinline__ uint64_t add2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+
+// 2^x for a pair of fp32 values on the FMA/ALU pipes instead of the MUFU unit.
+// Cody-Waite style split x = n + f, n = round-to-nearest(x) by the 1.5*2^23 shifter
+// (the integer lands in the low mantissa bits), f in [-0.5, 0.5]; 2^f by a degree-3
+// minimax polynomial (relative error <= 7.5e-5 on [-0.5, 0.5], coefficients fitted for
+// this library by a Remez exchange); 2^n applied by adding n to the exponent field.
+// Inputs are clamped to >= -125 so the exponent never underflows: results below 2^-125
+// come out as ~2^-125 instead of 0, which is immaterial next to a row maximum >= 1.
+__device__ __forceinline__ void exp2_poly_pair(float& a, float& b) {
+  constexpr float kShift = 12582912.0f;  // 1.5 * 2^23
+  constexpr float c0 = 0.99992806f, c1 = 0.69326097f, c2 = 0.24261113f, c3 = 0.05517167f;
+  a = fmaxf(a, -125.f);
+  b = fmaxf(b, -125.f);
+  const uint64_t x = f2pack(a, b);
+  const uint64_t t = add2(x, f2pack(kShift, kShift));
+  const uint64_t n = add2(t, f2pack(-kShift, -kShift));
+  const uint64_t f = fma2(n, f2pack(-1.f, -1.f), x);
+  uint64_t p = fma2(f, f2pack(c3, c3), f2pack(c2, c2));
+  p = fma2(p, f, f2pack(c1, c1));
+  p = fma2(p, f, f2pack(c0, c0));
+  float p0, p1, t0, t1;
+  f2unpack(p, p0, p1);
+  f2unpack(t, t0, t1);
+  a = __int_as_float(__float_as_int(p0) + (__float_as_int(t0) << 23));
+  b = __int_as_float(__float_as_int(p1) + (__float_as_int(t1) << 23));
+}
+
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
   __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
   return *reinterpret_cast<uint32_t*>(&v);

@@ -8,8 +8,7 @@
 //   transpose     numpy_dit.py:291 ([B,S,H,D] -> [B,H,S,D])
 //   cast          fp32 -> bf16/f16 operands for the tensor cores
 // One warp owns one token (b, s) of one tensor and walks its H head rows, so the RoPE
-// row of that token is read once and reused for every head.  Lane t holds elements
-// {2t, 2t+1} and {64+2t, 64+2t+1} of a row: exactly the RoPE pairs p = 2t, 2t+1.
+// row of that token is read once and reused for every head (layout in prologue_kernel).
 //
 // rmsnorm_kernel / rope_kernel: the stand-alone drop-ins behind anima_rt_run_rmsnorm
 // and anima_rt_run_rope (fp32 in, fp32 out, any row length / even head size).
@@ -30,19 +29,26 @@ struct PrologueParams {
   long long tokens_q, tokens_k;  // B*S_q, B*S_kv
 };
 
+// Four consecutive elements of a row as fp32.
 template <typename T>
-__device__ __forceinline__ float2 load2(const T* p);
+__device__ __forceinline__ float4 load4(const T* p);
 template <>
-__device__ __forceinline__ float2 load2<float>(const float* p) {
-  return *reinterpret_cast<const float2*>(p);
+__device__ __forceinline__ float4 load4<float>(const float* p) {
+  return __ldg(reinterpret_cast<const float4*>(p));
 }
 template <>
-__device__ __forceinline__ float2 load2<__nv_bfloat16>(const __nv_bfloat16* p) {
-  return __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(p));
+__device__ __forceinline__ float4 load4<__nv_bfloat16>(const __nv_bfloat16* p) {
+  const uint2 u = __ldg(reinterpret_cast<const uint2*>(p));
+  const float2 a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.x));
+  const float2 b = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.y));
+  return make_float4(a.x, a.y, b.x, b.y);
 }
 template <>
-__device__ __forceinline__ float2 load2<__half>(const __half* p) {
-  return __half22float2(*reinterpret_cast<const __half2*>(p));
+__device__ __forceinline__ float4 load4<__half>(const __half* p) {
+  const uint2 u = __ldg(reinterpret_cast<const uint2*>(p));
+  const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&u.x));
+  const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&u.y));
+  return make_float4(a.x, a.y, b.x, b.y);
 }
 
 template <int kOp>
@@ -50,19 +56,42 @@ __device__ __forceinline__ uint32_t pack_op(float lo, float hi) {
   return kOp == ANIMA_DTYPE_BF16 ? pack_bf16x2(lo, hi) : pack_f16x2(lo, hi);
 }
 
+// x * inv * w with both products rounded (the reference's order), for 4 lanes of a row.
+__device__ __forceinline__ float4 scale4(float4 x, float inv, float4 w) {
+  return make_float4(__fmul_rn(__fmul_rn(x.x, inv), w.x), __fmul_rn(__fmul_rn(x.y, inv), w.y),
+                     __fmul_rn(__fmul_rn(x.z, inv), w.z), __fmul_rn(__fmul_rn(x.w, inv), w.w));
+}
+
+// One RoPE pair (a, c) with table entry f = [cos, -sin, sin, cos]; products and sums
+// rounded separately as in the reference (no FMA contraction).
+__device__ __forceinline__ void rot(float& a, float& c, float4 f) {
+  const float x = __fadd_rn(__fmul_rn(f.x, a), __fmul_rn(f.y, c));
+  const float y = __fadd_rn(__fmul_rn(f.z, a), __fmul_rn(f.w, c));
+  a = x;
+  c = y;
+}
+
+// Work item = one token (b, s) of one tensor.  A half-warp owns one head row: lane
+// l = lane & 15 holds elements [4l, 4l+4) and [64+4l, 64+4l+4), i.e. RoPE pairs
+// p = 4l..4l+3, so the rotation needs no shuffles and the norm reduces over 16 lanes.
+// The two half-warps take heads h and h+1; 2*kPairsInFlight heads are loaded before any
+// is processed to keep enough bytes in flight per SM.
 template <typename Tin, int kOp>
 __global__ void __launch_bounds__(256) prologue_kernel(const PrologueParams p) {
+  constexpr int kPairsInFlight = 4;  // 8 heads per batch of loads
   const int lane = threadIdx.x & 31;
+  const int hl = lane & 15;
+  const int half = lane >> 4;
   const long long warp0 = ((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const long long nwarps = ((long long)gridDim.x * blockDim.x) >> 5;
   const long long total = p.tokens_q + 2 * p.tokens_k;
 
-  float wq[4], wk[4];
+  float4 wlo[2], whi[2];
 #pragma unroll
-  for (int e = 0; e < 4; ++e) {
-    const int col = (e < 2) ? 2 * lane + e : 64 + 2 * lane + (e - 2);
-    wq[e] = p.w[0] ? p.w[0][col] : 1.f;
-    wk[e] = p.w[1] ? p.w[1][col] : 1.f;
+  for (int t = 0; t < 2; ++t) {
+    const float* w = p.w[t];
+    wlo[t] = w ? *reinterpret_cast<const float4*>(w + 4 * hl) : make_float4(1.f, 1.f, 1.f, 1.f);
+    whi[t] = w ? *reinterpret_cast<const float4*>(w + 64 + 4 * hl) : make_float4(1.f, 1.f, 1.f, 1.f);
   }
 
   for (long long item = warp0; item < total; item += nwarps) {
@@ -83,45 +112,58 @@ __global__ void __launch_bounds__(256) prologue_kernel(const PrologueParams p) {
     const int s = (int)(tok - (long long)b * S);
     const Tin* src = reinterpret_cast<const Tin*>(p.in[t]) + (long long)b * p.sb[t] +
                      (long long)s * p.ss[t];
-    uint32_t* dst = reinterpret_cast<uint32_t*>(p.out[t]);
+    const long long sh = p.sh[t];
+    uint2* dst = reinterpret_cast<uint2*>(p.out[t]);
     const bool norm = (p.norm_mask >> t) & 1u;
     const bool rope = (p.freqs != nullptr) && t < 2;
-    const float* w = t == 0 ? wq : wk;
+    const float4 w_lo = t == 1 ? wlo[1] : wlo[0];
+    const float4 w_hi = t == 1 ? whi[1] : whi[0];
 
-    float4 f0 = make_float4(1.f, 0.f, 0.f, 1.f), f1 = f0;
+    float4 f[4];
     if (rope) {
-      const float4* fr = reinterpret_cast<const float4*>(p.freqs + (long long)s * 256) + 2 * lane;
-      f0 = __ldg(fr);
-      f1 = __ldg(fr + 1);
+      const float4* fr = reinterpret_cast<const float4*>(p.freqs + (long long)s * 256) + 4 * hl;
+#pragma unroll
+      for (int k = 0; k < 4; ++k) f[k] = __ldg(fr + k);
     }
 
-#pragma unroll 4
-    for (int h = 0; h < p.H; ++h) {
-      const Tin* row = src + (long long)h * p.sh[t];
-      float2 a = load2<Tin>(row + 2 * lane);
-      float2 c = load2<Tin>(row + 64 + 2 * lane);
-      if (norm) {
-        float ss = a.x * a.x + a.y * a.y + c.x * c.x + c.y * c.y;
+    for (int h0 = 0; h0 < p.H; h0 += 2 * kPairsInFlight) {
+      float4 lo[kPairsInFlight], hi[kPairsInFlight];
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-        const float inv = 1.0f / sqrtf(ss / 128.0f + p.eps);
-        a.x = __fmul_rn(__fmul_rn(a.x, inv), w[0]);
-        a.y = __fmul_rn(__fmul_rn(a.y, inv), w[1]);
-        c.x = __fmul_rn(__fmul_rn(c.x, inv), w[2]);
-        c.y = __fmul_rn(__fmul_rn(c.y, inv), w[3]);
+      for (int u = 0; u < kPairsInFlight; ++u) {
+        const int h = h0 + 2 * u + half;
+        if (h < p.H) {
+          const Tin* row = src + (long long)h * sh;
+          lo[u] = load4<Tin>(row + 4 * hl);
+          hi[u] = load4<Tin>(row + 64 + 4 * hl);
+        } else {
+          lo[u] = hi[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+        }
       }
-      if (rope) {
-        // pair p = 2*lane uses f0 = [cos, -sin, sin, cos], pair 2*lane+1 uses f1
-        const float x0 = __fadd_rn(__fmul_rn(f0.x, a.x), __fmul_rn(f0.y, c.x));
-        const float y0 = __fadd_rn(__fmul_rn(f0.z, a.x), __fmul_rn(f0.w, c.x));
-        const float x1 = __fadd_rn(__fmul_rn(f1.x, a.y), __fmul_rn(f1.y, c.y));
-        const float y1 = __fadd_rn(__fmul_rn(f1.z, a.y), __fmul_rn(f1.w, c.y));
-        a = make_float2(x0, x1);
-        c = make_float2(y0, y1);
+#pragma unroll
+      for (int u = 0; u < kPairsInFlight; ++u) {
+        const int h = h0 + 2 * u + half;
+        float4 a = lo[u], c = hi[u];
+        if (norm) {
+          float ss = a.x * a.x + a.y * a.y + a.z * a.z + a.w * a.w + c.x * c.x + c.y * c.y +
+                     c.z * c.z + c.w * c.w;
+#pragma unroll
+          for (int o = 8; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+          const float inv = 1.0f / sqrtf(ss / 128.0f + p.eps);
+          a = scale4(a, inv, w_lo);
+          c = scale4(c, inv, w_hi);
+        }
+        if (rope) {
+          rot(a.x, c.x, f[0]);
+          rot(a.y, c.y, f[1]);
+          rot(a.z, c.z, f[2]);
+          rot(a.w, c.w, f[3]);
+        }
+        if (h < p.H) {
+          const long long orow = (((long long)b * p.H + h) * S + s) * 32;  // 8-byte units
+          dst[orow + hl] = make_uint2(pack_op<kOp>(a.x, a.y), pack_op<kOp>(a.z, a.w));
+          dst[orow + 16 + hl] = make_uint2(pack_op<kOp>(c.x, c.y), pack_op<kOp>(c.z, c.w));
+        }
       }
-      const long long orow = (((long long)b * p.H + h) * S + s) * 64;  // in 32-bit words
-      dst[orow + lane] = pack_op<kOp>(a.x, a.y);
-      dst[orow + 32 + lane] = pack_op<kOp>(c.x, c.y);
     }
   }
 }
@@ -195,14 +237,19 @@ int prologue_launch(const AnimaPrologueArgs* a, int sm_count, cudaStream_t st) {
   PrologueParams prm;
   for (int t = 0; t < 3; ++t) {
     for (int d = 0; d < 3; ++d)
-      if (st3[t][d] < 0 || (st3[t][d] % 2) != 0) return ANIMA_ERR_ARG;  // pair loads
-    if ((reinterpret_cast<uintptr_t>(in3[t]) % (2 * esz)) != 0) return ANIMA_ERR_ARG;
+      if (st3[t][d] < 0 || (st3[t][d] % 4) != 0) return ANIMA_ERR_ARG;  // 4-element loads
+    if ((reinterpret_cast<uintptr_t>(in3[t]) % (4 * esz)) != 0) return ANIMA_ERR_ARG;
     prm.in[t] = in3[t];
     prm.sb[t] = st3[t][0];
     prm.ss[t] = st3[t][1];
     prm.sh[t] = st3[t][2];
   }
   if ((reinterpret_cast<uintptr_t>(a->rope_freqs) & 15u) != 0) return ANIMA_ERR_ARG;
+  if ((reinterpret_cast<uintptr_t>(a->q_norm_w) & 15u) || (reinterpret_cast<uintptr_t>(a->k_norm_w) & 15u))
+    return ANIMA_ERR_ARG;
+  if ((reinterpret_cast<uintptr_t>(a->q_out) | reinterpret_cast<uintptr_t>(a->k_out) |
+       reinterpret_cast<uintptr_t>(a->v_out)) & 15u)
+    return ANIMA_ERR_ARG;
   prm.out[0] = a->q_out;
   prm.out[1] = a->k_out;
   prm.out[2] = a->v_out;
