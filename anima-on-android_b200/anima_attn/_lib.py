@@ -38,7 +38,8 @@ class AttnArgs(ct.Structure):
     _fields_ = [("q", _P), ("k", _P), ("v", _P), ("op_dtype", ct.c_int), ("out", _P),
                 ("out_dtype", ct.c_int), ("out_stride", _I64x3), ("B", ct.c_int),
                 ("H", ct.c_int), ("S_q", ct.c_int), ("S_kv", ct.c_int), ("D", ct.c_int),
-                ("scale", ct.c_float), ("flags", ct.c_uint), ("kv_valid_len", _P)]
+                ("scale", ct.c_float), ("flags", ct.c_uint), ("kv_valid_len", _P),
+                ("workspace", _P), ("workspace_bytes", ct.c_uint64)]
 
 
 # Every symbol the headers declare, with its ctypes signature.
@@ -56,6 +57,7 @@ SIGNATURES = {
     # include/anima_attn.h
     "anima_attn_prologue": ([ct.POINTER(PrologueArgs), _P], ct.c_int),
     "anima_attn_fwd": ([ct.POINTER(AttnArgs), _P], ct.c_int),
+    "anima_attn_workspace_size": ([ct.c_int] * 4 + [ct.c_uint], ct.c_uint64),
     "anima_attn_status": ([_P, ct.c_int], ct.c_int),
     "anima_attn_device_info": ([ct.POINTER(ct.c_int), ct.POINTER(ct.c_int)], ct.c_int),
     "anima_attn_version": ([], ct.c_char_p),

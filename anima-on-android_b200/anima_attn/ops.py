@@ -100,15 +100,33 @@ def prologue(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
     return qo, ko, vo
 
 
+_WORKSPACES: dict = {}
+
+
+def _workspace(device: torch.device, nbytes: int) -> Optional[torch.Tensor]:
+    """Grow-only scratch per (device, stream) for the stream-K schedule's partials."""
+    if nbytes == 0:
+        return None
+    key = (device.index, torch.cuda.current_stream(device).cuda_stream)
+    ws = _WORKSPACES.get(key)
+    if ws is None or ws.numel() < nbytes:
+        ws = torch.empty(nbytes, dtype=torch.uint8, device=device)
+        _WORKSPACES[key] = ws
+    return ws
+
+
 def attention_core(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, B: int, H: int,
                    scale: Optional[float] = None, kv_valid_len: Optional[torch.Tensor] = None,
                    causal: bool = False, out: Optional[torch.Tensor] = None,
-                   out_layout: str = "bshd", out_dtype=torch.float32) -> torch.Tensor:
+                   out_layout: str = "bshd", out_dtype=torch.float32,
+                   stream_k: bool = True) -> torch.Tensor:
     """tcgen05 flash attention on 16-bit head-major operands.
 
     q [B*H, S_q, 128], k/v [B*H, S_kv, 128] contiguous bf16/fp16.  Returns (or fills)
     ``out`` in ``out_layout`` "bshd" [B, S_q, H, D] or "bhsd" [B, H, S_q, D].
     ``kv_valid_len`` int32 [B] masks keys >= kv_valid_len[b] (cross-attention padding).
+    ``stream_k`` lets calls of more than one wave use the persistent stream-K schedule
+    (with a cached workspace); False forces one CTA per 256-row unit.
     """
     _check_cuda(q, k, v)
     BH, Sq, D = q.shape
@@ -147,6 +165,11 @@ def attention_core(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, B: int, H:
     a.scale = float(1.0 / math.sqrt(D) if scale is None else scale)
     a.flags = flags
     a.kv_valid_len = _ptr(vl)
+    ws = None
+    if stream_k:
+        ws = _workspace(q.device, int(L.lib.anima_attn_workspace_size(B, H, Sq, Skv, flags)))
+    a.workspace = _ptr(ws)
+    a.workspace_bytes = 0 if ws is None else ws.numel()
     L.check(L.lib.anima_attn_fwd(ct.byref(a), ct.c_void_p(_stream())), "anima_attn_fwd")
     return out
 

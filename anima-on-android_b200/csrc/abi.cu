@@ -15,7 +15,8 @@
 #include "common.cuh"
 
 namespace anima {
-int attn_fwd_launch(const AnimaAttnArgs* a, int* status, cudaStream_t st);
+int attn_fwd_launch(const AnimaAttnArgs* a, int* status, int sm_count, cudaStream_t st);
+size_t attn_workspace_bytes(int B, int H, int S_q, unsigned flags, int sm_count);
 int prologue_launch(const AnimaPrologueArgs* a, int sm_count, cudaStream_t st);
 int rmsnorm_launch(const float* x, const float* w, float* y, long long m, int d, float eps,
                    int sm_count, cudaStream_t st);
@@ -190,6 +191,12 @@ bool rt_attention(const float* q, const float* k, const float* v, const float* q
   const size_t o_w = carve(2 * D * 4);
   const size_t o_f = carve(freqs ? (size_t)S_q * D * 2 * 4 : 0);
   const size_t o_valid = carve(kv_valid ? (size_t)B * 4 : 0);
+  const unsigned aflags = (flags & ANIMA_FLAG_CAUSAL) | (kv_valid ? ANIMA_FLAG_MASK : 0u);
+  int drc = ANIMA_OK;
+  DeviceState* dev = current_device(&drc);
+  if (!dev) return false;
+  const size_t ws_split = attn_workspace_bytes(B, H, S_q, aflags, dev->sm_count);
+  const size_t o_split = carve(ws_split);
   if (!rt_prepare(off)) return false;
   char* ws = static_cast<char*>(g_rt.ws);
   cudaStream_t st = g_rt.stream;
@@ -256,8 +263,10 @@ bool rt_attention(const float* q, const float* k, const float* v, const float* q
   aa.S_kv = S_kv;
   aa.D = D;
   aa.scale = scale;
-  aa.flags = (flags & ANIMA_FLAG_CAUSAL) | (kv_valid ? ANIMA_FLAG_MASK : 0u);
+  aa.flags = aflags;
   aa.kv_valid_len = kv_valid ? (const int*)(ws + o_valid) : nullptr;
+  aa.workspace = ws_split ? ws + o_split : nullptr;
+  aa.workspace_bytes = ws_split;
   rc = anima_attn_fwd(&aa, st);
   if (rc != ANIMA_OK) return rt_fail(std::string(who) + ": attention: " + code_name(rc));
   if (!rt_check(cudaMemcpyAsync(out, dout, nq * 4, cudaMemcpyDeviceToHost, st), who))
@@ -292,9 +301,17 @@ int anima_attn_fwd(const AnimaAttnArgs* a, void* stream) {
   int rc = ANIMA_OK;
   DeviceState* d = current_device(&rc);
   if (!d) return rc;
-  rc = attn_fwd_launch(a, d->status, static_cast<cudaStream_t>(stream));
+  rc = attn_fwd_launch(a, d->status, d->sm_count, static_cast<cudaStream_t>(stream));
   if (rc != ANIMA_OK) set_error(std::string("anima_attn_fwd: ") + code_name(rc));
   return rc;
+}
+
+uint64_t anima_attn_workspace_size(int B, int H, int S_q, int S_kv, unsigned flags) {
+  (void)S_kv;
+  int rc = ANIMA_OK;
+  DeviceState* d = current_device(&rc);
+  if (!d || B <= 0 || H <= 0 || S_q <= 0) return 0;
+  return attn_workspace_bytes(B, H, S_q, flags, d->sm_count);
 }
 
 int anima_attn_status(void* stream, int reset) {
@@ -324,8 +341,9 @@ int anima_attn_device_info(int* sm_count, int* cc) {
 }
 
 const char* anima_attn_version(void) {
-  return "anima_attn sm_100a: tcgen05 flash fwd (2x128-row Q tiles/CTA, 128-key tiles, "
-         "4-slot K/V ring, TMEM S/P/O), fused RMSNorm+RoPE prologue";
+  return "anima_attn sm_100a: tcgen05 flash fwd (2x128-row Q tiles per unit, 128-key tiles, "
+         "4-slot K/V ring, TMEM S/P/O, stream-K persistent schedule), fused RMSNorm+RoPE "
+         "prologue";
 }
 
 // ---------------------------------------------------------------- anima_rt drop-ins

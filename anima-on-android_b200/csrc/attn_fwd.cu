@@ -1,29 +1,37 @@
-// attn_fwd.cu -- non-causal / causal / key-padding-masked flash-attention forward for
-// sm_100a: TMA-staged tiles, tcgen05.mma with TMEM accumulators, fp32 online softmax.
+// attn_fwd.cu -- flash-attention forward for sm_100a: TMA-staged tiles, tcgen05.mma
+// with TMEM accumulators, fp32 online softmax; non-causal, causal and key-padding
+// masked.  Replaces anima::cpu::flash_attention
+// (anima_rt/include/cpu/flash_attention.h:55-208): out = softmax(Q K^T * scale) V per
+// (batch, head), D = 128.
 //
-// Replaces anima::cpu::flash_attention (anima_rt/include/cpu/flash_attention.h:55-208):
-// out = softmax(Q K^T * scale) V per (batch, head), D = 128.  The reference tiles
-// queries by 256/64/32 and keys by 512 on one CPU thread; here one CTA owns 256 query
-// rows of one head and streams 128-key tiles:
+// Work unit = 256 query rows (two 128-row tiles) of one (batch, head) against its keys,
+// streamed in 128-key tiles.  Two schedules share one kernel:
+//   unit mode      one CTA per unit (masked / causal calls, or at most one wave);
+//   stream-K mode  a persistent grid of one CTA per SM takes an equal slice of the
+//                  (unit x key-tile) sequence, so the last wave is not partly idle.  A
+//                  unit cut by a slice boundary is finished by attn_combine_kernel from
+//                  the two fp32 partials (O, running max, running sum) its CTAs wrote.
 //
-//   warp 8     TMA producer: Q (2 tiles, once), then K_j / V_j into a 4-slot ring
+// Warp roles (384 threads, 3 warpgroups):
+//   warps 0-7  two softmax warpgroups, one per query tile; thread = query row = TMEM
+//              lane.  Reads its S row from TMEM, updates running max / sum, writes P
+//              (16-bit) back over S, rescales its O row when the max moved, and at the
+//              end of a segment stores O (or the partial) and frees O for the next one.
+//   warp 8     TMA producer of K_j / V_j through a 4-slot ring.
 //   warp 9     MMA issuer (one thread) + TMEM owner:
-//                S_i  = Q_i K_j^T          (SS form, both operands in shared memory)
-//                O_i += P_i V_j            (TS form, P read from tensor memory)
-//   warps 10-11 idle (they complete the third warpgroup, which donates its registers)
-//   warps 0-7  two softmax warpgroups, one per 128-row Q tile; thread = query row =
-//              TMEM lane.  Each reads its S row from TMEM, updates the running max
-//              and sum, writes P (16-bit) back over S, rescales its O row when the
-//              max moved, and finally normalises O and stores it.
+//                S_i  = Q_i K_j^T   (SS form, both operands in shared memory)
+//                O_i += P_i V_j     (TS form, P read from tensor memory)
+//   warp 10    TMA producer of the Q tiles of each segment.
+//   warp 11    idle.  Warps 8-11 give registers to the softmax warpgroups (setmaxnreg).
 //
 // Tensor memory (512 columns x 128 lanes, fp32): S_0 [0,128) S_1 [128,256)
-// O_0 [256,384) O_1 [384,512); P_i overlays the first 64 columns of S_i (two 16-bit
-// values per column).  The two query tiles ping-pong: while warpgroup 0 runs the
-// softmax of tile 0, the tensor core computes tile 1, and vice versa.
+// O_0 [256,384) O_1 [384,512); P_i overlays the first 64 columns of S_i.  The two query
+// tiles ping-pong: while warpgroup 0 runs the softmax of tile 0 the tensor core works
+// on tile 1, and vice versa.
 //
-// Online softmax in the exp2 domain (scores scaled by scale*log2(e)), with a lazy
-// rescale: the running max used for P moves only when the new row max exceeds it by
-// more than 8 (a factor 256), so the O correction is rare after the first tiles.
+// Online softmax in the exp2 domain (scores scaled by scale*log2(e)) with a lazy
+// rescale: the max used for P moves only when the new row max exceeds it by more than
+// 8 (a factor 256), so the O correction is rare after the first tiles.
 #include "common.cuh"
 
 namespace anima {
@@ -31,34 +39,42 @@ namespace attn {
 
 constexpr int kD = 128;
 constexpr int kBM = 128;               // query rows per tile (TMEM lanes)
-constexpr int kNT = 2;                 // query tiles per CTA
+constexpr int kNT = 2;                 // query tiles per unit
+constexpr int kUnitRows = kBM * kNT;   // 256
 constexpr int kBN = 128;               // keys per K/V tile
 constexpr int kStages = 4;             // K/V ring slots
 constexpr int kPanel = 128 * 128;      // [128 rows][64 x 16-bit], 128B-swizzled = 16 KB
 constexpr int kTile = 2 * kPanel;      // [128 rows][128 x 16-bit] = 32 KB
-constexpr int kProducerWarp = 8;
+constexpr int kKvWarp = 8;
 constexpr int kMmaWarp = 9;
-constexpr int kThreads = 384;              // 3 warpgroups
+constexpr int kQWarp = 10;
+constexpr int kThreads = 384;          // 3 warpgroups
 // Launch budget 384 x 168 registers; the control warpgroup gives registers back to the
-// two softmax warpgroups: 2*128*208 + 128*80 = 63488 <= 384*168.
-constexpr uint32_t kRegsSoftmax = 208;
-constexpr uint32_t kRegsControl = 80;
+// two softmax warpgroups: 2*128*200 + 128*104 = 64512 = 384*168.
+constexpr uint32_t kRegsSoftmax = 200;
+constexpr uint32_t kRegsControl = 104;
 constexpr uint32_t kTmemCols = 512;
 constexpr float kRescaleThreshold = 8.0f;  // log2 units
 #ifndef ANIMA_POLY_PER8
-#define ANIMA_POLY_PER8 2
+#define ANIMA_POLY_PER8 0
 #endif
-constexpr int kPolyPer8 = ANIMA_POLY_PER8;  // of every 8 column pairs, polynomial exp2
+// Of every 8 column pairs, how many take the FMA-pipe polynomial exp2 instead of MUFU.
+// 0 by default: on this kernel the tensor pipe is bounded by shared-memory operand
+// bandwidth, not by MUFU, and measured cycles were 1-5% lower with MUFU alone.
+constexpr int kPolyPer8 = ANIMA_POLY_PER8;
+// One partial of a split unit: O [256][128] fp32 (unnormalised), then m [256], l [256].
+constexpr int kPartFloats = kUnitRows * kD + 2 * kUnitRows;
 
 struct Smem {
   uint8_t q[kNT][kTile];
   uint8_t kv[kStages][kTile];
-  uint64_t bar_q;
+  uint64_t q_full, q_empty;
   uint64_t kv_full[kStages];
   uint64_t kv_empty[kStages];
   uint64_t s_full[kNT];
   uint64_t p_full[kNT];
   uint64_t o_full[kNT];
+  uint64_t o_empty[kNT];
   uint64_t mma_done;
   uint32_t tmem_base;
   int abort;
@@ -75,6 +91,72 @@ struct Params {
   void* out;
   long long ob, oh, os;
   int* status;
+  int nqb;             // query units per (batch, head)
+  int split;           // 1: stream-K over uniform key tiles
+  int n_kv;            // key tiles per unit (stream-K mode)
+  long long total;     // units * n_kv (stream-K mode)
+  float* part;         // stream-K partial slots [gridDim.x][2][kPartFloats]
+};
+
+// One piece of work of a CTA: key tiles [k0, k1) of unit `unit`.
+struct Seg {
+  int unit, k0, k1;
+  int full;            // covers every key tile of the unit
+  int slot;            // partial slot (0: starts the CTA's slice, 1: ends it)
+};
+
+// Key tiles of a unit in unit mode (mask / causal aware).
+__device__ __forceinline__ int unit_kv_len(const Params& p, int unit) {
+  const int b = (unit / p.nqb) / p.H;
+  int kv_len = p.S_kv;
+  if (p.flags & ANIMA_FLAG_MASK) kv_len = min(max(p.kv_valid[b], 0), p.S_kv);
+  return kv_len;
+}
+__device__ __forceinline__ int unit_tiles(const Params& p, int unit) {
+  if (p.split) return p.n_kv;
+  int n = (unit_kv_len(p, unit) + kBN - 1) / kBN;
+  if (p.flags & ANIMA_FLAG_CAUSAL) {
+    const int q0 = (unit % p.nqb) * kUnitRows;
+    const int last_row = min(q0 + kUnitRows, p.S_q) - 1;
+    n = min(n, last_row / kBN + 1);
+  }
+  return n;
+}
+
+// Segment iterator: every role walks the same sequence.
+struct SegIter {
+  long long t, lo, hi;
+  __device__ __forceinline__ SegIter(const Params& p) {
+    if (p.split) {
+      lo = (long long)blockIdx.x * p.total / gridDim.x;
+      hi = (long long)(blockIdx.x + 1) * p.total / gridDim.x;
+    } else {
+      lo = 0;
+      hi = 1;
+    }
+    t = lo;
+  }
+  __device__ __forceinline__ bool next(const Params& p, Seg& s) {
+    if (t >= hi) return false;
+    if (!p.split) {
+      s.unit = blockIdx.x;
+      s.k0 = 0;
+      s.k1 = unit_tiles(p, s.unit);
+      s.full = 1;
+      s.slot = 0;
+      t = hi;
+      return true;
+    }
+    const int n = p.n_kv;
+    s.unit = (int)(t / n);
+    const long long ubeg = (long long)s.unit * n, uend = ubeg + n;
+    s.k0 = (int)(t - ubeg);
+    s.k1 = (int)(min(uend, hi) - ubeg);
+    s.full = (s.k0 == 0 && s.k1 == n);
+    s.slot = (t == lo) ? 0 : 1;
+    t = min(uend, hi);
+    return true;
+  }
 };
 
 // Bounded wait that only gives up on its time limit; used to drain in-flight copies
@@ -92,6 +174,27 @@ __device__ __forceinline__ uint32_t pack2(float lo, float hi) {
   return kOp == ANIMA_DTYPE_BF16 ? pack_bf16x2(lo, hi) : pack_f16x2(lo, hi);
 }
 
+template <int kOut>
+__device__ __forceinline__ void store_row(char* out_row, const uint32_t (&o)[32], int c,
+                                          float inv) {
+  if (kOut == ANIMA_DTYPE_F32) {
+    float4* dst = reinterpret_cast<float4*>(out_row) + c * 8;
+#pragma unroll
+    for (int e = 0; e < 8; ++e)
+      dst[e] = make_float4(__uint_as_float(o[4 * e]) * inv, __uint_as_float(o[4 * e + 1]) * inv,
+                           __uint_as_float(o[4 * e + 2]) * inv, __uint_as_float(o[4 * e + 3]) * inv);
+  } else {
+    uint4* dst = reinterpret_cast<uint4*>(out_row) + c * 4;
+#pragma unroll
+    for (int e = 0; e < 4; ++e)
+      dst[e] = make_uint4(
+          pack_bf16x2(__uint_as_float(o[8 * e]) * inv, __uint_as_float(o[8 * e + 1]) * inv),
+          pack_bf16x2(__uint_as_float(o[8 * e + 2]) * inv, __uint_as_float(o[8 * e + 3]) * inv),
+          pack_bf16x2(__uint_as_float(o[8 * e + 4]) * inv, __uint_as_float(o[8 * e + 5]) * inv),
+          pack_bf16x2(__uint_as_float(o[8 * e + 6]) * inv, __uint_as_float(o[8 * e + 7]) * inv));
+  }
+}
+
 template <int kOp, int kOut>
 __global__ void __launch_bounds__(kThreads, 1)
     attn_fwd_kernel(const __grid_constant__ CUtensorMap tmap_q,
@@ -103,21 +206,11 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int bh = blockIdx.y;
-  const int b = bh / p.H;
-  const int q0 = blockIdx.x * (kBM * kNT);
-
-  int kv_len = p.S_kv;
-  if (p.flags & ANIMA_FLAG_MASK) kv_len = min(max(p.kv_valid[b], 0), p.S_kv);
-  int n_kv = (kv_len + kBN - 1) / kBN;
-  if (p.flags & ANIMA_FLAG_CAUSAL) {
-    const int last_row = min(q0 + kBM * kNT, p.S_q) - 1;
-    n_kv = min(n_kv, last_row / kBN + 1);
-  }
   volatile int* abort = &sm.abort;
 
   if (threadIdx.x == 0) {
-    mbar_init(&sm.bar_q, 1);
+    mbar_init(&sm.q_full, 1);
+    mbar_init(&sm.q_empty, 1);
     for (int s = 0; s < kStages; ++s) {
       mbar_init(&sm.kv_full[s], 1);
       mbar_init(&sm.kv_empty[s], 1);
@@ -126,6 +219,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&sm.s_full[i], 1);
       mbar_init(&sm.p_full[i], kBM);
       mbar_init(&sm.o_full[i], 1);
+      mbar_init(&sm.o_empty[i], kBM);
     }
     mbar_init(&sm.mma_done, 1);
     sm.abort = 0;
@@ -142,47 +236,63 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (warp >= 8) {
     regs_dec<kRegsControl>();
-  if (warp == kProducerWarp) {
-    // ------------------------------------------------------------ TMA producer
-    if (lane == 0) {
-      tma_prefetch_desc(&tmap_q);
+    if (warp == kKvWarp && lane == 0) {
+      // ---------------------------------------------------------- K/V producer
       tma_prefetch_desc(&tmap_k);
       tma_prefetch_desc(&tmap_v);
-      mbar_arrive_expect_tx(&sm.bar_q, kNT * kTile);
-      for (int i = 0; i < kNT; ++i)
-        for (int pn = 0; pn < 2; ++pn)
-          tma_load_3d(sm.q[i] + pn * kPanel, &tmap_q, &sm.bar_q, pn * 64, q0 + i * kBM, bh);
-      int issued = 0;
+      SegIter it(p);
+      Seg sg;
+      int item = 0;  // K of tile-step g is item 2g, V is item 2g+1
       bool ok = true;
-      for (int j = 0; j < n_kv && ok; ++j) {
-        for (int kind = 0; kind < 2; ++kind) {
-          const int c = 2 * j + kind;
-          const int slot = c % kStages;
-          const uint32_t round = c / kStages;
-          if (!mbar_wait(&sm.kv_empty[slot], (round & 1u) ^ 1u, abort, p.status,
-                         ANIMA_ERR_TIMEOUT)) {
-            ok = false;
-            break;
+      while (ok && it.next(p, sg)) {
+        const int bh = sg.unit / p.nqb;
+        for (int j = sg.k0; j < sg.k1 && ok; ++j) {
+          for (int kind = 0; kind < 2; ++kind, ++item) {
+            const int slot = (int)(item % kStages);
+            const uint32_t round = (uint32_t)(item / kStages);
+            if (!mbar_wait(&sm.kv_empty[slot], (round & 1u) ^ 1u, abort, p.status,
+                           ANIMA_ERR_TIMEOUT)) {
+              ok = false;
+              break;
+            }
+            mbar_arrive_expect_tx(&sm.kv_full[slot], kTile);
+            const CUtensorMap* m = kind ? &tmap_v : &tmap_k;
+            tma_load_3d(sm.kv[slot], m, &sm.kv_full[slot], 0, j * kBN, bh);
+            tma_load_3d(sm.kv[slot] + kPanel, m, &sm.kv_full[slot], 64, j * kBN, bh);
           }
-          mbar_arrive_expect_tx(&sm.kv_full[slot], kTile);
-          const CUtensorMap* m = kind ? &tmap_v : &tmap_k;
-          tma_load_3d(sm.kv[slot], m, &sm.kv_full[slot], 0, j * kBN, bh);
-          tma_load_3d(sm.kv[slot] + kPanel, m, &sm.kv_full[slot], 64, j * kBN, bh);
-          ++issued;
         }
       }
       // Every copy this thread started must land before the CTA may exit.
-      drain_wait(&sm.bar_q, 0);
       for (int s = 0; s < kStages; ++s) {
         int last = -1;
-        for (int c = s; c < issued; c += kStages) last = c;
+        for (int c = s; c < item; c += kStages) last = c;
         if (last >= 0) drain_wait(&sm.kv_full[s], (uint32_t)(last / kStages) & 1u);
       }
-    }
-    __syncwarp();
-  } else if (warp == kMmaWarp) {
-    // ------------------------------------------------------------ MMA issuer
-    if (lane == 0 && n_kv > 0) {
+    } else if (warp == kQWarp && lane == 0) {
+      // ---------------------------------------------------------- Q producer
+      tma_prefetch_desc(&tmap_q);
+      SegIter it(p);
+      Seg sg;
+      int a = 0;  // active (non-empty) segments so far
+      bool ok = true;
+      while (ok && it.next(p, sg)) {
+        if (sg.k1 <= sg.k0) continue;
+        if (a > 0 && !mbar_wait(&sm.q_empty, (uint32_t)(a - 1) & 1u, abort, p.status,
+                                ANIMA_ERR_TIMEOUT)) {
+          ok = false;
+          break;
+        }
+        const int bh = sg.unit / p.nqb;
+        const int q0 = (sg.unit % p.nqb) * kUnitRows;
+        mbar_arrive_expect_tx(&sm.q_full, kNT * kTile);
+        for (int i = 0; i < kNT; ++i)
+          for (int pn = 0; pn < 2; ++pn)
+            tma_load_3d(sm.q[i] + pn * kPanel, &tmap_q, &sm.q_full, pn * 64, q0 + i * kBM, bh);
+        ++a;
+      }
+      if (a > 0) drain_wait(&sm.q_full, (uint32_t)(a - 1) & 1u);
+    } else if (warp == kMmaWarp && lane == 0) {
+      // ---------------------------------------------------------- MMA issuer
       constexpr uint32_t ab = kOp == ANIMA_DTYPE_BF16 ? 1u : 0u;  // idesc: 0 f16, 1 bf16
       constexpr uint32_t idesc_qk = make_idesc_f16(ab, kBM, kBN, 0);
       constexpr uint32_t idesc_pv = make_idesc_f16(ab, kBM, kD, 1);
@@ -210,58 +320,76 @@ __global__ void __launch_bounds__(kThreads, 1)
       auto wait = [&](uint64_t* bar, uint32_t parity) {
         return mbar_wait(bar, parity, abort, p.status, ANIMA_ERR_TIMEOUT);
       };
+      auto slot_of = [](int item) { return item % kStages; };
+      auto par_of = [](int item) { return (uint32_t)(item / kStages) & 1u; };
 
-      bool ok = wait(&sm.bar_q, 0) && wait(&sm.kv_full[0], 0);
-      if (ok) {
+      SegIter it(p);
+      Seg sg;
+      int g = 0;        // global tile-step counter
+      int a = 0;        // active segments so far
+      bool ok = true;
+      while (ok && it.next(p, sg)) {
+        const int n = sg.k1 - sg.k0;
+        if (n <= 0) continue;
+        const uint32_t pa = (uint32_t)(a - 1) & 1u;  // parity of the previous segment
+        if (!(ok = wait(&sm.q_full, (uint32_t)a & 1u))) break;
         tc_fence_after();
-        issue_qk(0, 0);
-        umma_commit(&sm.s_full[0]);
-        issue_qk(1, 0);
-        umma_commit(&sm.s_full[1]);
-        umma_commit(&sm.kv_empty[0]);
-      }
-      for (int j = 1; j < n_kv && ok; ++j) {
-        const int ck = 2 * j, cv = 2 * (j - 1) + 1;
-        const int sk = ck % kStages, sv = cv % kStages;
-        const uint32_t pk = (uint32_t)(ck / kStages) & 1u, pv = (uint32_t)(cv / kStages) & 1u;
-        const uint32_t pp = (uint32_t)(j - 1) & 1u;
-        ok = wait(&sm.kv_full[sk], pk) && wait(&sm.kv_full[sv], pv) && wait(&sm.p_full[0], pp);
+        for (int jj = 0; jj < n && ok; ++jj, ++g) {
+          const int ik = 2 * g;
+          if (!(ok = wait(&sm.kv_full[slot_of(ik)], par_of(ik)))) break;
+          if (jj == 0) {
+            tc_fence_after();
+            issue_qk(0, slot_of(ik));
+            umma_commit(&sm.s_full[0]);
+            issue_qk(1, slot_of(ik));
+            umma_commit(&sm.s_full[1]);
+            umma_commit(&sm.kv_empty[slot_of(ik)]);
+          } else {
+            const int iv = 2 * (g - 1) + 1;
+            const uint32_t pp = (uint32_t)(g - 1) & 1u;
+            ok = wait(&sm.kv_full[slot_of(iv)], par_of(iv)) && wait(&sm.p_full[0], pp);
+            if (ok && jj == 1 && a > 0) ok = wait(&sm.o_empty[0], pa);
+            if (!ok) break;
+            tc_fence_after();
+            issue_pv(0, slot_of(iv), jj > 1);
+            issue_qk(0, slot_of(ik));
+            umma_commit(&sm.s_full[0]);
+            ok = wait(&sm.p_full[1], pp);
+            if (ok && jj == 1 && a > 0) ok = wait(&sm.o_empty[1], pa);
+            if (!ok) break;
+            tc_fence_after();
+            issue_pv(1, slot_of(iv), jj > 1);
+            umma_commit(&sm.kv_empty[slot_of(iv)]);
+            issue_qk(1, slot_of(ik));
+            umma_commit(&sm.s_full[1]);
+            umma_commit(&sm.kv_empty[slot_of(ik)]);
+          }
+          if (jj == n - 1) umma_commit(&sm.q_empty);  // all QK^T of this segment issued
+        }
+        if (!ok) break;
+        // tail: P V of the segment's last key tile, then O is final
+        const int iv = 2 * (g - 1) + 1;
+        const uint32_t pp = (uint32_t)(g - 1) & 1u;
+        ok = wait(&sm.kv_full[slot_of(iv)], par_of(iv)) && wait(&sm.p_full[0], pp);
+        if (ok && n == 1 && a > 0) ok = wait(&sm.o_empty[0], pa);
         if (!ok) break;
         tc_fence_after();
-        issue_pv(0, sv, j - 1 > 0);
-        issue_qk(0, sk);
-        umma_commit(&sm.s_full[0]);
-        if (!(ok = wait(&sm.p_full[1], pp))) break;
+        issue_pv(0, slot_of(iv), n > 1);
+        umma_commit(&sm.o_full[0]);
+        ok = wait(&sm.p_full[1], pp);
+        if (ok && n == 1 && a > 0) ok = wait(&sm.o_empty[1], pa);
+        if (!ok) break;
         tc_fence_after();
-        issue_pv(1, sv, j - 1 > 0);
-        umma_commit(&sm.kv_empty[sv]);
-        issue_qk(1, sk);
-        umma_commit(&sm.s_full[1]);
-        umma_commit(&sm.kv_empty[sk]);
-      }
-      if (ok) {
-        const int j = n_kv - 1;
-        const int cv = 2 * j + 1, sv = cv % kStages;
-        const uint32_t pv = (uint32_t)(cv / kStages) & 1u, pp = (uint32_t)j & 1u;
-        ok = wait(&sm.kv_full[sv], pv) && wait(&sm.p_full[0], pp);
-        if (ok) {
-          tc_fence_after();
-          issue_pv(0, sv, j > 0);
-          umma_commit(&sm.o_full[0]);
-          if (wait(&sm.p_full[1], pp)) {
-            tc_fence_after();
-            issue_pv(1, sv, j > 0);
-            umma_commit(&sm.o_full[1]);
-            umma_commit(&sm.kv_empty[sv]);
-          }
-        }
+        issue_pv(1, slot_of(iv), n > 1);
+        umma_commit(&sm.o_full[1]);
+        umma_commit(&sm.kv_empty[slot_of(iv)]);
+        ++a;
       }
       // Let every MMA this thread issued retire before TMEM is released.
       umma_commit(&sm.mma_done);
       drain_wait(&sm.mma_done, 0);
     }
     __syncwarp();
-  }
     // Teardown of the control warpgroup: TMEM is released once every warp is done.
     tc_fence_before();
     __syncthreads();
@@ -276,162 +404,216 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int i = warp >> 2;            // query tile of this warpgroup
     const int quarter = warp & 3;       // TMEM lane quarter this warp may access
     const int row = quarter * 32 + lane;
-    const int grow = q0 + i * kBM + row;
     const uint32_t lane_field = (uint32_t)(quarter * 32) << 16;
     const uint32_t tS = tmem + lane_field + i * 128;
     const uint32_t tO = tmem + lane_field + 256 + i * 128;
     const bool causal = (p.flags & ANIMA_FLAG_CAUSAL) != 0;
     const float sl2 = p.scale_log2;
 
-    float m = -INFINITY;  // running max, scaled log2 units
-    float l = 0.f;        // running sum of P
+    SegIter it(p);
+    Seg sg;
+    int g = 0;
+    int a = 0;
     bool ok = true;
-    for (int j = 0; j < n_kv; ++j) {
-      const bool got = mbar_wait(&sm.s_full[i], (uint32_t)j & 1u, abort, p.status,
-                                 ANIMA_ERR_TIMEOUT);
-      if (!__all_sync(0xffffffffu, got)) {
-        ok = false;
-        break;
-      }
-      tc_fence_after();
-      uint32_t r[4][32];
+    while (ok && it.next(p, sg)) {
+      const int bh = sg.unit / p.nqb;
+      const int b = bh / p.H;
+      const int grow = (sg.unit % p.nqb) * kUnitRows + i * kBM + row;
+      const int kv_len = unit_kv_len(p, sg.unit);
+      const int n = sg.k1 - sg.k0;
+      float m = -INFINITY;  // running max, scaled log2 units
+      float l = 0.f;        // running sum of P
+      for (int jj = 0; jj < n; ++jj, ++g) {
+        const int j = sg.k0 + jj;  // key tile index within the unit
+        const bool got = mbar_wait(&sm.s_full[i], (uint32_t)g & 1u, abort, p.status,
+                                   ANIMA_ERR_TIMEOUT);
+        if (!__all_sync(0xffffffffu, got)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        uint32_t r[4][32];
 #pragma unroll
-      for (int c = 0; c < 4; ++c) tmem_ld32(tS + c * 32, r[c]);
-      tmem_ld_wait();
+        for (int c = 0; c < 4; ++c) tmem_ld32(tS + c * 32, r[c]);
+        tmem_ld_wait();
 
-      int lim = kv_len - j * kBN;
-      if (causal) lim = min(lim, grow - j * kBN + 1);
-      const bool full = lim >= kBN;
-      if (!full) {
+        int lim = kv_len - j * kBN;
+        if (causal) lim = min(lim, grow - j * kBN + 1);
+        const bool full = lim >= kBN;
+        if (!full) {
 #pragma unroll
-        for (int c = 0; c < 4; ++c)
+          for (int c = 0; c < 4; ++c)
 #pragma unroll
-          for (int e = 0; e < 32; ++e)
-            if (c * 32 + e >= lim) r[c][e] = __float_as_uint(-INFINITY);
-      }
+            for (int e = 0; e < 32; ++e)
+              if (c * 32 + e >= lim) r[c][e] = __float_as_uint(-INFINITY);
+        }
 #define SV(e) __uint_as_float(r[(e) >> 5][(e) & 31])
-      // Row max: 8 independent 3-input-max chains, then a small tree.
-      float acc[8];
+        // Row max: 8 independent 3-input-max chains, then a small tree.
+        float acc[8];
 #pragma unroll
-      for (int k = 0; k < 8; ++k) acc[k] = fmaxf(SV(2 * k), SV(2 * k + 1));
+        for (int k = 0; k < 8; ++k) acc[k] = fmaxf(SV(2 * k), SV(2 * k + 1));
 #pragma unroll
-      for (int e = 16; e < 128; e += 16)
+        for (int e = 16; e < 128; e += 16)
 #pragma unroll
-        for (int k = 0; k < 8; ++k) acc[k] = max3f(acc[k], SV(e + 2 * k), SV(e + 2 * k + 1));
-      const float mx = max3f(max3f(acc[0], acc[1], acc[2]), max3f(acc[3], acc[4], acc[5]),
-                             fmaxf(acc[6], acc[7]));
-      const float m_tile = mx * sl2;
-      float m_use = m, alpha = 1.f;
-      if (m == -INFINITY) {
-        m_use = m_tile;
-        alpha = 0.f;
-      } else if (m_tile > m + kRescaleThreshold) {
-        m_use = m_tile;
-        alpha = ex2_approx(m - m_tile);
-      }
-      const float neg_base = (m_use == -INFINITY) ? 0.f : -m_use;
-      const uint64_t scale2 = f2pack(sl2, sl2), base2 = f2pack(neg_base, neg_base);
-      uint64_t sum2[4];
+          for (int k = 0; k < 8; ++k) acc[k] = max3f(acc[k], SV(e + 2 * k), SV(e + 2 * k + 1));
+        const float mx = max3f(max3f(acc[0], acc[1], acc[2]), max3f(acc[3], acc[4], acc[5]),
+                               fmaxf(acc[6], acc[7]));
+        const float m_tile = mx * sl2;
+        float m_use = m, alpha = 1.f;
+        if (m == -INFINITY) {
+          m_use = m_tile;
+          alpha = 0.f;
+        } else if (m_tile > m + kRescaleThreshold) {
+          m_use = m_tile;
+          alpha = ex2_approx(m - m_tile);
+        }
+        const float neg_base = (m_use == -INFINITY) ? 0.f : -m_use;
+        const uint64_t scale2 = f2pack(sl2, sl2), base2 = f2pack(neg_base, neg_base);
+        uint64_t sum2[4];
 #pragma unroll
-      for (int k = 0; k < 4; ++k) sum2[k] = 0ull;
-      uint32_t pk[2][32];
-      // P = 2^(s*scale*log2e - m): pairs of columns through the packed FMA pipe; in full
-      // tiles kPolyPer8 of every 8 pairs take the polynomial exp2, the rest MUFU ex2.
-      if (full) {
+        for (int k = 0; k < 4; ++k) sum2[k] = 0ull;
+        // P = 2^(s*scale*log2e - m): pairs of columns through the packed FMA pipe; in full
+        // tiles kPolyPer8 of every 8 pairs take the polynomial exp2, the rest MUFU ex2.
+        uint32_t pk[2][32];
+        if (full) {
 #pragma unroll
-        for (int pr = 0; pr < 64; ++pr) {
-          float x0, x1;
-          f2unpack(fma2(f2pack(SV(2 * pr), SV(2 * pr + 1)), scale2, base2), x0, x1);
-          if ((pr & 7) < kPolyPer8) {
-            exp2_poly_pair(x0, x1);
-          } else {
+          for (int pr = 0; pr < 64; ++pr) {
+            float x0, x1;
+            f2unpack(fma2(f2pack(SV(2 * pr), SV(2 * pr + 1)), scale2, base2), x0, x1);
+            if ((pr & 7) < kPolyPer8) {
+              exp2_poly_pair(x0, x1);
+            } else {
+              x0 = ex2_approx(x0);
+              x1 = ex2_approx(x1);
+            }
+            sum2[pr & 3] = add2(sum2[pr & 3], f2pack(x0, x1));
+            pk[pr >> 5][pr & 31] = pack2<kOp>(x0, x1);
+          }
+        } else {
+#pragma unroll
+          for (int pr = 0; pr < 64; ++pr) {
+            float x0, x1;
+            f2unpack(fma2(f2pack(SV(2 * pr), SV(2 * pr + 1)), scale2, base2), x0, x1);
             x0 = ex2_approx(x0);
             x1 = ex2_approx(x1);
+            sum2[pr & 3] = add2(sum2[pr & 3], f2pack(x0, x1));
+            pk[pr >> 5][pr & 31] = pack2<kOp>(x0, x1);
           }
-          sum2[pr & 3] = add2(sum2[pr & 3], f2pack(x0, x1));
-          pk[pr >> 5][pr & 31] = pack2<kOp>(x0, x1);
+        }
+        tmem_st32(tS, pk[0]);
+        tmem_st32(tS + 32, pk[1]);
+#undef SV
+        float sa, sb;
+        f2unpack(add2(add2(sum2[0], sum2[1]), add2(sum2[2], sum2[3])), sa, sb);
+        const float sum = sa + sb;
+        l = l * alpha + sum;
+        if (__any_sync(0xffffffffu, jj > 0 && alpha != 1.f)) {
+#pragma unroll 1
+          for (int c = 0; c < 4; ++c) {
+            uint32_t o[32];
+            tmem_ld32(tO + c * 32, o);
+            tmem_ld_wait();
+#pragma unroll
+            for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
+            tmem_st32(tO + c * 32, o);
+          }
+        }
+        tmem_st_wait();
+        tc_fence_before();
+        mbar_arrive(&sm.p_full[i]);
+        m = m_use;
+      }
+      if (!ok) break;
+      if (n > 0) {
+        const bool got = mbar_wait(&sm.o_full[i], (uint32_t)a & 1u, abort, p.status,
+                                   ANIMA_ERR_TIMEOUT);
+        if (!(ok = __all_sync(0xffffffffu, got))) break;
+        tc_fence_after();
+      }
+      if (sg.full) {
+        const float inv = (l > 0.f) ? 1.f / l : 0.f;
+        char* out_row = reinterpret_cast<char*>(p.out) +
+                        ((long long)b * p.ob + (long long)(bh % p.H) * p.oh +
+                         (long long)grow * p.os) *
+                            (kOut == ANIMA_DTYPE_F32 ? 4 : 2);
+#pragma unroll 1
+        for (int c = 0; c < 4; ++c) {
+          uint32_t o[32];
+          if (n > 0) {
+            tmem_ld32(tO + c * 32, o);
+            tmem_ld_wait();
+          } else {
+#pragma unroll
+            for (int e = 0; e < 32; ++e) o[e] = 0u;
+          }
+          if (grow < p.S_q) store_row<kOut>(out_row, o, c, inv);
         }
       } else {
-#pragma unroll
-        for (int pr = 0; pr < 64; ++pr) {
-          float x0, x1;
-          f2unpack(fma2(f2pack(SV(2 * pr), SV(2 * pr + 1)), scale2, base2), x0, x1);
-          x0 = ex2_approx(x0);
-          x1 = ex2_approx(x1);
-          sum2[pr & 3] = add2(sum2[pr & 3], f2pack(x0, x1));
-          pk[pr >> 5][pr & 31] = pack2<kOp>(x0, x1);
-        }
-      }
-#undef SV
-      float sa, sb;
-      f2unpack(add2(add2(sum2[0], sum2[1]), add2(sum2[2], sum2[3])), sa, sb);
-      const float sum = sa + sb;
-      l = l * alpha + sum;
-      tmem_st32(tS, pk[0]);
-      tmem_st32(tS + 32, pk[1]);
-      if (__any_sync(0xffffffffu, j > 0 && alpha != 1.f)) {
+        // partial of a split unit: raw O, the running max it is relative to, and the sum
+        float* part = p.part + ((long long)blockIdx.x * 2 + sg.slot) * kPartFloats;
+        const int r = i * kBM + row;
+        char* prow = reinterpret_cast<char*>(part + (long long)r * kD);
 #pragma unroll 1
         for (int c = 0; c < 4; ++c) {
           uint32_t o[32];
           tmem_ld32(tO + c * 32, o);
           tmem_ld_wait();
-#pragma unroll
-          for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
-          tmem_st32(tO + c * 32, o);
+          store_row<ANIMA_DTYPE_F32>(prow, o, c, 1.f);
         }
+        part[kUnitRows * kD + r] = m;
+        part[kUnitRows * kD + kUnitRows + r] = l;
       }
-      tmem_st_wait();
-      tc_fence_before();
-      mbar_arrive(&sm.p_full[i]);
-      m = m_use;
-    }
-
-    if (ok && n_kv > 0) {
-      const bool got = mbar_wait(&sm.o_full[i], 0, abort, p.status, ANIMA_ERR_TIMEOUT);
-      ok = __all_sync(0xffffffffu, got);
-      tc_fence_after();
-    }
-    if (ok) {
-      const float inv = (l > 0.f) ? 1.f / l : 0.f;
-      const bool live = grow < p.S_q;
-      char* out_row = reinterpret_cast<char*>(p.out) +
-                      ((long long)b * p.ob + (long long)(bh % p.H) * p.oh +
-                       (long long)grow * p.os) *
-                          (kOut == ANIMA_DTYPE_F32 ? 4 : 2);
-#pragma unroll 1
-      for (int c = 0; c < 4; ++c) {
-        uint32_t o[32];
-        if (n_kv > 0) {
-          tmem_ld32(tO + c * 32, o);
-          tmem_ld_wait();
-        } else {
-#pragma unroll
-          for (int e = 0; e < 32; ++e) o[e] = 0u;
-        }
-        if (live) {
-          if (kOut == ANIMA_DTYPE_F32) {
-            float4* dst = reinterpret_cast<float4*>(out_row) + c * 8;
-#pragma unroll
-            for (int e = 0; e < 8; ++e)
-              dst[e] = make_float4(__uint_as_float(o[4 * e]) * inv,
-                                   __uint_as_float(o[4 * e + 1]) * inv,
-                                   __uint_as_float(o[4 * e + 2]) * inv,
-                                   __uint_as_float(o[4 * e + 3]) * inv);
-          } else {
-            uint4* dst = reinterpret_cast<uint4*>(out_row) + c * 4;
-#pragma unroll
-            for (int e = 0; e < 4; ++e)
-              dst[e] = make_uint4(
-                  pack_bf16x2(__uint_as_float(o[8 * e]) * inv, __uint_as_float(o[8 * e + 1]) * inv),
-                  pack_bf16x2(__uint_as_float(o[8 * e + 2]) * inv, __uint_as_float(o[8 * e + 3]) * inv),
-                  pack_bf16x2(__uint_as_float(o[8 * e + 4]) * inv, __uint_as_float(o[8 * e + 5]) * inv),
-                  pack_bf16x2(__uint_as_float(o[8 * e + 6]) * inv, __uint_as_float(o[8 * e + 7]) * inv));
-          }
-        }
+      if (n > 0) {
+        tc_fence_before();
+        mbar_arrive(&sm.o_empty[i]);
+        ++a;
       }
     }
     tc_fence_before();
     __syncthreads();  // pairs with the control warpgroup's teardown barrier
+  }
+}
+
+// Finishes units cut by a stream-K slice boundary.  Block c - 1 looks at boundary c
+// (the first key tile of CTA c's slice); a unit holds at most one boundary because
+// slices are at least one unit long, so its two partials sit in CTA c-1's and CTA c's
+// slots.  out = (w1 O1 + w2 O2) / (w1 l1 + w2 l2), w = 2^(m - max(m1, m2)).
+template <int kOut>
+__global__ void __launch_bounds__(256) attn_combine_kernel(const Params p, int grid) {
+  const int c = blockIdx.x + 1;
+  const int n = p.n_kv;
+  const long long lo_c = (long long)c * p.total / grid;
+  const long long lo_prev = (long long)(c - 1) * p.total / grid;
+  const int u = (int)(lo_c / n);
+  const long long ubeg = (long long)u * n;
+  if (lo_c == ubeg || lo_prev > ubeg) return;
+  const float* part1 = p.part + ((long long)(c - 1) * 2 + (ubeg == lo_prev ? 0 : 1)) * kPartFloats;
+  const float* part2 = p.part + ((long long)c * 2 + 0) * kPartFloats;
+  const int bh = u / p.nqb, b = bh / p.H, h = bh % p.H;
+  const int q0 = (u % p.nqb) * kUnitRows;
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  for (int r = w; r < kUnitRows; r += 8) {
+    const int grow = q0 + r;
+    if (grow >= p.S_q) break;
+    const float m1 = part1[kUnitRows * kD + r], m2 = part2[kUnitRows * kD + r];
+    const float l1 = part1[kUnitRows * kD + kUnitRows + r];
+    const float l2 = part2[kUnitRows * kD + kUnitRows + r];
+    const float mx = fmaxf(m1, m2);
+    const float w1 = exp2f(m1 - mx), w2 = exp2f(m2 - mx);
+    const float den = w1 * l1 + w2 * l2;
+    const float inv = den > 0.f ? 1.f / den : 0.f;
+    const float4 a = reinterpret_cast<const float4*>(part1 + (long long)r * kD)[lane];
+    const float4 bb = reinterpret_cast<const float4*>(part2 + (long long)r * kD)[lane];
+    const float4 o = make_float4((w1 * a.x + w2 * bb.x) * inv, (w1 * a.y + w2 * bb.y) * inv,
+                                 (w1 * a.z + w2 * bb.z) * inv, (w1 * a.w + w2 * bb.w) * inv);
+    char* out_row = reinterpret_cast<char*>(p.out) +
+                    ((long long)b * p.ob + (long long)h * p.oh + (long long)grow * p.os) *
+                        (kOut == ANIMA_DTYPE_F32 ? 4 : 2);
+    if (kOut == ANIMA_DTYPE_F32) {
+      reinterpret_cast<float4*>(out_row)[lane] = o;
+    } else {
+      reinterpret_cast<uint2*>(out_row)[lane] = make_uint2(pack_bf16x2(o.x, o.y), pack_bf16x2(o.z, o.w));
+    }
   }
 }
 
@@ -475,26 +657,44 @@ static int make_head_map(CUtensorMap* map, const void* base, int op_dtype, int b
 
 template <int kOp, int kOut>
 static int launch_t(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv,
-                    const attn::Params& prm, dim3 grid, cudaStream_t st) {
+                    const attn::Params& prm, int grid, cudaStream_t st) {
   auto kern = attn::attn_fwd_kernel<kOp, kOut>;
-  static bool attr_set = false;  // per instantiation
-  if (!attr_set) {
+  static int attr_dev_mask = 0;  // devices on which the smem attribute was raised
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!(attr_dev_mask & (1 << (dev & 31)))) {
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              (int)attn::kSmemBytes) != cudaSuccess)
       return ANIMA_ERR_CUDA;
-    attr_set = true;
+    attr_dev_mask |= 1 << (dev & 31);
   }
   kern<<<grid, attn::kThreads, attn::kSmemBytes, st>>>(mq, mk, mv, prm);
-  return cudaGetLastError() == cudaSuccess ? ANIMA_OK : ANIMA_ERR_CUDA;
+  if (cudaGetLastError() != cudaSuccess) return ANIMA_ERR_CUDA;
+  if (prm.split) {
+    attn::attn_combine_kernel<kOut><<<grid - 1, 256, 0, st>>>(prm, grid);
+    if (cudaGetLastError() != cudaSuccess) return ANIMA_ERR_CUDA;
+  }
+  return ANIMA_OK;
 }
 
-int attn_fwd_launch(const AnimaAttnArgs* a, int* status, cudaStream_t st) {
+// Stream-K pays off only past one full wave of units, and needs uniform key tiles.
+static bool use_split(int bh, int S_q, unsigned flags, int sm_count) {
+  if (flags & (ANIMA_FLAG_MASK | ANIMA_FLAG_CAUSAL)) return false;
+  const long long units = (long long)bh * ((S_q + attn::kUnitRows - 1) / attn::kUnitRows);
+  return units > sm_count && sm_count > 1;
+}
+
+size_t attn_workspace_bytes(int B, int H, int S_q, unsigned flags, int sm_count) {
+  if (!use_split(B * H, S_q, flags, sm_count)) return 0;
+  return (size_t)sm_count * 2 * attn::kPartFloats * sizeof(float);
+}
+
+int attn_fwd_launch(const AnimaAttnArgs* a, int* status, int sm_count, cudaStream_t st) {
   if (a->D != attn::kD) return ANIMA_ERR_SHAPE;
   if (a->op_dtype != ANIMA_DTYPE_BF16 && a->op_dtype != ANIMA_DTYPE_F16) return ANIMA_ERR_ARG;
   if (a->out_dtype != ANIMA_DTYPE_F32 && a->out_dtype != ANIMA_DTYPE_BF16) return ANIMA_ERR_ARG;
   const int bh = a->B * a->H;
-  if (bh <= 0 || a->S_q <= 0 || a->S_kv <= 0) return ANIMA_ERR_SHAPE;
-  if (bh > 65535) return ANIMA_ERR_SHAPE;
+  if (a->B <= 0 || a->H <= 0 || a->S_q <= 0 || a->S_kv <= 0) return ANIMA_ERR_SHAPE;
   CUtensorMap mq, mk, mv;
   int rc;
   if ((rc = make_head_map(&mq, a->q, a->op_dtype, bh, a->S_q))) return rc;
@@ -513,7 +713,18 @@ int attn_fwd_launch(const AnimaAttnArgs* a, int* status, cudaStream_t st) {
   prm.oh = a->out_stride[1];
   prm.os = a->out_stride[2];
   prm.status = status;
-  dim3 grid((a->S_q + attn::kBM * attn::kNT - 1) / (attn::kBM * attn::kNT), bh);
+  prm.nqb = (a->S_q + attn::kUnitRows - 1) / attn::kUnitRows;
+  prm.n_kv = (a->S_kv + attn::kBN - 1) / attn::kBN;
+  const long long units = (long long)bh * prm.nqb;
+  if (units > 0x7fffffffLL) return ANIMA_ERR_SHAPE;
+  const size_t need = attn_workspace_bytes(a->B, a->H, a->S_q, a->flags, sm_count);
+  prm.split = (need > 0 && a->workspace && a->workspace_bytes >= need &&
+               (reinterpret_cast<uintptr_t>(a->workspace) & 15u) == 0)
+                  ? 1
+                  : 0;
+  prm.total = units * prm.n_kv;
+  prm.part = static_cast<float*>(a->workspace);
+  const int grid = prm.split ? sm_count : (int)units;
   const bool bf = a->op_dtype == ANIMA_DTYPE_BF16;
   const bool of32 = a->out_dtype == ANIMA_DTYPE_F32;
   if (bf && of32) return launch_t<ANIMA_DTYPE_BF16, ANIMA_DTYPE_F32>(mq, mk, mv, prm, grid, st);

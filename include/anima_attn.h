@@ -85,6 +85,12 @@ typedef struct AnimaPrologueArgs {
  *   [B, S_q, H, D] (feeds the o-proj):     {S_q*H*D, D, H*D}
  * kv_valid_len: device int32 [B], used with ANIMA_FLAG_MASK (keys >= valid are masked;
  * a sample with 0 valid keys gets a zero output).
+ * workspace: optional device scratch of workspace_bytes (16-byte aligned).  When it
+ * holds anima_attn_workspace_size() bytes and the call spans more than one wave of
+ * 256-row units, the kernel runs a persistent stream-K schedule (one CTA per SM, equal
+ * slices of key tiles) and a combine kernel finishes the units cut between two CTAs;
+ * otherwise it launches one CTA per unit.  Results agree either way to fp32 rounding.
+ * Calls that share a workspace must be ordered on one stream.
  */
 typedef struct AnimaAttnArgs {
   const void* q;
@@ -98,6 +104,8 @@ typedef struct AnimaAttnArgs {
   float scale;
   unsigned flags;
   const int* kv_valid_len;
+  void* workspace;
+  uint64_t workspace_bytes;
 } AnimaAttnArgs;
 
 /* Replaces the norm/RoPE/transpose steps listed above (numpy_dit.py:285-291). */
@@ -106,6 +114,10 @@ int anima_attn_prologue(const AnimaPrologueArgs* args, void* stream);
 /* Replaces anima::cpu::flash_attention (anima_rt/include/cpu/flash_attention.h:55-208)
  * for device-resident operands. */
 int anima_attn_fwd(const AnimaAttnArgs* args, void* stream);
+
+/* Workspace bytes anima_attn_fwd can use for this shape on the current device
+ * (0 when the one-CTA-per-unit schedule is used anyway). */
+uint64_t anima_attn_workspace_size(int B, int H, int S_q, int S_kv, unsigned flags);
 
 /* Device status word of the current device: 0, or the first ANIMA_ERR_* a kernel
  * recorded.  Synchronises `stream`; clears the word when reset != 0. */
