@@ -104,13 +104,14 @@ _WORKSPACES: dict = {}
 
 
 def _workspace(device: torch.device, nbytes: int) -> Optional[torch.Tensor]:
-    """Grow-only scratch per (device, stream) for the stream-K schedule's partials."""
+    """Grow-only, zero-filled scratch per (device, stream) for the split schedule.  The
+    kernel leaves its arrival counters at zero, so the buffer is reused as is."""
     if nbytes == 0:
         return None
     key = (device.index, torch.cuda.current_stream(device).cuda_stream)
     ws = _WORKSPACES.get(key)
     if ws is None or ws.numel() < nbytes:
-        ws = torch.empty(nbytes, dtype=torch.uint8, device=device)
+        ws = torch.zeros(nbytes, dtype=torch.uint8, device=device)
         _WORKSPACES[key] = ws
     return ws
 
@@ -125,7 +126,7 @@ def attention_core(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, B: int, H:
     q [B*H, S_q, 128], k/v [B*H, S_kv, 128] contiguous bf16/fp16.  Returns (or fills)
     ``out`` in ``out_layout`` "bshd" [B, S_q, H, D] or "bhsd" [B, H, S_q, D].
     ``kv_valid_len`` int32 [B] masks keys >= kv_valid_len[b] (cross-attention padding).
-    ``stream_k`` lets calls of more than one wave use the persistent stream-K schedule
+    ``stream_k`` lets calls of more than one wave use the persistent split schedule
     (with a cached workspace); False forces one CTA per 256-row unit.
     """
     _check_cuda(q, k, v)
@@ -216,8 +217,13 @@ def sdpa(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, scale: Optional[floa
 
 
 def status(reset: bool = True) -> int:
-    """Synchronise the current stream and return the device status word (0 = clean)."""
-    return L.lib.anima_attn_status(ct.c_void_p(_stream()), int(reset))
+    """Synchronise the current stream and return the device status word (0 = clean).
+    A non-zero status drops the cached workspaces (an aborted kernel may have left
+    arrival counters non-zero)."""
+    rc = L.lib.anima_attn_status(ct.c_void_p(_stream()), int(reset))
+    if rc != 0:
+        _WORKSPACES.clear()
+    return rc
 
 
 def device_info():

@@ -16,7 +16,7 @@
 
 namespace anima {
 int attn_fwd_launch(const AnimaAttnArgs* a, int* status, int sm_count, cudaStream_t st);
-size_t attn_workspace_bytes(int B, int H, int S_q, unsigned flags, int sm_count);
+size_t attn_workspace_bytes(int B, int H, int S_q, int S_kv, unsigned flags, int sm_count);
 int prologue_launch(const AnimaPrologueArgs* a, int sm_count, cudaStream_t st);
 int rmsnorm_launch(const float* x, const float* w, float* y, long long m, int d, float eps,
                    int sm_count, cudaStream_t st);
@@ -195,9 +195,14 @@ bool rt_attention(const float* q, const float* k, const float* v, const float* q
   int drc = ANIMA_OK;
   DeviceState* dev = current_device(&drc);
   if (!dev) return false;
-  const size_t ws_split = attn_workspace_bytes(B, H, S_q, aflags, dev->sm_count);
+  const size_t ws_split = attn_workspace_bytes(B, H, S_q, S_kv, aflags, dev->sm_count);
   const size_t o_split = carve(ws_split);
   if (!rt_prepare(off)) return false;
+  // The split schedule's arrival counters (first 4 KiB of its workspace) must start at
+  // zero; this workspace is shared with other data, so clear them on every call.
+  if (ws_split && !rt_check(cudaMemsetAsync(static_cast<char*>(g_rt.ws) + o_split, 0, 4096,
+                                            g_rt.stream), who))
+    return false;
   char* ws = static_cast<char*>(g_rt.ws);
   cudaStream_t st = g_rt.stream;
   float *dq = (float*)(ws + o_q), *dk = (float*)(ws + o_k), *dv = (float*)(ws + o_v);
@@ -307,11 +312,10 @@ int anima_attn_fwd(const AnimaAttnArgs* a, void* stream) {
 }
 
 uint64_t anima_attn_workspace_size(int B, int H, int S_q, int S_kv, unsigned flags) {
-  (void)S_kv;
   int rc = ANIMA_OK;
   DeviceState* d = current_device(&rc);
-  if (!d || B <= 0 || H <= 0 || S_q <= 0) return 0;
-  return attn_workspace_bytes(B, H, S_q, flags, d->sm_count);
+  if (!d || B <= 0 || H <= 0 || S_q <= 0 || S_kv <= 0) return 0;
+  return attn_workspace_bytes(B, H, S_q, S_kv, flags, d->sm_count);
 }
 
 int anima_attn_status(void* stream, int reset) {
@@ -342,7 +346,8 @@ int anima_attn_device_info(int* sm_count, int* cc) {
 
 const char* anima_attn_version(void) {
   return "anima_attn sm_100a: tcgen05 flash fwd (2x128-row Q tiles per unit, 128-key tiles, "
-         "4-slot K/V ring, TMEM S/P/O, stream-K persistent schedule), fused RMSNorm+RoPE "
+         "4-slot K/V ring, TMEM S/P/O, persistent split schedule for the last round), fused "
+         "RMSNorm+RoPE "
          "prologue";
 }
 

@@ -6,11 +6,15 @@
 //
 // Work unit = 256 query rows (two 128-row tiles) of one (batch, head) against its keys,
 // streamed in 128-key tiles.  Two schedules share one kernel:
-//   unit mode      one CTA per unit (masked / causal calls, or at most one wave);
-//   stream-K mode  a persistent grid of one CTA per SM takes an equal slice of the
-//                  (unit x key-tile) sequence, so the last wave is not partly idle.  A
-//                  unit cut by a slice boundary is finished by attn_combine_kernel from
-//                  the two fp32 partials (O, running max, running sum) its CTAs wrote.
+//   unit mode    one CTA per unit (masked / causal calls, or at most one wave);
+//   split mode   a persistent grid of one CTA per SM.  Whole units are dealt round-robin
+//                (CTA c takes units c, c+G, ...), so the CTAs in flight share heads and
+//                their K/V stay in L2; the units of the last, partial round are cut into
+//                equal slices of key tiles spread over all CTAs, so that round is not
+//                left half idle.  A CTA holding a slice writes an fp32 partial (O, running
+//                max, running sum); the last warpgroup to finish a cut unit, told by an
+//                arrival counter, merges the partials and writes the output.  No CTA waits
+//                on another.
 //
 // Warp roles (384 threads, 3 warpgroups):
 //   warps 0-7  two softmax warpgroups, one per query tile; thread = query row = TMEM
@@ -64,6 +68,8 @@ constexpr float kRescaleThreshold = 8.0f;  // log2 units
 constexpr int kPolyPer8 = ANIMA_POLY_PER8;
 // One partial of a split unit: O [256][128] fp32 (unnormalised), then m [256], l [256].
 constexpr int kPartFloats = kUnitRows * kD + 2 * kUnitRows;
+constexpr int kMinSliceTiles = 4;       // shortest key-tile slice of the last round
+constexpr int kSemBytes = 4096;         // arrival counters at the start of the workspace
 
 struct Smem {
   uint8_t q[kNT][kTile];
@@ -78,6 +84,7 @@ struct Smem {
   uint64_t mma_done;
   uint32_t tmem_base;
   int abort;
+  int last[kNT];  // warpgroup i merges the cut unit it just finished
 };
 
 constexpr size_t kSmemBytes = sizeof(Smem) + 1024;  // + slack to align the base to 1 KB
@@ -92,11 +99,24 @@ struct Params {
   long long ob, oh, os;
   int* status;
   int nqb;             // query units per (batch, head)
-  int split;           // 1: stream-K over uniform key tiles
-  int n_kv;            // key tiles per unit (stream-K mode)
-  long long total;     // units * n_kv (stream-K mode)
-  float* part;         // stream-K partial slots [gridDim.x][2][kPartFloats]
+  int split;           // 1: split mode (persistent, last round cut into slices)
+  int n_kv;            // key tiles per unit (split mode)
+  int rounds;          // whole-unit rounds: CTA c owns units c + r * gridDim.x
+  int tail_base;       // first unit of the cut last round (rounds * gridDim.x)
+  int tail_tiles;      // key-tile steps of the last round
+  int tail_ctas;       // CTAs sharing the last round (<= gridDim.x)
+  int* sem;            // arrival counters [tail unit][tile], zero between calls
+  float* part;         // partial slots [tail_ctas][2][kPartFloats]
 };
+
+// Slice of the last round owned by CTA c: key-tile steps [slice_lo(c), slice_lo(c+1)).
+__device__ __forceinline__ int slice_lo(const Params& p, int c) {
+  return (int)((long long)c * p.tail_tiles / p.tail_ctas);
+}
+// The CTA whose slice holds key-tile step t of the last round.
+__device__ __forceinline__ int slice_of(const Params& p, int t) {
+  return (int)((((long long)t + 1) * p.tail_ctas + p.tail_tiles - 1) / p.tail_tiles) - 1;
+}
 
 // One piece of work of a CTA: key tiles [k0, k1) of unit `unit`.
 struct Seg {
@@ -125,20 +145,23 @@ __device__ __forceinline__ int unit_tiles(const Params& p, int unit) {
 
 // Segment iterator: every role walks the same sequence.
 struct SegIter {
-  long long t, lo, hi;
-  __device__ __forceinline__ SegIter(const Params& p) {
-    if (p.split) {
-      lo = (long long)blockIdx.x * p.total / gridDim.x;
-      hi = (long long)(blockIdx.x + 1) * p.total / gridDim.x;
-    } else {
+  int r;          // whole-unit rounds handed out so far
+  int t, lo, hi;  // this CTA's slice of the last round (key-tile steps)
+  __device__ __forceinline__ SegIter(const Params& p) : r(0) {
+    if (!p.split) {
       lo = 0;
       hi = 1;
+    } else if ((int)blockIdx.x < p.tail_ctas) {
+      lo = slice_lo(p, blockIdx.x);
+      hi = slice_lo(p, blockIdx.x + 1);
+    } else {
+      lo = hi = 0;
     }
     t = lo;
   }
   __device__ __forceinline__ bool next(const Params& p, Seg& s) {
-    if (t >= hi) return false;
     if (!p.split) {
+      if (t >= hi) return false;
       s.unit = blockIdx.x;
       s.k0 = 0;
       s.k1 = unit_tiles(p, s.unit);
@@ -148,10 +171,21 @@ struct SegIter {
       return true;
     }
     const int n = p.n_kv;
-    s.unit = (int)(t / n);
-    const long long ubeg = (long long)s.unit * n, uend = ubeg + n;
-    s.k0 = (int)(t - ubeg);
-    s.k1 = (int)(min(uend, hi) - ubeg);
+    if (r < p.rounds) {
+      s.unit = blockIdx.x + r * gridDim.x;
+      s.k0 = 0;
+      s.k1 = n;
+      s.full = 1;
+      s.slot = 0;
+      ++r;
+      return true;
+    }
+    if (t >= hi) return false;
+    const int ut = t / n;
+    const int ubeg = ut * n, uend = ubeg + n;
+    s.unit = p.tail_base + ut;
+    s.k0 = t - ubeg;
+    s.k1 = min(uend, hi) - ubeg;
     s.full = (s.k0 == 0 && s.k1 == n);
     s.slot = (t == lo) ? 0 : 1;
     t = min(uend, hi);
@@ -167,6 +201,11 @@ __device__ __forceinline__ void drain_wait(uint64_t* bar, uint32_t parity) {
   while (!mbar_try_wait(bar, parity)) {
     if (globaltimer_ns() - t0 > kWaitLimitNs) return;
   }
+}
+
+// Barrier over the 128 threads of one softmax warpgroup (ids 1, 2; 0 is __syncthreads).
+__device__ __forceinline__ void wg_sync(int id) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(kBM) : "memory");
 }
 
 template <int kOp>
@@ -549,9 +588,13 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (grow < p.S_q) store_row<kOut>(out_row, o, c, inv);
         }
       } else {
-        // partial of a split unit: raw O, the running max it is relative to, and the sum
-        float* part = p.part + ((long long)blockIdx.x * 2 + sg.slot) * kPartFloats;
+        // A slice of a cut unit: write the raw O row, the running max it is relative to,
+        // and the running sum; then count this tile's arrival.  The warpgroup that
+        // completes the count merges every slice of the tile:
+        //   out = sum_s 2^(m_s - M) O_s / sum_s 2^(m_s - M) l_s,  M = max_s m_s.
+        const int ut = sg.unit - p.tail_base;
         const int r = i * kBM + row;
+        float* part = p.part + ((long long)blockIdx.x * 2 + sg.slot) * kPartFloats;
         char* prow = reinterpret_cast<char*>(part + (long long)r * kD);
 #pragma unroll 1
         for (int c = 0; c < 4; ++c) {
@@ -562,6 +605,60 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         part[kUnitRows * kD + r] = m;
         part[kUnitRows * kD + kUnitRows + r] = l;
+        const int t0 = ut * p.n_kv, t1 = t0 + p.n_kv;
+        const int c0 = slice_of(p, t0), c1 = slice_of(p, t1 - 1);
+        __threadfence();
+        wg_sync(1 + i);
+        if (row == 0) {
+          const int prev = atomicAdd(&p.sem[ut * kNT + i], 1);
+          sm.last[i] = (prev == c1 - c0) ? 1 : 0;
+        }
+        wg_sync(1 + i);
+        if (sm.last[i]) {
+          __threadfence();
+          float mx = -INFINITY;
+          for (int c = c0; c <= c1; ++c) {
+            const int lo_c = slice_lo(p, c);
+            const float* pc = p.part + ((long long)c * 2 + (max(t0, lo_c) == lo_c ? 0 : 1)) * kPartFloats;
+            mx = fmaxf(mx, __ldcg(pc + kUnitRows * kD + r));
+          }
+          float den = 0.f;
+          for (int c = c0; c <= c1; ++c) {
+            const int lo_c = slice_lo(p, c);
+            const float* pc = p.part + ((long long)c * 2 + (max(t0, lo_c) == lo_c ? 0 : 1)) * kPartFloats;
+            den += exp2f(__ldcg(pc + kUnitRows * kD + r) - mx) * __ldcg(pc + kUnitRows * kD + kUnitRows + r);
+          }
+          const float inv = den > 0.f ? 1.f / den : 0.f;
+          char* out_row = reinterpret_cast<char*>(p.out) +
+                          ((long long)b * p.ob + (long long)(bh % p.H) * p.oh +
+                           (long long)grow * p.os) *
+                              (kOut == ANIMA_DTYPE_F32 ? 4 : 2);
+#pragma unroll 1
+          for (int ch = 0; ch < 4; ++ch) {
+            float acc[32];
+#pragma unroll
+            for (int e = 0; e < 32; ++e) acc[e] = 0.f;
+            for (int c = c0; c <= c1; ++c) {
+              const int lo_c = slice_lo(p, c);
+              const float* pc = p.part + ((long long)c * 2 + (max(t0, lo_c) == lo_c ? 0 : 1)) * kPartFloats;
+              const float w = exp2f(__ldcg(pc + kUnitRows * kD + r) - mx);
+              const float4* src = reinterpret_cast<const float4*>(pc + (long long)r * kD + ch * 32);
+#pragma unroll
+              for (int e = 0; e < 8; ++e) {
+                const float4 v4 = __ldcg(src + e);
+                acc[4 * e] += w * v4.x;
+                acc[4 * e + 1] += w * v4.y;
+                acc[4 * e + 2] += w * v4.z;
+                acc[4 * e + 3] += w * v4.w;
+              }
+            }
+            uint32_t o[32];
+#pragma unroll
+            for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(acc[e]);
+            if (grow < p.S_q) store_row<kOut>(out_row, o, ch, inv);
+          }
+          if (row == 0) p.sem[ut * kNT + i] = 0;  // leave the counter zero for the next call
+        }
       }
       if (n > 0) {
         tc_fence_before();
@@ -571,49 +668,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     tc_fence_before();
     __syncthreads();  // pairs with the control warpgroup's teardown barrier
-  }
-}
-
-// Finishes units cut by a stream-K slice boundary.  Block c - 1 looks at boundary c
-// (the first key tile of CTA c's slice); a unit holds at most one boundary because
-// slices are at least one unit long, so its two partials sit in CTA c-1's and CTA c's
-// slots.  out = (w1 O1 + w2 O2) / (w1 l1 + w2 l2), w = 2^(m - max(m1, m2)).
-template <int kOut>
-__global__ void __launch_bounds__(256) attn_combine_kernel(const Params p, int grid) {
-  const int c = blockIdx.x + 1;
-  const int n = p.n_kv;
-  const long long lo_c = (long long)c * p.total / grid;
-  const long long lo_prev = (long long)(c - 1) * p.total / grid;
-  const int u = (int)(lo_c / n);
-  const long long ubeg = (long long)u * n;
-  if (lo_c == ubeg || lo_prev > ubeg) return;
-  const float* part1 = p.part + ((long long)(c - 1) * 2 + (ubeg == lo_prev ? 0 : 1)) * kPartFloats;
-  const float* part2 = p.part + ((long long)c * 2 + 0) * kPartFloats;
-  const int bh = u / p.nqb, b = bh / p.H, h = bh % p.H;
-  const int q0 = (u % p.nqb) * kUnitRows;
-  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
-  for (int r = w; r < kUnitRows; r += 8) {
-    const int grow = q0 + r;
-    if (grow >= p.S_q) break;
-    const float m1 = part1[kUnitRows * kD + r], m2 = part2[kUnitRows * kD + r];
-    const float l1 = part1[kUnitRows * kD + kUnitRows + r];
-    const float l2 = part2[kUnitRows * kD + kUnitRows + r];
-    const float mx = fmaxf(m1, m2);
-    const float w1 = exp2f(m1 - mx), w2 = exp2f(m2 - mx);
-    const float den = w1 * l1 + w2 * l2;
-    const float inv = den > 0.f ? 1.f / den : 0.f;
-    const float4 a = reinterpret_cast<const float4*>(part1 + (long long)r * kD)[lane];
-    const float4 bb = reinterpret_cast<const float4*>(part2 + (long long)r * kD)[lane];
-    const float4 o = make_float4((w1 * a.x + w2 * bb.x) * inv, (w1 * a.y + w2 * bb.y) * inv,
-                                 (w1 * a.z + w2 * bb.z) * inv, (w1 * a.w + w2 * bb.w) * inv);
-    char* out_row = reinterpret_cast<char*>(p.out) +
-                    ((long long)b * p.ob + (long long)h * p.oh + (long long)grow * p.os) *
-                        (kOut == ANIMA_DTYPE_F32 ? 4 : 2);
-    if (kOut == ANIMA_DTYPE_F32) {
-      reinterpret_cast<float4*>(out_row)[lane] = o;
-    } else {
-      reinterpret_cast<uint2*>(out_row)[lane] = make_uint2(pack_bf16x2(o.x, o.y), pack_bf16x2(o.z, o.w));
-    }
   }
 }
 
@@ -669,24 +723,37 @@ static int launch_t(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensor
     attr_dev_mask |= 1 << (dev & 31);
   }
   kern<<<grid, attn::kThreads, attn::kSmemBytes, st>>>(mq, mk, mv, prm);
-  if (cudaGetLastError() != cudaSuccess) return ANIMA_ERR_CUDA;
-  if (prm.split) {
-    attn::attn_combine_kernel<kOut><<<grid - 1, 256, 0, st>>>(prm, grid);
-    if (cudaGetLastError() != cudaSuccess) return ANIMA_ERR_CUDA;
-  }
-  return ANIMA_OK;
+  return cudaGetLastError() == cudaSuccess ? ANIMA_OK : ANIMA_ERR_CUDA;
 }
 
-// Stream-K pays off only past one full wave of units, and needs uniform key tiles.
-static bool use_split(int bh, int S_q, unsigned flags, int sm_count) {
-  if (flags & (ANIMA_FLAG_MASK | ANIMA_FLAG_CAUSAL)) return false;
+// Split-mode plan for a call: whole-unit rounds plus the last round cut into slices.
+struct SplitPlan {
+  int rounds, tail_units, tail_tiles, tail_ctas;
+  size_t bytes;  // workspace: counters + partial slots (0: use unit mode)
+};
+
+static SplitPlan plan_split(int bh, int S_q, int S_kv, unsigned flags, int sm_count) {
+  SplitPlan sp = {0, 0, 0, 0, 0};
+  if (flags & (ANIMA_FLAG_MASK | ANIMA_FLAG_CAUSAL) || sm_count < 2) return sp;
   const long long units = (long long)bh * ((S_q + attn::kUnitRows - 1) / attn::kUnitRows);
-  return units > sm_count && sm_count > 1;
+  const long long n = (S_kv + attn::kBN - 1) / attn::kBN;
+  if (units <= sm_count || units > 0x7fffffffLL) return sp;  // one wave: nothing to balance
+  const long long rounds = units / sm_count, tail = units - rounds * sm_count;
+  if (tail == 0 || tail * n > 0x7fffffffLL) return sp;         // whole rounds only
+  sp.rounds = (int)rounds;
+  sp.tail_units = (int)tail;
+  sp.tail_tiles = (int)(tail * n);
+  long long ctas = sp.tail_tiles / attn::kMinSliceTiles;
+  if (ctas > sm_count) ctas = sm_count;
+  if (ctas < 1) ctas = 1;
+  sp.tail_ctas = (int)ctas;
+  if (2LL * tail * (long long)sizeof(int) > attn::kSemBytes) return SplitPlan{0, 0, 0, 0, 0};
+  sp.bytes = attn::kSemBytes + (size_t)ctas * 2 * attn::kPartFloats * sizeof(float);
+  return sp;
 }
 
-size_t attn_workspace_bytes(int B, int H, int S_q, unsigned flags, int sm_count) {
-  if (!use_split(B * H, S_q, flags, sm_count)) return 0;
-  return (size_t)sm_count * 2 * attn::kPartFloats * sizeof(float);
+size_t attn_workspace_bytes(int B, int H, int S_q, int S_kv, unsigned flags, int sm_count) {
+  return plan_split(B * H, S_q, S_kv, flags, sm_count).bytes;
 }
 
 int attn_fwd_launch(const AnimaAttnArgs* a, int* status, int sm_count, cudaStream_t st) {
@@ -717,13 +784,17 @@ int attn_fwd_launch(const AnimaAttnArgs* a, int* status, int sm_count, cudaStrea
   prm.n_kv = (a->S_kv + attn::kBN - 1) / attn::kBN;
   const long long units = (long long)bh * prm.nqb;
   if (units > 0x7fffffffLL) return ANIMA_ERR_SHAPE;
-  const size_t need = attn_workspace_bytes(a->B, a->H, a->S_q, a->flags, sm_count);
-  prm.split = (need > 0 && a->workspace && a->workspace_bytes >= need &&
-               (reinterpret_cast<uintptr_t>(a->workspace) & 15u) == 0)
+  const SplitPlan sp = plan_split(bh, a->S_q, a->S_kv, a->flags, sm_count);
+  prm.split = (sp.bytes > 0 && a->workspace && a->workspace_bytes >= sp.bytes &&
+               (reinterpret_cast<uintptr_t>(a->workspace) & 255u) == 0)
                   ? 1
                   : 0;
-  prm.total = units * prm.n_kv;
-  prm.part = static_cast<float*>(a->workspace);
+  prm.rounds = sp.rounds;
+  prm.tail_base = sp.rounds * sm_count;
+  prm.tail_tiles = sp.tail_tiles;
+  prm.tail_ctas = sp.tail_ctas;
+  prm.sem = static_cast<int*>(a->workspace);
+  prm.part = reinterpret_cast<float*>(static_cast<char*>(a->workspace) + attn::kSemBytes);
   const int grid = prm.split ? sm_count : (int)units;
   const bool bf = a->op_dtype == ANIMA_DTYPE_BF16;
   const bool of32 = a->out_dtype == ANIMA_DTYPE_F32;

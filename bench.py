@@ -72,12 +72,17 @@ def load_traffic(L):
 
 # ---------------------------------------------------------------- clocks (NVML)
 class ClockSampler:
+    """NVML sampler of SM clock, power and throttle reasons on a background thread.
+
+    Samples carry host timestamps; summary(t0, t1) reports the samples taken inside the
+    timed region [t0, t1] (or the whole sampling window when the region was too short
+    for three samples, which is then stated)."""
     REASONS = {0x4: "sw_power_cap", 0x8: "hw_slowdown", 0x20: "sw_thermal_slowdown",
                0x40: "hw_thermal_slowdown", 0x80: "hw_power_brake_slowdown",
-               0x2: "applications_clocks_setting", 0x1: "gpu_idle"}
+               0x2: "applications_clocks_setting"}
 
     def __init__(self, index):
-        self.samples, self.reasons, self.ok = [], set(), False
+        self.samples = []  # (t, sm_mhz, power_w, reasons_mask)
         self.max_mhz = None
         try:
             import pynvml
@@ -94,14 +99,14 @@ class ClockSampler:
         nv = self.nv
         while not self._stop.is_set():
             try:
-                self.samples.append(nv.nvmlDeviceGetClockInfo(self.h, nv.NVML_CLOCK_SM))
+                t = time.perf_counter()
+                mhz = nv.nvmlDeviceGetClockInfo(self.h, nv.NVML_CLOCK_SM)
+                pw = nv.nvmlDeviceGetPowerUsage(self.h) / 1000.0
                 r = nv.nvmlDeviceGetCurrentClocksEventReasons(self.h)
-                for bit, name in self.REASONS.items():
-                    if r & bit and bit != 0x1:
-                        self.reasons.add(name)
+                self.samples.append((t, mhz, pw, r))
             except Exception:
                 pass
-            time.sleep(0.002)
+            time.sleep(0.001)
 
     def __enter__(self):
         if self.ok:
@@ -114,12 +119,21 @@ class ClockSampler:
             self._stop.set()
             self.t.join()
 
-    def summary(self):
+    def summary(self, t0=None, t1=None):
         if not self.ok or not self.samples:
-            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": sorted(self.reasons),
-                    "samples": len(self.samples)}
-        return {"sm_mhz": statistics.median(self.samples), "sm_max_mhz": self.max_mhz,
-                "reasons": sorted(self.reasons), "samples": len(self.samples)}
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": [], "samples": 0}
+        inside = [s for s in self.samples if t0 is not None and t0 <= s[0] <= t1]
+        window = "timed region"
+        if len(inside) < 3:
+            inside, window = self.samples, "warm-up + timed region (timed region too short)"
+        reasons = set()
+        for s in inside:
+            for bit, name in self.REASONS.items():
+                if s[3] & bit:
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(s[1] for s in inside), "sm_max_mhz": self.max_mhz,
+                "reasons": sorted(reasons), "samples": len(inside), "window": window,
+                "power_w_median": round(statistics.median(s[2] for s in inside), 1)}
 
 
 # ---------------------------------------------------------------- inputs
@@ -228,7 +242,8 @@ def run_ours(args, rank, world, local_rank):
         qh, kh, vh = anima_attn.prologue(dq, dk, dv, dqw, dkw, freqs, out=ws)
         if evs is not None:
             evs[1].record(stream)
-        anima_attn.attention_core(qh, kh, vh, B, heads, out=out)
+        anima_attn.attention_core(qh, kh, vh, B, heads, out=out,
+                                  stream_k=(args.schedule == "auto"))
         if evs is not None:
             evs[2].record(stream)
 
@@ -241,16 +256,17 @@ def run_ours(args, rank, world, local_rank):
             dist.barrier()
         torch.cuda.synchronize()
 
-    for _ in range(args.warmup):
-        step()
-    barrier()
     evs = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(args.steps)]
     clocks = ClockSampler(local_rank)
     with clocks:
+        for _ in range(args.warmup):
+            step()
         barrier()
+        t_begin = time.perf_counter()
         for i in range(args.steps):
             step(evs[i])
         torch.cuda.synchronize()
+        t_end = time.perf_counter()
         barrier()
     if anima_attn.status() != 0:
         raise SystemExit("device status word reports a kernel timeout")
@@ -318,6 +334,7 @@ def run_ours(args, rank, world, local_rank):
                    "parallelism": f"{args.shard}{world}",
                    "l2": f"inputs {3 * B * L_ * heads * D * 4 / 2**20:.0f} MiB fp32 > 126 MB L2",
                    "attn_ms": round(att_ms, 4), "prologue_ms": round(pro_ms, 4),
+                   "schedule": args.schedule,
                    "prologue_gbs": round(pro_bytes / (pro_ms * 1e-3) / 1e9, 1),
                    "pct_of_dense_bf16_peak": round(100 * value / world / peaks["tflops"], 2)},
         "roofline": {"bound": "tensor", "achieved": round(achieved, 2), "peak": peaks["tflops"],
@@ -330,7 +347,7 @@ def run_ours(args, rank, world, local_rank):
                               "traffic": load_traffic(L_).get("prologue")},
         "e2e": e2e,
         "gpu_launches": 2 * args.steps,
-        "clocks": clocks.summary(),
+        "clocks": clocks.summary(t_begin, t_end),
     }
     return res
 
@@ -344,6 +361,9 @@ def main():
     ap.add_argument("--L", type=int, default=4096)
     ap.add_argument("--shard", choices=["replicas", "heads"], default="replicas")
     ap.add_argument("--seed", type=int, default=0)
+    ap.add_argument("--schedule", choices=["auto", "unit"], default="auto",
+                    help="auto: persistent stream-K when the call spans more than one wave; "
+                         "unit: one CTA per 256-row unit")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()

@@ -85,11 +85,13 @@ typedef struct AnimaPrologueArgs {
  *   [B, S_q, H, D] (feeds the o-proj):     {S_q*H*D, D, H*D}
  * kv_valid_len: device int32 [B], used with ANIMA_FLAG_MASK (keys >= valid are masked;
  * a sample with 0 valid keys gets a zero output).
- * workspace: optional device scratch of workspace_bytes (16-byte aligned).  When it
- * holds anima_attn_workspace_size() bytes and the call spans more than one wave of
- * 256-row units, the kernel runs a persistent stream-K schedule (one CTA per SM, equal
- * slices of key tiles) and a combine kernel finishes the units cut between two CTAs;
- * otherwise it launches one CTA per unit.  Results agree either way to fp32 rounding.
+ * workspace: optional device scratch of workspace_bytes, 256-byte aligned, ZERO-FILLED
+ * before its first use.  When it holds anima_attn_workspace_size() bytes and the call
+ * spans more than one wave of 256-row units, the kernel runs persistently (one CTA per
+ * SM): whole units round-robin, and the last partial round cut into equal slices of
+ * key tiles whose fp32 partials are merged in-kernel; otherwise it launches one CTA per
+ * unit.  The kernel leaves the workspace's counters (its first 4 KiB) at zero, so a
+ * zero-filled workspace can be reused; after an ANIMA_ERR_TIMEOUT, zero it again.
  * Calls that share a workspace must be ordered on one stream.
  */
 typedef struct AnimaAttnArgs {

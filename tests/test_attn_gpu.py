@@ -167,11 +167,13 @@ def test_masked_cross_attention(aa, O):
     _ok(got, ref)
 
 
-@pytest.mark.parametrize("Sq,Skv", [(1300, 700), (4000, 3000), (1280, 128)])
+@pytest.mark.parametrize("Sq,Skv", [(1300, 700), (4000, 3000), (1280, 128), (4096, 4096)])
 def test_stream_k_schedule_matches_unit_schedule_and_oracle(aa, O, Sq, Skv):
     """More than one wave of 256-row units (B*H*ceil(Sq/256) > 148 SMs) runs the
-    persistent stream-K schedule; units cut between two CTAs are finished by the combine
-    kernel.  Ragged Sq/Skv exercise partial query units and partial key tiles."""
+    persistent split schedule: whole units round-robin, the last round cut into key-tile
+    slices merged in-kernel.  Ragged Sq/Skv exercise partial query units and partial key
+    tiles; (1280, 128) has one-tile units (nothing to cut); (4096, 4096) is the bench
+    shape, whose 68 last-round units are each cut across about three CTAs."""
     from anima_attn import _lib as L
     B, H = 2, 16
     rng = np.random.default_rng(Sq + Skv)
