@@ -17,6 +17,8 @@
 namespace anima {
 int attn_fwd_launch(const AnimaAttnArgs* a, int* status, int sm_count, cudaStream_t st);
 size_t attn_workspace_bytes(int B, int H, int S_q, int S_kv, unsigned flags, int sm_count);
+int attn_fwd_launch_noalloc(const AnimaAttnArgs* a, int* status, int sm_count, cudaStream_t st,
+                            const char** why);
 int prologue_launch(const AnimaPrologueArgs* a, int sm_count, cudaStream_t st);
 int rmsnorm_launch(const float* x, const float* w, float* y, long long m, int d, float eps,
                    int sm_count, cudaStream_t st);
@@ -308,6 +310,25 @@ int anima_attn_fwd(const AnimaAttnArgs* a, void* stream) {
   if (!d) return rc;
   rc = attn_fwd_launch(a, d->status, d->sm_count, static_cast<cudaStream_t>(stream));
   if (rc != ANIMA_OK) set_error(std::string("anima_attn_fwd: ") + code_name(rc));
+  return rc;
+}
+
+int anima_attn_fwd_noalloc(const AnimaAttnArgs* a, void* stream) {
+  if (!a || !a->q || !a->k || !a->v || !a->out) return ANIMA_ERR_ARG;
+  if ((a->flags & ANIMA_FLAG_MASK) && !a->kv_valid_len) return ANIMA_ERR_ARG;
+  const int oe = a->out_dtype == ANIMA_DTYPE_F32 ? 4 : 8;
+  for (int i = 0; i < 3; ++i)
+    if (a->out_stride[i] < 0 || a->out_stride[i] % oe) return ANIMA_ERR_ARG;
+  const uintptr_t al = reinterpret_cast<uintptr_t>(a->q) | reinterpret_cast<uintptr_t>(a->k) |
+                       reinterpret_cast<uintptr_t>(a->v) | reinterpret_cast<uintptr_t>(a->out);
+  if (al & 15u) return ANIMA_ERR_ARG;
+  int rc = ANIMA_OK;
+  DeviceState* d = current_device(&rc);
+  if (!d) return rc;
+  const char* why = nullptr;
+  rc = attn_fwd_launch_noalloc(a, d->status, d->sm_count, static_cast<cudaStream_t>(stream), &why);
+  if (rc != ANIMA_OK)
+    set_error(std::string("anima_attn_fwd_noalloc: ") + (why ? why : code_name(rc)));
   return rc;
 }
 

@@ -673,6 +673,19 @@ __global__ void __launch_bounds__(kThreads, 1)
 
 }  // namespace attn
 
+// ---------------------------------------------------------------- no-allocation scratch
+// Scratch of the split schedule for anima_attn_fwd_noalloc, for callers that cannot
+// allocate device memory.  Sized for GPUs with up to kNoAllocMaxCtas SMs: 4 KiB of
+// arrival counters plus two fp32 partial slots per CTA (about 40.6 MB).  Every GPU that
+// loads this library holds it until the process exits.  Zero at module load; each call
+// clears the counters again before its kernel runs.
+namespace attn {
+constexpr int kNoAllocMaxCtas = 160;
+constexpr size_t kNoAllocScratchBytes =
+    kSemBytes + (size_t)kNoAllocMaxCtas * 2 * kPartFloats * sizeof(float);
+}  // namespace attn
+static __device__ __align__(256) unsigned char g_noalloc_scratch[attn::kNoAllocScratchBytes];
+
 // ---------------------------------------------------------------- host launcher
 typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
                                   const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
@@ -802,6 +815,46 @@ int attn_fwd_launch(const AnimaAttnArgs* a, int* status, int sm_count, cudaStrea
   if (bf) return launch_t<ANIMA_DTYPE_BF16, ANIMA_DTYPE_BF16>(mq, mk, mv, prm, grid, st);
   if (of32) return launch_t<ANIMA_DTYPE_F16, ANIMA_DTYPE_F32>(mq, mk, mv, prm, grid, st);
   return launch_t<ANIMA_DTYPE_F16, ANIMA_DTYPE_BF16>(mq, mk, mv, prm, grid, st);
+}
+
+// Same launch as attn_fwd_launch, with the split schedule's scratch taken from
+// g_noalloc_scratch instead of the caller's workspace.  Host code only ever passes
+// the array's device address, looked up once per device with that device current.
+int attn_fwd_launch_noalloc(const AnimaAttnArgs* a, int* status, int sm_count, cudaStream_t st,
+                            const char** why) {
+  static void* scratch_ptr[64] = {};
+  int dev = -1;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) {
+    cudaGetLastError();
+    *why = "no usable CUDA device";
+    return ANIMA_ERR_CUDA;
+  }
+  if (!scratch_ptr[dev]) {
+    void* ptr = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&ptr, g_noalloc_scratch);
+    if (e != cudaSuccess || !ptr) {
+      cudaGetLastError();
+      *why = "cudaGetSymbolAddress of the no-allocation scratch failed";
+      return ANIMA_ERR_CUDA;
+    }
+    scratch_ptr[dev] = ptr;
+  }
+  const SplitPlan sp = plan_split(a->B * a->H, a->S_q, a->S_kv, a->flags, sm_count);
+  if (sp.bytes > attn::kNoAllocScratchBytes) {
+    *why = "this call's split schedule needs more scratch than the no-allocation entry's "
+           "static array holds (it is sized for GPUs with up to 160 SMs)";
+    return ANIMA_ERR_SHAPE;
+  }
+  if (sp.bytes > 0 &&
+      cudaMemsetAsync(scratch_ptr[dev], 0, attn::kSemBytes, st) != cudaSuccess) {
+    cudaGetLastError();
+    *why = "clearing the no-allocation scratch counters failed";
+    return ANIMA_ERR_CUDA;
+  }
+  AnimaAttnArgs b = *a;
+  b.workspace = scratch_ptr[dev];
+  b.workspace_bytes = attn::kNoAllocScratchBytes;
+  return attn_fwd_launch(&b, status, sm_count, st);
 }
 
 }  // namespace anima

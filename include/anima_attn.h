@@ -117,6 +117,23 @@ int anima_attn_prologue(const AnimaPrologueArgs* args, void* stream);
  * for device-resident operands. */
 int anima_attn_fwd(const AnimaAttnArgs* args, void* stream);
 
+/* anima_attn_fwd for callers that cannot allocate device memory.  No counterpart in the
+ * reference.  Some hosts cannot let a library allocate: a host that owns the whole device
+ * budget through its own allocator (a cudaMalloc behind its back breaks its accounting),
+ * and C plugins that are handed only device pointers and sizes, with no allocator to
+ * call; cudaMalloc and cudaFree also stall the device, which a caller in a tight loop
+ * cannot afford.  This entry takes the same arguments as anima_attn_fwd, ignores
+ * args->workspace, and allocates nothing: the scratch of the split schedule lives in a
+ * static device array of about 40.6 MB (4 KiB of counters plus two partial slots for
+ * each of up to 160 SMs), which every GPU that loads the library holds until the process
+ * exits.  The first call on each device looks the array up with that device current;
+ * make that first call before any stream capture.  Each call clears the array's counters
+ * on `stream` before its kernel; all calls on a device share the array, so calls that
+ * overlap on the GPU (different streams, no ordering) race and must not be issued.
+ * A call whose schedule would need more scratch than the array holds returns
+ * ANIMA_ERR_SHAPE (see anima_rt_last_error). */
+int anima_attn_fwd_noalloc(const AnimaAttnArgs* args, void* stream);
+
 /* Workspace bytes anima_attn_fwd can use for this shape on the current device
  * (0 when the one-CTA-per-unit schedule is used anyway). */
 uint64_t anima_attn_workspace_size(int B, int H, int S_q, int S_kv, unsigned flags);
