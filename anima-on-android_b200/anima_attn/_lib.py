@@ -60,6 +60,7 @@ SIGNATURES = {
     "anima_attn_fwd_noalloc": ([ct.POINTER(AttnArgs), _P], ct.c_int),
     "anima_attn_workspace_size": ([ct.c_int] * 4 + [ct.c_uint], ct.c_uint64),
     "anima_attn_status": ([_P, ct.c_int], ct.c_int),
+    "anima_attn_selftest_timeout": ([ct.c_uint, _P], ct.c_int),
     "anima_attn_device_info": ([ct.POINTER(ct.c_int), ct.POINTER(ct.c_int)], ct.c_int),
     "anima_attn_version": ([], ct.c_char_p),
 }

@@ -1,0 +1,275 @@
+"""One denoising step of the Anima 2B DiT on B200, head-parallel over N GPUs.
+
+This restates, for inference, the reference model and sampler step around the attention
+library:
+  MiniTrainDIT._forward   src/predict2.py:841-908  (patch embed, RoPE table, timestep
+                          embedding with adaLN-LoRA, blocks, final layer, unpatchify)
+  Block.forward           src/predict2.py:469-583  (adaLN-modulated self-attention,
+                          cross-attention and GELU MLP with gated residuals)
+  Attention               src/predict2.py:91-214   (q/k/v projections, per-head q/k
+                          RMSNorm, RoPE on self-attention, SDPA, o-proj)
+  EulerSampler step       anima_rt/scripts/sampling.py:115-140 (CFG pair, Euler update)
+The attention of every block (norm, RoPE, SDPA) runs in this library's kernels; the
+GEMMs, LayerNorm, GELU and adaLN arithmetic run in PyTorch.  Activations and the residual
+stream stay fp32; GEMMs take 16-bit operands with fp32 accumulation and fp32 outputs.
+The operand type is fp16 by default: the weights are bf16 values (exact in fp16 unless
+below 2^-14), the GEMM inputs are normalised activations, and fp16's 10-bit mantissa
+keeps the step's latent within 1.1e-3 rel-L2 of the fp32 reference model at 2 blocks,
+where bf16 operands give 8.5e-3.  The attention runs on fp16 operands for the same
+reason (q and k are RMS-normalised; v is a projection of normalised activations).
+
+Head parallelism: rank r of N owns heads [r*16/N, (r+1)*16/N).  It projects q/k/v for
+those heads only, runs their attention, and one all_gather_into_tensor per attention
+(self and cross) collects every rank's head outputs before the replicated o-proj.  The
+o-proj consumes the gathered chunks directly (one GEMM per rank's column block of the
+o-proj weight, accumulated), so no transpose copy is needed.  Everything else (adaLN,
+LayerNorm, MLP, final layer) is replicated.
+
+Weights follow the reference's parameter names (state-dict keys of MiniTrainDIT with
+use_adaln_lora=True), so the same seeded weights load into the reference model for the
+CPU oracle.
+"""
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass
+from typing import Callable, Dict, List, Optional, Tuple
+
+import torch
+import torch.nn.functional as F
+
+
+@dataclass
+class DiTConfig:
+    hidden: int = 2048
+    heads: int = 16
+    blocks: int = 28
+    mlp_ratio: float = 4.0
+    adaln_lora: int = 256
+    in_channels: int = 16
+    out_channels: int = 16
+    patch: int = 2
+    patch_t: int = 1
+    ctx_dim: int = 1024
+    eps: float = 1e-6
+    rope_h_ratio: float = 4.0
+    rope_w_ratio: float = 4.0
+    rope_t_ratio: float = 1.0
+    gemm_dtype: torch.dtype = torch.float16   # 16-bit operand type of GEMMs and attention
+
+    @property
+    def head_dim(self) -> int:
+        return self.hidden // self.heads
+
+
+def weight_spec(cfg: DiTConfig) -> List[Tuple[str, tuple, str]]:
+    """(reference parameter name, shape, kind) in a fixed order; kind 'w' = Linear
+    weight drawn N(0, 0.02) and stored bf16, 'one' = norm weight, fp32 ones."""
+    D, H, hd, L = cfg.hidden, cfg.heads, cfg.head_dim, cfg.adaln_lora
+    cin = (cfg.in_channels + 1) * cfg.patch * cfg.patch * cfg.patch_t  # + padding mask
+    spec = [("x_embedder.proj.1.weight", (D, cin), "w"),
+            ("t_embedder.1.linear_1.weight", (D, D), "w"),
+            ("t_embedder.1.linear_2.weight", (3 * D, D), "w"),
+            ("t_embedding_norm.weight", (D,), "one")]
+    mlp = int(D * cfg.mlp_ratio)
+    for b in range(cfg.blocks):
+        p = f"blocks.{b}."
+        for att, kv_in in (("self_attn", D), ("cross_attn", cfg.ctx_dim)):
+            spec += [(p + att + ".q_proj.weight", (D, D), "w"),
+                     (p + att + ".q_norm.weight", (hd,), "one"),
+                     (p + att + ".k_proj.weight", (D, kv_in), "w"),
+                     (p + att + ".k_norm.weight", (hd,), "one"),
+                     (p + att + ".v_proj.weight", (D, kv_in), "w"),
+                     (p + att + ".output_proj.weight", (D, D), "w")]
+        spec += [(p + "mlp.layer1.weight", (mlp, D), "w"),
+                 (p + "mlp.layer2.weight", (D, mlp), "w")]
+        for m in ("self_attn", "cross_attn", "mlp"):
+            spec += [(p + f"adaln_modulation_{m}.1.weight", (L, D), "w"),
+                     (p + f"adaln_modulation_{m}.2.weight", (3 * D, L), "w")]
+    pout = cfg.patch * cfg.patch * cfg.patch_t * cfg.out_channels
+    spec += [("final_layer.linear.weight", (pout, D), "w"),
+             ("final_layer.adaln_modulation.1.weight", (L, D), "w"),
+             ("final_layer.adaln_modulation.2.weight", (2 * D, L), "w")]
+    return spec
+
+
+def make_weights(cfg: DiTConfig, seed: int = 0, device="cpu", rng_device="cpu",
+                 keep: Optional[Callable[[str], bool]] = None) -> Dict[str, torch.Tensor]:
+    """Seeded random weights: Linear ~ N(0, 0.02) rounded to bf16, norm weights 1.
+
+    With rng_device='cpu' the values are identical on every machine (used by the parity
+    tests and the reference oracle); 'cuda' draws them on the GPU (fast, for benches).
+    ``keep`` filters names (a rank may skip weights it never uses)."""
+    g = torch.Generator(device=rng_device).manual_seed(seed)
+    out = {}
+    for name, shape, kind in weight_spec(cfg):
+        if kind == "one":
+            t = torch.ones(shape, dtype=torch.float32)
+        else:
+            t = torch.empty(shape, dtype=torch.float32, device=rng_device).normal_(0.0, 0.02, generator=g)
+            t = t.to(torch.bfloat16)
+        if keep is None or keep(name):
+            out[name] = t.to(device)
+    return out
+
+
+def timestep_sinusoid(t: torch.Tensor, channels: int) -> torch.Tensor:
+    """Timesteps.forward (predict2.py:222-235): [B] -> [B, 1, channels] = [cos | sin]."""
+    half = channels // 2
+    exponent = -math.log(10000) * torch.arange(half, dtype=torch.float32, device=t.device)
+    exponent = exponent / (half - 0.0)
+    emb = t.float()[:, None] * torch.exp(exponent)[None, :]
+    return torch.cat([torch.cos(emb), torch.sin(emb)], dim=-1)[:, None, :]
+
+
+def _linear(x: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
+    """x [..., K] @ w[N, K]^T: operands in w's 16-bit type, fp32 accumulation and output."""
+    shp = x.shape
+    x2 = x.reshape(-1, shp[-1])
+    if x.is_cuda:
+        y = torch.mm(x2.to(w.dtype), w.t(), out_dtype=torch.float32)
+    else:  # CPU tests of the sharding logic: same operand rounding, fp32 math
+        y = x2.to(w.dtype).float() @ w.float().t()
+    return y.reshape(*shp[:-1], w.shape[0])
+
+
+AttnFn = Callable[..., torch.Tensor]
+
+
+class AnimaDiT:
+    """Inference forward of the Anima DiT with this library's attention.
+
+    ``weights`` is a make_weights() dict (full model; a rank slices its head rows).
+    ``group``: torch.distributed process group for head parallelism (None = 1 GPU).
+    ``attn_fn`` replaces the attention op (signature of anima_attn.attention); tests on
+    CPU pass a reference implementation, the product uses the B200 kernels.
+    """
+
+    def __init__(self, cfg: DiTConfig, weights: Dict[str, torch.Tensor], rank: int = 0,
+                 world: int = 1, group=None, attn_fn: Optional[AttnFn] = None):
+        if cfg.heads % world:
+            raise ValueError("heads must divide evenly over ranks")
+        self.cfg, self.rank, self.world, self.group = cfg, rank, world, group
+        self.h_local = cfg.heads // world
+        self.w = {}
+        lo = rank * self.h_local * cfg.head_dim
+        hi = lo + self.h_local * cfg.head_dim
+        for name, t in weights.items():
+            if any(name.endswith(f".{p}_proj.weight") for p in ("q", "k", "v")):
+                t = t[lo:hi].contiguous()  # this rank's heads (output rows)
+            if t.dtype == torch.bfloat16:
+                t = t.to(cfg.gemm_dtype)  # GEMM operand type
+            self.w[name] = t
+        if attn_fn is None:
+            from .ops import attention as attn_fn
+        self.attn_fn = attn_fn
+        self._freqs_cache = {}
+
+    # ------------------------------------------------------------------ pieces
+    def _rope(self, T, Hp, Wp, device):
+        key = (T, Hp, Wp, str(device))
+        if key not in self._freqs_cache:
+            from .rope import rope_freqs_3d
+            self._freqs_cache[key] = rope_freqs_3d(
+                T, Hp, Wp, self.cfg.head_dim, self.cfg.rope_h_ratio, self.cfg.rope_w_ratio,
+                self.cfg.rope_t_ratio, device=device)
+        return self._freqs_cache[key]
+
+    def _ln_mod(self, x, scale, shift):
+        return F.layer_norm(x, (x.shape[-1],), eps=self.cfg.eps) * (1 + scale) + shift
+
+    def _gather_oproj(self, o_local: torch.Tensor, w_o: torch.Tensor) -> torch.Tensor:
+        """o_local [B, S, H/N, hd] -> o-proj of all heads [B, S, hidden] (fp32)."""
+        B, S = o_local.shape[:2]
+        cols = self.h_local * self.cfg.head_dim
+        if self.world == 1:
+            return _linear(o_local.reshape(B, S, cols).float(), w_o)
+        import torch.distributed as dist
+        # gathered along dim 0 ([world * B, S, H/N, hd]); viewed as [world, B, ...]
+        full = torch.empty((self.world * B,) + tuple(o_local.shape[1:]), dtype=o_local.dtype,
+                           device=o_local.device)
+        dist.all_gather_into_tensor(full, o_local.contiguous(), group=self.group)
+        full = full.view((self.world,) + tuple(o_local.shape))
+        out = None
+        for r in range(self.world):
+            part = _linear(full[r].reshape(B, S, cols).float(), w_o[:, r * cols:(r + 1) * cols])
+            out = part if out is None else out + part
+        return out
+
+    def _attention(self, p: str, x: torch.Tensor, ctx: Optional[torch.Tensor], freqs):
+        cfg = self.cfg
+        B, S = x.shape[:2]
+        src = x if ctx is None else ctx
+        Skv = src.shape[1]
+        hl, hd = self.h_local, cfg.head_dim
+        q = _linear(x, self.w[p + ".q_proj.weight"]).view(B, S, hl, hd)
+        k = _linear(src, self.w[p + ".k_proj.weight"]).view(B, Skv, hl, hd)
+        v = _linear(src, self.w[p + ".v_proj.weight"]).view(B, Skv, hl, hd)
+        o = self.attn_fn(q, k, v, self.w[p + ".q_norm.weight"], self.w[p + ".k_norm.weight"],
+                         freqs if ctx is None else None, eps=cfg.eps, out_dtype=cfg.gemm_dtype,
+                         op_dtype=cfg.gemm_dtype)
+        return self._gather_oproj(o, self.w[p + ".output_proj.weight"])
+
+    def _block(self, b: int, x, emb, lora, ctx, freqs):
+        p = f"blocks.{b}."
+        w = self.w
+
+        def mods(m):
+            h = _linear(F.silu(emb), w[p + f"adaln_modulation_{m}.1.weight"])
+            return (_linear(h, w[p + f"adaln_modulation_{m}.2.weight"]) + lora).chunk(3, dim=-1)
+
+        sh_sa, sc_sa, g_sa = mods("self_attn")
+        sh_ca, sc_ca, g_ca = mods("cross_attn")
+        sh_m, sc_m, g_m = mods("mlp")
+        h = self._ln_mod(x, sc_sa, sh_sa)
+        x = x + g_sa * self._attention(p + "self_attn", h, None, freqs)
+        h = self._ln_mod(x, sc_ca, sh_ca)
+        x = self._attention(p + "cross_attn", h, ctx, None) * g_ca + x
+        h = self._ln_mod(x, sc_m, sh_m)
+        h = _linear(F.gelu(_linear(h, w[p + "mlp.layer1.weight"])), w[p + "mlp.layer2.weight"])
+        return x + g_m * h
+
+    # ------------------------------------------------------------------ forward
+    def forward(self, x: torch.Tensor, timesteps: torch.Tensor, context: torch.Tensor):
+        """x [B, C, T, H, W] latent, timesteps [B], context [B, N, ctx_dim] -> v, x's shape."""
+        cfg, w = self.cfg, self.w
+        B, C, T, Hh, Ww = x.shape
+        ps, pt = cfg.patch, cfg.patch_t
+        if Hh % ps or Ww % ps or T % pt:
+            raise ValueError("latent must be a multiple of the patch size")
+        mask = torch.zeros(B, 1, T, Hh, Ww, dtype=x.dtype, device=x.device)
+        xm = torch.cat([x, mask], dim=1)
+        Tp, Hp, Wp = T // pt, Hh // ps, Ww // ps
+        # "b c (t r) (h m) (w n) -> b t h w (c r m n)"
+        xp = xm.reshape(B, C + 1, Tp, pt, Hp, ps, Wp, ps).permute(0, 2, 4, 6, 1, 3, 5, 7)
+        xp = xp.reshape(B, Tp * Hp * Wp, (C + 1) * pt * ps * ps)
+        h = _linear(xp, w["x_embedder.proj.1.weight"])  # [B, L, hidden]
+        freqs = self._rope(Tp, Hp, Wp, x.device)
+        sample = timestep_sinusoid(timesteps, cfg.hidden)  # [B, 1, hidden]
+        lora = _linear(F.silu(_linear(sample, w["t_embedder.1.linear_1.weight"])),
+                       w["t_embedder.1.linear_2.weight"])
+        emb = F.rms_norm(sample, (cfg.hidden,), w["t_embedding_norm.weight"], cfg.eps)
+        ctx = context.float()
+        for b in range(cfg.blocks):
+            h = self._block(b, h, emb, lora, ctx, freqs)
+        fm = _linear(_linear(F.silu(emb), w["final_layer.adaln_modulation.1.weight"]),
+                     w["final_layer.adaln_modulation.2.weight"])
+        shift, scale = (fm + lora[:, :, :2 * cfg.hidden]).chunk(2, dim=-1)
+        h = self._ln_mod(h, scale, shift)
+        out = _linear(h, w["final_layer.linear.weight"])  # [B, L, p*p*t*C]
+        # "B T H W (p1 p2 t C) -> B C (T t) (H p1) (W p2)"
+        out = out.reshape(B, Tp, Hp, Wp, ps, ps, pt, cfg.out_channels)
+        out = out.permute(0, 7, 1, 6, 2, 4, 3, 5).reshape(B, cfg.out_channels, T, Hh, Ww)
+        return out
+
+    def euler_cfg_step(self, x: torch.Tensor, sigma: float, sigma_next: float,
+                       ctx_cond: torch.Tensor, ctx_uncond: torch.Tensor, cfg_scale: float):
+        """One EulerSampler step (sampling.py:121-138): CFG pair [uncond, cond] in one
+        batch, v = v_u + cfg (v_c - v_u), x' = x + v (sigma_next - sigma).
+        x [1, C, H, W] -> [1, C, H, W]."""
+        xb = x[:, :, None].expand(2, -1, -1, -1, -1).contiguous()
+        ctx = torch.cat([ctx_uncond, ctx_cond], dim=0)
+        t = torch.full((2,), sigma, dtype=torch.float32, device=x.device)
+        v = self.forward(xb, t, ctx)
+        v_cfg = v[0:1] + cfg_scale * (v[1:2] - v[0:1])
+        return x + v_cfg[:, :, 0] * (sigma_next - sigma)

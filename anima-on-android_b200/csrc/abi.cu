@@ -17,6 +17,7 @@
 namespace anima {
 int attn_fwd_launch(const AnimaAttnArgs* a, int* status, int sm_count, cudaStream_t st);
 size_t attn_workspace_bytes(int B, int H, int S_q, int S_kv, unsigned flags, int sm_count);
+int selftest_wait_launch(int* status, unsigned timeout_us, cudaStream_t st);
 int attn_fwd_launch_noalloc(const AnimaAttnArgs* a, int* status, int sm_count, cudaStream_t st,
                             const char** why);
 int prologue_launch(const AnimaPrologueArgs* a, int sm_count, cudaStream_t st);
@@ -354,6 +355,13 @@ int anima_attn_status(void* stream, int reset) {
   }
   if (reset && code) cudaMemset(d->status, 0, sizeof(int));
   return code;
+}
+
+int anima_attn_selftest_timeout(unsigned timeout_us, void* stream) {
+  int rc = ANIMA_OK;
+  DeviceState* d = current_device(&rc);
+  if (!d) return rc;
+  return selftest_wait_launch(d->status, timeout_us, static_cast<cudaStream_t>(stream));
 }
 
 int anima_attn_device_info(int* sm_count, int* cc) {

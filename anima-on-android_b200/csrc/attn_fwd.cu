@@ -227,10 +227,10 @@ __device__ __forceinline__ void store_row(char* out_row, const uint32_t (&o)[32]
 #pragma unroll
     for (int e = 0; e < 4; ++e)
       dst[e] = make_uint4(
-          pack_bf16x2(__uint_as_float(o[8 * e]) * inv, __uint_as_float(o[8 * e + 1]) * inv),
-          pack_bf16x2(__uint_as_float(o[8 * e + 2]) * inv, __uint_as_float(o[8 * e + 3]) * inv),
-          pack_bf16x2(__uint_as_float(o[8 * e + 4]) * inv, __uint_as_float(o[8 * e + 5]) * inv),
-          pack_bf16x2(__uint_as_float(o[8 * e + 6]) * inv, __uint_as_float(o[8 * e + 7]) * inv));
+          pack2<kOut>(__uint_as_float(o[8 * e]) * inv, __uint_as_float(o[8 * e + 1]) * inv),
+          pack2<kOut>(__uint_as_float(o[8 * e + 2]) * inv, __uint_as_float(o[8 * e + 3]) * inv),
+          pack2<kOut>(__uint_as_float(o[8 * e + 4]) * inv, __uint_as_float(o[8 * e + 5]) * inv),
+          pack2<kOut>(__uint_as_float(o[8 * e + 6]) * inv, __uint_as_float(o[8 * e + 7]) * inv));
   }
 }
 
@@ -772,7 +772,9 @@ size_t attn_workspace_bytes(int B, int H, int S_q, int S_kv, unsigned flags, int
 int attn_fwd_launch(const AnimaAttnArgs* a, int* status, int sm_count, cudaStream_t st) {
   if (a->D != attn::kD) return ANIMA_ERR_SHAPE;
   if (a->op_dtype != ANIMA_DTYPE_BF16 && a->op_dtype != ANIMA_DTYPE_F16) return ANIMA_ERR_ARG;
-  if (a->out_dtype != ANIMA_DTYPE_F32 && a->out_dtype != ANIMA_DTYPE_BF16) return ANIMA_ERR_ARG;
+  if (a->out_dtype != ANIMA_DTYPE_F32 && a->out_dtype != ANIMA_DTYPE_BF16 &&
+      a->out_dtype != ANIMA_DTYPE_F16)
+    return ANIMA_ERR_ARG;
   const int bh = a->B * a->H;
   if (a->B <= 0 || a->H <= 0 || a->S_q <= 0 || a->S_kv <= 0) return ANIMA_ERR_SHAPE;
   CUtensorMap mq, mk, mv;
@@ -810,11 +812,17 @@ int attn_fwd_launch(const AnimaAttnArgs* a, int* status, int sm_count, cudaStrea
   prm.part = reinterpret_cast<float*>(static_cast<char*>(a->workspace) + attn::kSemBytes);
   const int grid = prm.split ? sm_count : (int)units;
   const bool bf = a->op_dtype == ANIMA_DTYPE_BF16;
-  const bool of32 = a->out_dtype == ANIMA_DTYPE_F32;
-  if (bf && of32) return launch_t<ANIMA_DTYPE_BF16, ANIMA_DTYPE_F32>(mq, mk, mv, prm, grid, st);
-  if (bf) return launch_t<ANIMA_DTYPE_BF16, ANIMA_DTYPE_BF16>(mq, mk, mv, prm, grid, st);
-  if (of32) return launch_t<ANIMA_DTYPE_F16, ANIMA_DTYPE_F32>(mq, mk, mv, prm, grid, st);
-  return launch_t<ANIMA_DTYPE_F16, ANIMA_DTYPE_BF16>(mq, mk, mv, prm, grid, st);
+  switch (a->out_dtype) {
+    case ANIMA_DTYPE_F32:
+      return bf ? launch_t<ANIMA_DTYPE_BF16, ANIMA_DTYPE_F32>(mq, mk, mv, prm, grid, st)
+                : launch_t<ANIMA_DTYPE_F16, ANIMA_DTYPE_F32>(mq, mk, mv, prm, grid, st);
+    case ANIMA_DTYPE_BF16:
+      return bf ? launch_t<ANIMA_DTYPE_BF16, ANIMA_DTYPE_BF16>(mq, mk, mv, prm, grid, st)
+                : launch_t<ANIMA_DTYPE_F16, ANIMA_DTYPE_BF16>(mq, mk, mv, prm, grid, st);
+    default:
+      return bf ? launch_t<ANIMA_DTYPE_BF16, ANIMA_DTYPE_F16>(mq, mk, mv, prm, grid, st)
+                : launch_t<ANIMA_DTYPE_F16, ANIMA_DTYPE_F16>(mq, mk, mv, prm, grid, st);
+  }
 }
 
 // Same launch as attn_fwd_launch, with the split schedule's scratch taken from

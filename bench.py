@@ -215,6 +215,104 @@ def _cpu_model():
     return None
 
 
+# ---------------------------------------------------------------- DiT step (config 4)
+def dit_flops(blocks=28, L=4096, B=2, ctx=512, hidden=2048, mlp=8192, ctx_dim=1024):
+    """Matmul FLOP of one CFG-batched forward (GEMMs + attention), as counted for the
+    config: per block self q/k/v/o, cross q/o, cross k/v, MLP, and both attentions."""
+    g = lambda m, n, k: 2.0 * m * n * k
+    per = (4 * g(B * L, hidden, hidden) + 2 * g(B * L, hidden, hidden) +
+           2 * g(B * ctx, hidden, ctx_dim) + g(B * L, mlp, hidden) + g(B * L, hidden, mlp) +
+           attn_flops(B, 16, L, L) + attn_flops(B, 16, L, ctx))
+    return blocks * per
+
+
+def run_dit(args, rank, world, local_rank):
+    """One Euler+CFG step of the Anima DiT: latent 16x128x128 (4096
+    tokens), 28 blocks, hidden 2048, 16 heads, CFG pair batched (B=2), sigma 0.5 -> 0,
+    cfg 5; heads split over the ranks, one NCCL all-gather per attention."""
+    import torch
+    from anima_attn.dit import AnimaDiT, DiTConfig, make_weights
+
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    cfg = DiTConfig(blocks=args.blocks)
+    group = None
+    if world > 1:
+        import torch.distributed as dist
+        group = dist.group.WORLD
+    weights = make_weights(cfg, seed=1234, device=dev, rng_device=dev)
+    model = AnimaDiT(cfg, weights, rank=rank, world=world, group=group)
+    del weights
+    side = args.latent
+    g = torch.Generator(device=dev).manual_seed(4321)
+    x = torch.randn(1, 16, side, side, device=dev, generator=g)
+    cc = torch.randn(1, 512, 1024, device=dev, generator=g)
+    cu = torch.randn(1, 512, 1024, device=dev, generator=g)
+    stream = torch.cuda.current_stream()
+
+    def barrier():
+        if world > 1:
+            import torch.distributed as dist
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    with torch.no_grad():
+        clocks = ClockSampler(local_rank)
+        with clocks:
+            for _ in range(args.warmup):
+                model.euler_cfg_step(x, 0.5, 0.0, cc, cu, 5.0)
+            barrier()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            t_begin = time.perf_counter()
+            e0.record(stream)
+            for _ in range(args.steps):
+                model.euler_cfg_step(x, 0.5, 0.0, cc, cu, 5.0)
+            e1.record(stream)
+            torch.cuda.synchronize()
+            t_end = time.perf_counter()
+            barrier()
+        ms = e0.elapsed_time(e1) / args.steps
+        # end to end: host latent + contexts in, host latent out, every step
+        hx, hcc, hcu = (t.cpu().pin_memory() for t in (x, cc, cu))
+        hout = torch.empty_like(hx).pin_memory()
+
+        def host_step():
+            dx, dcc, dcu = (t.to(dev, non_blocking=True) for t in (hx, hcc, hcu))
+            hout.copy_(model.euler_cfg_step(dx, 0.5, 0.0, dcc, dcu, 5.0), non_blocking=True)
+            torch.cuda.synchronize()
+
+        host_step()
+        barrier()
+        t0 = time.perf_counter()
+        n_e2e = max(2, min(args.steps, 5))
+        for _ in range(n_e2e):
+            host_step()
+        e2e_ms = (time.perf_counter() - t0) / n_e2e * 1e3
+    t = torch.tensor([ms, e2e_ms], device=dev, dtype=torch.float64)
+    if world > 1:
+        import torch.distributed as dist
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms, e2e_ms = t.tolist()
+    L = (side // 2) ** 2
+    fl = dit_flops(args.blocks, L)
+    return {
+        "metric": METRIC, "value": round(ms, 3), "unit": "ms", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 3),
+        "higher_is_better": False, "scaling": "strong", "vs_baseline": None,
+        "dtype": "fp16 GEMM/attention operands, fp32 activations",
+        "data": "synthetic (seeded latent and context, N(0,0.02) bf16-valued weights)",
+        "config": {"workload": f"Anima DiT Euler+CFG step, {args.blocks} blocks, latent "
+                               f"16x{side}x{side} ({L} tokens), context 512x1024, CFG pair",
+                   "global_batch": 2, "seq_len": L, "parallelism": f"heads{world}",
+                   "heads_per_gpu": 16 // world, "tflops_per_gpu": round(fl / world / (ms * 1e-3) / 1e12, 1),
+                   "model_tflop_per_step": round(fl / 1e12, 2)},
+        "e2e": {"value": round(e2e_ms, 3), "unit": "ms", "h2d_bytes_per_step": (hx.numel() + hcc.numel() + hcu.numel()) * 4,
+                "d2h_bytes_per_step": hout.numel() * 4},
+        "gpu_launches": args.steps * args.blocks * 4,
+        "clocks": clocks.summary(t_begin, t_end),
+    }
+
+
 # ---------------------------------------------------------------- our arm
 def run_ours(args, rank, world, local_rank):
     import numpy as np
@@ -361,6 +459,10 @@ def main():
     ap.add_argument("--L", type=int, default=4096)
     ap.add_argument("--shard", choices=["replicas", "heads"], default="replicas")
     ap.add_argument("--seed", type=int, default=0)
+    ap.add_argument("--workload", choices=["attn", "dit"], default="attn",
+                    help="attn: fused attention op (headline); dit: one full DiT step (config 4)")
+    ap.add_argument("--blocks", type=int, default=28, help="DiT blocks (dit workload)")
+    ap.add_argument("--latent", type=int, default=128, help="latent side (dit workload)")
     ap.add_argument("--schedule", choices=["auto", "unit"], default="auto",
                     help="auto: persistent stream-K when the call spans more than one wave; "
                          "unit: one CTA per 256-row unit")
@@ -397,6 +499,15 @@ def main():
         torch.cuda.set_device(local_rank)
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device("cuda", local_rank))
+    if args.workload == "dit":
+        res = run_dit(args, rank, world, local_rank)
+        if rank == 0:
+            print(json.dumps(res))
+        if world > 1:
+            import torch.distributed as dist
+            dist.barrier()
+            dist.destroy_process_group()
+        return
     res = run_ours(args, rank, world, local_rank)
     if rank == 0:
         if world == 1 and not args.no_cpu_baseline:

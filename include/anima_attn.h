@@ -80,7 +80,7 @@ typedef struct AnimaPrologueArgs {
 /*
  * Attention core (tcgen05 / TMEM flash forward, sm_100a).
  * q [B*H, S_q, D], k/v [B*H, S_kv, D] contiguous, dtype op_dtype (BF16 or F16), D = 128.
- * out: element strides out_stride = {b, h, s}, D contiguous, dtype out_dtype (F32, BF16).
+ * out: element strides out_stride = {b, h, s}, D contiguous, dtype out_dtype (F32, BF16, F16).
  *   [B*H, S_q, D] (the anima_rt layout):   {H*S_q*D, S_q*D, D}
  *   [B, S_q, H, D] (feeds the o-proj):     {S_q*H*D, D, H*D}
  * kv_valid_len: device int32 [B], used with ANIMA_FLAG_MASK (keys >= valid are masked;
@@ -141,6 +141,13 @@ uint64_t anima_attn_workspace_size(int B, int H, int S_q, int S_kv, unsigned fla
 /* Device status word of the current device: 0, or the first ANIMA_ERR_* a kernel
  * recorded.  Synchronises `stream`; clears the word when reset != 0. */
 int anima_attn_status(void* stream, int reset);
+
+/* Self-test of the bounded-wait path (no reference counterpart): launches one block
+ * whose mbarrier wait can never complete and gives up after timeout_us microseconds
+ * (1..1000000), recording ANIMA_ERR_TIMEOUT in the status word exactly as a stalled
+ * attention kernel would.  The kernel returns normally and the context stays usable;
+ * read and clear the result with anima_attn_status. */
+int anima_attn_selftest_timeout(unsigned timeout_us, void* stream);
 
 /* Number of streaming multiprocessors and compute capability of the current device
  * (major*10 + minor); returns ANIMA_ERR_CUDA without a device. */

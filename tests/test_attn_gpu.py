@@ -267,3 +267,21 @@ def test_long_sequence_rows_and_properties(aa, O, L):
     torch.cuda.synchronize()
     assert np.abs(o1.cpu().numpy() - 1.0).max() < 1e-2
     assert aa.status() == 0
+
+
+def test_bounded_wait_reports_timeout_and_context_survives(aa, O):
+    """Failure detection without a GPU fault: a wait on a flag nothing sets runs out
+    after 20 ms, the status word reads ANIMA_ERR_TIMEOUT, and the next call works."""
+    from anima_attn import _lib as L
+    st = ct.c_void_p(torch.cuda.current_stream().cuda_stream)
+    assert L.lib.anima_attn_status(st, 1) == 0
+    assert L.lib.anima_attn_selftest_timeout(20000, st) == L.OK
+    assert L.lib.anima_attn_status(st, 1) == L.ERR_TIMEOUT
+    assert L.lib.anima_attn_status(st, 1) == 0  # cleared by the previous read
+    assert L.lib.anima_attn_selftest_timeout(0, st) == L.ERR_ARG
+    rng = np.random.default_rng(1)
+    q, k, v = (rng.standard_normal((1, 2, 200, 128), dtype=np.float32) for _ in range(3))
+    got = aa.sdpa(_dev(q), _dev(k), _dev(v))
+    torch.cuda.synchronize()
+    _ok(got.cpu().numpy(), O.sdpa(q, k, v))
+    assert aa.status() == 0
