@@ -120,7 +120,7 @@ def attention_core(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, B: int, H:
                    scale: Optional[float] = None, kv_valid_len: Optional[torch.Tensor] = None,
                    causal: bool = False, out: Optional[torch.Tensor] = None,
                    out_layout: str = "bshd", out_dtype=torch.float32,
-                   stream_k: bool = True) -> torch.Tensor:
+                   stream_k: bool = True, pair: bool = False) -> torch.Tensor:
     """tcgen05 flash attention on 16-bit head-major operands.
 
     q [B*H, S_q, 128], k/v [B*H, S_kv, 128] contiguous bf16/fp16.  Returns (or fills)
@@ -128,6 +128,7 @@ def attention_core(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, B: int, H:
     ``kv_valid_len`` int32 [B] masks keys >= kv_valid_len[b] (cross-attention padding).
     ``stream_k`` lets calls of more than one wave use the persistent split schedule
     (with a cached workspace); False forces one CTA per 256-row unit.
+    ``pair`` runs the CTA-pair kernel (2-SM MMA, one pair per 512-row unit).
     """
     _check_cuda(q, k, v)
     BH, Sq, D = q.shape
@@ -149,7 +150,7 @@ def attention_core(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, B: int, H:
         raise ValueError("out_layout must be 'bshd' or 'bhsd'")
     if out.stride(3) != 1:
         raise ValueError("output head dimension must be contiguous")
-    flags = L.FLAG_CAUSAL if causal else 0
+    flags = (L.FLAG_CAUSAL if causal else 0) | (L.FLAG_PAIR if pair else 0)
     vl = None
     if kv_valid_len is not None:
         vl = kv_valid_len.to(device=q.device, dtype=torch.int32).contiguous()
@@ -167,7 +168,7 @@ def attention_core(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, B: int, H:
     a.flags = flags
     a.kv_valid_len = _ptr(vl)
     ws = None
-    if stream_k:
+    if stream_k and not pair:
         ws = _workspace(q.device, int(L.lib.anima_attn_workspace_size(B, H, Sq, Skv, flags)))
     a.workspace = _ptr(ws)
     a.workspace_bytes = 0 if ws is None else ws.numel()

@@ -16,6 +16,7 @@
 
 namespace anima {
 int attn_fwd_launch(const AnimaAttnArgs* a, int* status, int sm_count, cudaStream_t st);
+int attn_fwd_pair_launch(const AnimaAttnArgs* a, int* status, cudaStream_t st);
 size_t attn_workspace_bytes(int B, int H, int S_q, int S_kv, unsigned flags, int sm_count);
 int selftest_wait_launch(int* status, unsigned timeout_us, cudaStream_t st);
 int attn_fwd_launch_noalloc(const AnimaAttnArgs* a, int* status, int sm_count, cudaStream_t st,
@@ -309,7 +310,10 @@ int anima_attn_fwd(const AnimaAttnArgs* a, void* stream) {
   int rc = ANIMA_OK;
   DeviceState* d = current_device(&rc);
   if (!d) return rc;
-  rc = attn_fwd_launch(a, d->status, d->sm_count, static_cast<cudaStream_t>(stream));
+  if (a->flags & ANIMA_FLAG_PAIR)
+    rc = attn_fwd_pair_launch(a, d->status, static_cast<cudaStream_t>(stream));
+  else
+    rc = attn_fwd_launch(a, d->status, d->sm_count, static_cast<cudaStream_t>(stream));
   if (rc != ANIMA_OK) set_error(std::string("anima_attn_fwd: ") + code_name(rc));
   return rc;
 }

@@ -46,6 +46,8 @@ enum { ANIMA_DTYPE_F32 = 0, ANIMA_DTYPE_BF16 = 1, ANIMA_DTYPE_F16 = 2 };
 #define ANIMA_FLAG_ROPE 0x4u   /* rotate q and k with rope_freqs          */
 #define ANIMA_FLAG_MASK 0x8u   /* key-padding mask from kv_valid_len[B]   */
 #define ANIMA_FLAG_CAUSAL 0x10u /* top-left causal mask (col <= row)      */
+#define ANIMA_FLAG_PAIR 0x20u  /* anima_attn_fwd: run on CTA pairs (2-SM MMA), one pair per
+                                  512-row unit                             */
 
 /*
  * Prologue: per-head RMSNorm + RoPE + cast, one HBM pass.

@@ -285,3 +285,29 @@ def test_bounded_wait_reports_timeout_and_context_survives(aa, O):
     torch.cuda.synchronize()
     _ok(got.cpu().numpy(), O.sdpa(q, k, v))
     assert aa.status() == 0
+
+
+PAIR_SHAPES = [  # (B, H, Sq, Skv, causal, valid)
+    (1, 1, 512, 128, False, None), (1, 2, 700, 300, False, None), (2, 3, 1000, 1000, False, None),
+    (1, 2, 600, 600, True, None), (4, 2, 512, 512, False, [0, 5, 130, 512]),
+    (1, 1, 1, 1, False, None),
+]
+
+
+@pytest.mark.parametrize("B,H,Sq,Skv,causal,valid", PAIR_SHAPES)
+def test_cta_pair_kernel(aa, O, B, H, Sq, Skv, causal, valid):
+    """The opt-in CTA-pair kernel (tcgen05.mma.cta_group::2, M = 256 over two SMs, each
+    SM loading half of every K and V tile) against the oracle."""
+    rng = np.random.default_rng(Sq * 7 + Skv)
+    q = rng.standard_normal((B, H, Sq, 128), dtype=np.float32)
+    k = rng.standard_normal((B, H, Skv, 128), dtype=np.float32)
+    v = rng.standard_normal((B, H, Skv, 128), dtype=np.float32)
+    qh, kh, vh = (_dev(t).reshape(B * H, -1, 128).to(torch.bfloat16) for t in (q, k, v))
+    vl = None if valid is None else _dev(np.array(valid, np.int32))
+    out = aa.attention_core(qh, kh, vh, B, H, kv_valid_len=vl, causal=causal, out_layout="bhsd",
+                            pair=True)
+    torch.cuda.synchronize()
+    assert aa.status() == 0
+    ref = (O.sdpa(q, k, v, causal=causal) if valid is None
+           else O.sdpa_varlen(q, k, v, np.array(valid, np.int32)))
+    _ok(out.cpu().numpy(), ref)
