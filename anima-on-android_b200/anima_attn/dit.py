@@ -9,9 +9,13 @@ library:
   Attention               src/predict2.py:91-214   (q/k/v projections, per-head q/k
                           RMSNorm, RoPE on self-attention, SDPA, o-proj)
   EulerSampler step       anima_rt/scripts/sampling.py:115-140 (CFG pair, Euler update)
-The attention of every block (norm, RoPE, SDPA) runs in this library's kernels; the
-GEMMs, LayerNorm, GELU and adaLN arithmetic run in PyTorch.  Activations and the residual
-stream stay fp32; GEMMs take 16-bit operands with fp32 accumulation and fp32 outputs.
+The attention of every block (norm, RoPE, SDPA) runs in this library's kernels, and so
+do the two fused HBM passes around it: LayerNorm + adaLN modulation + 16-bit cast
+(anima_dit_ln_modulate) and the gated residual update (anima_dit_gate_residual).  GEMMs
+and GELU run in PyTorch.  The residual stream stays fp32; GEMMs take 16-bit operands with
+fp32 accumulation.  A GEMM whose consumer rounds to the operand type anyway (q/k/v into
+the attention prologue, MLP layer 1 into GELU and layer 2) writes 16-bit output; the others
+write fp32.
 The operand type is fp16 by default: the weights are bf16 values (exact in fp16 unless
 below 2^-14), the GEMM inputs are normalised activations, and fp16's 10-bit mantissa
 keeps the step's latent within 1.1e-3 rel-L2 of the fp32 reference model at 2 blocks,
@@ -122,14 +126,18 @@ def timestep_sinusoid(t: torch.Tensor, channels: int) -> torch.Tensor:
     return torch.cat([torch.cos(emb), torch.sin(emb)], dim=-1)[:, None, :]
 
 
-def _linear(x: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
-    """x [..., K] @ w[N, K]^T: operands in w's 16-bit type, fp32 accumulation and output."""
+def _linear(x: torch.Tensor, w: torch.Tensor, out_dtype=torch.float32) -> torch.Tensor:
+    """x [..., K] @ w[N, K]^T: operands in w's 16-bit type, fp32 accumulation, output in
+    ``out_dtype`` (fp32, or w's type)."""
     shp = x.shape
     x2 = x.reshape(-1, shp[-1])
     if x.is_cuda:
-        y = torch.mm(x2.to(w.dtype), w.t(), out_dtype=torch.float32)
+        if out_dtype == w.dtype:
+            y = torch.mm(x2.to(w.dtype), w.t())
+        else:
+            y = torch.mm(x2.to(w.dtype), w.t(), out_dtype=out_dtype)
     else:  # CPU tests of the sharding logic: same operand rounding, fp32 math
-        y = x2.to(w.dtype).float() @ w.float().t()
+        y = (x2.to(w.dtype).float() @ w.float().t()).to(out_dtype)
     return y.reshape(*shp[:-1], w.shape[0])
 
 
@@ -160,6 +168,15 @@ class AnimaDiT:
             if t.dtype == torch.bfloat16:
                 t = t.to(cfg.gemm_dtype)  # GEMM operand type
             self.w[name] = t
+        # One GEMM per input: self-attention [Wq; Wk; Wv] on x, cross-attention [Wk; Wv]
+        # on the context.  The prologue reads q/k/v as strided views of its output.
+        for b in range(cfg.blocks):
+            p = f"blocks.{b}."
+            sa, ca = p + "self_attn.", p + "cross_attn."
+            if sa + "q_proj.weight" in self.w:
+                self.w[sa + "qkv"] = torch.cat([self.w.pop(sa + f"{c}_proj.weight") for c in "qkv"])
+            if ca + "k_proj.weight" in self.w:
+                self.w[ca + "kv"] = torch.cat([self.w.pop(ca + f"{c}_proj.weight") for c in "kv"])
         if attn_fn is None:
             from .ops import attention as attn_fn
         self.attn_fn = attn_fn
@@ -176,14 +193,27 @@ class AnimaDiT:
         return self._freqs_cache[key]
 
     def _ln_mod(self, x, scale, shift):
-        return F.layer_norm(x, (x.shape[-1],), eps=self.cfg.eps) * (1 + scale) + shift
+        """LayerNorm(x) * (1 + scale) + shift as the next GEMM's 16-bit operand."""
+        if x.is_cuda:
+            from .ops import ln_modulate
+            return ln_modulate(x, scale, shift, self.cfg.eps, out_dtype=self.cfg.gemm_dtype)
+        h = F.layer_norm(x, (x.shape[-1],), eps=self.cfg.eps) * (1 + scale) + shift
+        return h.to(self.cfg.gemm_dtype)
+
+    @staticmethod
+    def _gate_add(x, gate, y):
+        """x + gate * y; in place on CUDA (x is this forward's own residual buffer)."""
+        if x.is_cuda:
+            from .ops import gate_residual_
+            return gate_residual_(x, gate, y)
+        return x + gate * y
 
     def _gather_oproj(self, o_local: torch.Tensor, w_o: torch.Tensor) -> torch.Tensor:
         """o_local [B, S, H/N, hd] -> o-proj of all heads [B, S, hidden] (fp32)."""
         B, S = o_local.shape[:2]
         cols = self.h_local * self.cfg.head_dim
         if self.world == 1:
-            return _linear(o_local.reshape(B, S, cols).float(), w_o)
+            return _linear(o_local.reshape(B, S, cols), w_o)
         import torch.distributed as dist
         # gathered along dim 0 ([world * B, S, H/N, hd]); viewed as [world, B, ...]
         full = torch.empty((self.world * B,) + tuple(o_local.shape[1:]), dtype=o_local.dtype,
@@ -192,7 +222,7 @@ class AnimaDiT:
         full = full.view((self.world,) + tuple(o_local.shape))
         out = None
         for r in range(self.world):
-            part = _linear(full[r].reshape(B, S, cols).float(), w_o[:, r * cols:(r + 1) * cols])
+            part = _linear(full[r].reshape(B, S, cols), w_o[:, r * cols:(r + 1) * cols])
             out = part if out is None else out + part
         return out
 
@@ -201,10 +231,14 @@ class AnimaDiT:
         B, S = x.shape[:2]
         src = x if ctx is None else ctx
         Skv = src.shape[1]
-        hl, hd = self.h_local, cfg.head_dim
-        q = _linear(x, self.w[p + ".q_proj.weight"]).view(B, S, hl, hd)
-        k = _linear(src, self.w[p + ".k_proj.weight"]).view(B, Skv, hl, hd)
-        v = _linear(src, self.w[p + ".v_proj.weight"]).view(B, Skv, hl, hd)
+        hl, hd, dt = self.h_local, cfg.head_dim, cfg.gemm_dtype
+        if ctx is None:
+            qkv = _linear(x, self.w[p + ".qkv"], dt).view(B, S, 3, hl, hd)
+            q, k, v = qkv[:, :, 0], qkv[:, :, 1], qkv[:, :, 2]
+        else:
+            q = _linear(x, self.w[p + ".q_proj.weight"], dt).view(B, S, hl, hd)
+            kv = _linear(src, self.w[p + ".kv"], dt).view(B, Skv, 2, hl, hd)
+            k, v = kv[:, :, 0], kv[:, :, 1]
         o = self.attn_fn(q, k, v, self.w[p + ".q_norm.weight"], self.w[p + ".k_norm.weight"],
                          freqs if ctx is None else None, eps=cfg.eps, out_dtype=cfg.gemm_dtype,
                          op_dtype=cfg.gemm_dtype)
@@ -221,13 +255,15 @@ class AnimaDiT:
         sh_sa, sc_sa, g_sa = mods("self_attn")
         sh_ca, sc_ca, g_ca = mods("cross_attn")
         sh_m, sc_m, g_m = mods("mlp")
+        dt = self.cfg.gemm_dtype
         h = self._ln_mod(x, sc_sa, sh_sa)
-        x = x + g_sa * self._attention(p + "self_attn", h, None, freqs)
+        x = self._gate_add(x, g_sa, self._attention(p + "self_attn", h, None, freqs))
         h = self._ln_mod(x, sc_ca, sh_ca)
-        x = self._attention(p + "cross_attn", h, ctx, None) * g_ca + x
+        x = self._gate_add(x, g_ca, self._attention(p + "cross_attn", h, ctx, None))
         h = self._ln_mod(x, sc_m, sh_m)
-        h = _linear(F.gelu(_linear(h, w[p + "mlp.layer1.weight"])), w[p + "mlp.layer2.weight"])
-        return x + g_m * h
+        # GELU in fp32 arithmetic on the 16-bit layer-1 output; layer 2 reads 16-bit anyway
+        h = _linear(F.gelu(_linear(h, w[p + "mlp.layer1.weight"], dt)), w[p + "mlp.layer2.weight"])
+        return self._gate_add(x, g_m, h)
 
     # ------------------------------------------------------------------ forward
     def forward(self, x: torch.Tensor, timesteps: torch.Tensor, context: torch.Tensor):

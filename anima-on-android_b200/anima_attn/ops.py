@@ -217,6 +217,36 @@ def sdpa(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, scale: Optional[floa
     return o if o.dtype == q.dtype else o.to(q.dtype)
 
 
+def ln_modulate(x: torch.Tensor, scale: torch.Tensor, shift: torch.Tensor, eps: float = 1e-6,
+                out_dtype=torch.float16) -> torch.Tensor:
+    """LayerNorm(x) * (1 + scale) + shift -> out_dtype, one pass (DiT block, predict2.py:512).
+    x [B, L, D] fp32 contiguous; scale/shift [B, 1, D] fp32 views with D contiguous."""
+    _check_cuda(x, scale, shift)
+    B, Lr, D = x.shape
+    if x.dtype != torch.float32 or not x.is_contiguous():
+        raise ValueError("x must be contiguous float32")
+    y = torch.empty((B, Lr, D), device=x.device, dtype=out_dtype)
+    if scale.stride(-1) != 1 or shift.stride(-1) != 1 or scale.stride(0) != shift.stride(0):
+        raise ValueError("scale/shift rows must be contiguous with a common batch stride")
+    L.check(L.lib.anima_dit_ln_modulate(_ptr(x), _ptr(scale), _ptr(shift), scale.stride(0), _ptr(y),
+                                        _TORCH_DT[out_dtype], B * Lr, Lr, D, float(eps),
+                                        ct.c_void_p(_stream())), "anima_dit_ln_modulate")
+    return y
+
+
+def gate_residual_(x: torch.Tensor, gate: torch.Tensor, y: torch.Tensor) -> torch.Tensor:
+    """x += gate * y in place; x, y [B, L, D] fp32 contiguous, gate [B, 1, D] view."""
+    _check_cuda(x, gate, y)
+    B, Lr, D = x.shape
+    if gate.stride(-1) != 1 or not y.is_contiguous() or not x.is_contiguous():
+        raise ValueError("contiguous operands expected")
+    if x.dtype != torch.float32 or y.dtype != torch.float32 or y.shape != x.shape:
+        raise ValueError("x and y must be float32 of one shape")
+    L.check(L.lib.anima_dit_gate_residual(_ptr(x), _ptr(gate), gate.stride(0), _ptr(y), B * Lr, Lr,
+                                          D, ct.c_void_p(_stream())), "anima_dit_gate_residual")
+    return x
+
+
 def status(reset: bool = True) -> int:
     """Synchronise the current stream and return the device status word (0 = clean).
     A non-zero status drops the cached workspaces (an aborted kernel may have left

@@ -19,6 +19,11 @@ int attn_fwd_launch(const AnimaAttnArgs* a, int* status, int sm_count, cudaStrea
 int attn_fwd_pair_launch(const AnimaAttnArgs* a, int* status, cudaStream_t st);
 size_t attn_workspace_bytes(int B, int H, int S_q, int S_kv, unsigned flags, int sm_count);
 int selftest_wait_launch(int* status, unsigned timeout_us, cudaStream_t st);
+int ln_modulate_launch(const float* x, const float* scale, const float* shift, long long mod_stride,
+                       void* y, int out_dtype, long long rows, int rows_per_b, int D, float eps,
+                       int sm_count, cudaStream_t st);
+int gate_residual_launch(float* x, const float* gate, long long gate_stride, const float* y,
+                         long long rows, int rows_per_b, int D, int sm_count, cudaStream_t st);
 int attn_fwd_launch_noalloc(const AnimaAttnArgs* a, int* status, int sm_count, cudaStream_t st,
                             const char** why);
 int prologue_launch(const AnimaPrologueArgs* a, int sm_count, cudaStream_t st);
@@ -359,6 +364,33 @@ int anima_attn_status(void* stream, int reset) {
   }
   if (reset && code) cudaMemset(d->status, 0, sizeof(int));
   return code;
+}
+
+static bool al16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+int anima_dit_ln_modulate(const float* x, const float* scale, const float* shift,
+                          int64_t mod_stride_b, void* y, int out_dtype, int64_t rows,
+                          int rows_per_b, int D, float eps, void* stream) {
+  if (!x || !scale || !shift || !y || rows < 0 || rows_per_b <= 0 || mod_stride_b % 4) return ANIMA_ERR_ARG;
+  if (!al16(x) || !al16(scale) || !al16(shift) || !al16(y)) return ANIMA_ERR_ARG;
+  if (rows == 0) return ANIMA_OK;
+  int rc = ANIMA_OK;
+  DeviceState* d = current_device(&rc);
+  if (!d) return rc;
+  return ln_modulate_launch(x, scale, shift, mod_stride_b, y, out_dtype, rows, rows_per_b, D, eps,
+                            d->sm_count, static_cast<cudaStream_t>(stream));
+}
+
+int anima_dit_gate_residual(float* x, const float* gate, int64_t gate_stride_b, const float* y,
+                            int64_t rows, int rows_per_b, int D, void* stream) {
+  if (!x || !gate || !y || rows < 0 || rows_per_b <= 0 || gate_stride_b % 4) return ANIMA_ERR_ARG;
+  if (!al16(x) || !al16(gate) || !al16(y)) return ANIMA_ERR_ARG;
+  if (rows == 0) return ANIMA_OK;
+  int rc = ANIMA_OK;
+  DeviceState* d = current_device(&rc);
+  if (!d) return rc;
+  return gate_residual_launch(x, gate, gate_stride_b, y, rows, rows_per_b, D, d->sm_count,
+                              static_cast<cudaStream_t>(stream));
 }
 
 int anima_attn_selftest_timeout(unsigned timeout_us, void* stream) {

@@ -144,6 +144,19 @@ uint64_t anima_attn_workspace_size(int B, int H, int S_q, int S_kv, unsigned fla
  * recorded.  Synchronises `stream`; clears the word when reset != 0. */
 int anima_attn_status(void* stream, int reset);
 
+/* DiT block helpers around the attention (fused HBM passes; no single reference
+ * counterpart, they replace chains of elementwise ops of src/predict2.py:469-583).
+ * anima_dit_ln_modulate: y = LayerNorm(x) * (1 + scale[b]) + shift[b] over rows of D = 2048
+ *   (eps, no affine; predict2.py:512-513), written as out_dtype (F16 or BF16) for the next
+ *   GEMM; b = row / rows_per_b; scale/shift rows are mod_stride_b floats apart.
+ * anima_dit_gate_residual: x += gate[b] * y, fp32, in place (predict2.py:536, 563, 582).
+ * Pointers 16-byte aligned, strides multiples of 4.  Asynchronous on `stream`. */
+int anima_dit_ln_modulate(const float* x, const float* scale, const float* shift,
+                          int64_t mod_stride_b, void* y, int out_dtype, int64_t rows,
+                          int rows_per_b, int D, float eps, void* stream);
+int anima_dit_gate_residual(float* x, const float* gate, int64_t gate_stride_b, const float* y,
+                            int64_t rows, int rows_per_b, int D, void* stream);
+
 /* Self-test of the bounded-wait path (no reference counterpart): launches one block
  * whose mbarrier wait can never complete and gives up after timeout_us microseconds
  * (1..1000000), recording ANIMA_ERR_TIMEOUT in the status word exactly as a stalled

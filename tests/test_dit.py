@@ -98,3 +98,36 @@ def test_dit_step_on_gpu_matches_reference_model(which):
     r = rel_l2(out, g["x_next"])
     print(f"DiT step {which}: latent rel-L2 {r:.3e}")
     assert r <= LATENT_REL_L2
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("out_dtype", [torch.float16, torch.bfloat16])
+def test_ln_modulate_kernel_vs_torch(out_dtype):
+    """anima_dit_ln_modulate against fp32 torch LayerNorm * (1 + scale) + shift, with
+    scale/shift as chunks of one [B, 1, 3D] tensor (the adaLN layout)."""
+    from anima_attn.ops import ln_modulate
+    g = torch.Generator(device="cuda").manual_seed(7)
+    B, S, D = 2, 777, 2048
+    x = torch.randn(B, S, D, device="cuda", generator=g) * 3 + 0.5
+    mods = torch.randn(B, 1, 3 * D, device="cuda", generator=g) * 0.2
+    sh, sc, _ = mods.chunk(3, dim=-1)
+    y = ln_modulate(x, sc, sh, 1e-6, out_dtype=out_dtype)
+    ref = torch.nn.functional.layer_norm(x, (D,), eps=1e-6) * (1 + sc) + sh
+    tol = 2 ** -8 if out_dtype == torch.float16 else 2 ** -5  # half an ulp of |y| < 4, plus fp32
+    err = (y.float() - ref).abs() / ref.abs().clamp_min(1.0)
+    assert err.max().item() <= tol
+
+
+@pytest.mark.gpu
+def test_gate_residual_kernel_vs_torch():
+    from anima_attn.ops import gate_residual_
+    g = torch.Generator(device="cuda").manual_seed(8)
+    B, S, D = 2, 1031, 2048
+    x = torch.randn(B, S, D, device="cuda", generator=g)
+    y = torch.randn(B, S, D, device="cuda", generator=g)
+    mods = torch.randn(B, 1, 3 * D, device="cuda", generator=g)
+    gate = mods.chunk(3, dim=-1)[2]
+    ref = x + gate * y
+    out = gate_residual_(x, gate, y)
+    assert out.data_ptr() == x.data_ptr()
+    torch.testing.assert_close(out, ref, rtol=1e-6, atol=1e-6)
