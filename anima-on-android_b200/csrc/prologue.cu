@@ -8,7 +8,8 @@
 //   transpose     numpy_dit.py:291 ([B,S,H,D] -> [B,H,S,D])
 //   cast          fp32 -> bf16/f16 operands for the tensor cores
 // One warp owns one token (b, s) of one tensor and walks its H head rows, so the RoPE
-// row of that token is read once and reused for every head (layout in prologue_kernel).
+// row of that token is read once and reused for every head (layout in prologue_kernel);
+// every lane moves 16 bytes per load for fp32 and 16-bit inputs alike.
 //
 // rmsnorm_kernel / rope_kernel: the stand-alone drop-ins behind anima_rt_run_rmsnorm
 // and anima_rt_run_rope (fp32 in, fp32 out, any row length / even head size).
@@ -29,26 +30,41 @@ struct PrologueParams {
   long long tokens_q, tokens_k;  // B*S_q, B*S_kv
 };
 
-// Four consecutive elements of a row as fp32.
-template <typename T>
-__device__ __forceinline__ float4 load4(const T* p);
+// One 16-byte load: 4 fp32 or 8 16-bit elements of a row, kept raw until used.
+template <typename Tin>
+__device__ __forceinline__ uint4 load16(const Tin* p) {
+  return __ldg(reinterpret_cast<const uint4*>(p));
+}
+
+// Raw 16 bytes -> E floats.
+template <typename Tin>
+__device__ __forceinline__ void widen(const uint4& u, float* f);
 template <>
-__device__ __forceinline__ float4 load4<float>(const float* p) {
-  return __ldg(reinterpret_cast<const float4*>(p));
+__device__ __forceinline__ void widen<float>(const uint4& u, float* f) {
+  f[0] = __uint_as_float(u.x);
+  f[1] = __uint_as_float(u.y);
+  f[2] = __uint_as_float(u.z);
+  f[3] = __uint_as_float(u.w);
 }
 template <>
-__device__ __forceinline__ float4 load4<__nv_bfloat16>(const __nv_bfloat16* p) {
-  const uint2 u = __ldg(reinterpret_cast<const uint2*>(p));
-  const float2 a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.x));
-  const float2 b = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.y));
-  return make_float4(a.x, a.y, b.x, b.y);
+__device__ __forceinline__ void widen<__half>(const uint4& u, float* f) {
+  const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 v = __half22float2(*reinterpret_cast<const __half2*>(&w[i]));
+    f[2 * i] = v.x;
+    f[2 * i + 1] = v.y;
+  }
 }
 template <>
-__device__ __forceinline__ float4 load4<__half>(const __half* p) {
-  const uint2 u = __ldg(reinterpret_cast<const uint2*>(p));
-  const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&u.x));
-  const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&u.y));
-  return make_float4(a.x, a.y, b.x, b.y);
+__device__ __forceinline__ void widen<__nv_bfloat16>(const uint4& u, float* f) {
+  const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 v = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w[i]));
+    f[2 * i] = v.x;
+    f[2 * i + 1] = v.y;
+  }
 }
 
 template <int kOp>
@@ -56,10 +72,15 @@ __device__ __forceinline__ uint32_t pack_op(float lo, float hi) {
   return kOp == ANIMA_DTYPE_BF16 ? pack_bf16x2(lo, hi) : pack_f16x2(lo, hi);
 }
 
-// x * inv * w with both products rounded (the reference's order), for 4 lanes of a row.
-__device__ __forceinline__ float4 scale4(float4 x, float inv, float4 w) {
-  return make_float4(__fmul_rn(__fmul_rn(x.x, inv), w.x), __fmul_rn(__fmul_rn(x.y, inv), w.y),
-                     __fmul_rn(__fmul_rn(x.z, inv), w.z), __fmul_rn(__fmul_rn(x.w, inv), w.w));
+// E floats -> E 16-bit operands at p (E = 4: 8 bytes, E = 8: 16 bytes).
+template <int E, int kOp>
+__device__ __forceinline__ void store_op(void* p, const float* v) {
+  if constexpr (E == 4) {
+    *reinterpret_cast<uint2*>(p) = make_uint2(pack_op<kOp>(v[0], v[1]), pack_op<kOp>(v[2], v[3]));
+  } else {
+    *reinterpret_cast<uint4*>(p) = make_uint4(pack_op<kOp>(v[0], v[1]), pack_op<kOp>(v[2], v[3]),
+                                              pack_op<kOp>(v[4], v[5]), pack_op<kOp>(v[6], v[7]));
+  }
 }
 
 // One RoPE pair (a, c) with table entry f = [cos, -sin, sin, cos]; products and sums
@@ -71,28 +92,27 @@ __device__ __forceinline__ void rot(float& a, float& c, float4 f) {
   c = y;
 }
 
-// Work item = one token (b, s) of one tensor.  A half-warp owns one head row: lane
-// l = lane & 15 holds elements [4l, 4l+4) and [64+4l, 64+4l+4), i.e. RoPE pairs
-// p = 4l..4l+3, so the rotation needs no shuffles and the norm reduces over 16 lanes.
-// The two half-warps take heads h and h+1; 2*kPairsInFlight heads are loaded before any
-// is processed to keep enough bytes in flight per SM.
+// Work item = one token (b, s) of one tensor; the warp walks that token's H head rows,
+// so the token's RoPE row is read once and reused for every head.
+// A head row (D = 128) is held by R = 64 / E lanes, E = 16 / sizeof(Tin) elements per
+// 16-byte load: lane l of the group holds elements [E*l, E*l + E) and 64 + the same,
+// i.e. RoPE pairs p = E*l .. E*l + E - 1, so the rotation needs no shuffles and the norm
+// reduces over the R lanes.  The warp's 32 / R lane groups take consecutive heads, and
+// kPasses such passes are loaded before any is processed: 16 heads (fp32: 8) and 4 KiB
+// per warp in flight.
 template <typename Tin, int kOp>
 __global__ void __launch_bounds__(256) prologue_kernel(const PrologueParams p) {
-  constexpr int kPairsInFlight = 4;  // 8 heads per batch of loads
+  constexpr int E = 16 / (int)sizeof(Tin);
+  constexpr int R = 64 / E;       // lanes per head row
+  constexpr int G = 32 / R;       // head rows per pass
+  constexpr int kPasses = 4;
+  constexpr int HB = G * kPasses; // heads per batch of loads
   const int lane = threadIdx.x & 31;
-  const int hl = lane & 15;
-  const int half = lane >> 4;
+  const int gl = lane % R;        // lane within the row group
+  const int grp = lane / R;
   const long long warp0 = ((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const long long nwarps = ((long long)gridDim.x * blockDim.x) >> 5;
   const long long total = p.tokens_q + 2 * p.tokens_k;
-
-  float4 wlo[2], whi[2];
-#pragma unroll
-  for (int t = 0; t < 2; ++t) {
-    const float* w = p.w[t];
-    wlo[t] = w ? *reinterpret_cast<const float4*>(w + 4 * hl) : make_float4(1.f, 1.f, 1.f, 1.f);
-    whi[t] = w ? *reinterpret_cast<const float4*>(w + 64 + 4 * hl) : make_float4(1.f, 1.f, 1.f, 1.f);
-  }
 
   for (long long item = warp0; item < total; item += nwarps) {
     int t;
@@ -111,57 +131,73 @@ __global__ void __launch_bounds__(256) prologue_kernel(const PrologueParams p) {
     const int b = (int)(tok / S);
     const int s = (int)(tok - (long long)b * S);
     const Tin* src = reinterpret_cast<const Tin*>(p.in[t]) + (long long)b * p.sb[t] +
-                     (long long)s * p.ss[t];
+                     (long long)s * p.ss[t] + E * gl;
     const long long sh = p.sh[t];
-    uint2* dst = reinterpret_cast<uint2*>(p.out[t]);
+    char* dst = reinterpret_cast<char*>(p.out[t]);
     const bool norm = (p.norm_mask >> t) & 1u;
     const bool rope = (p.freqs != nullptr) && t < 2;
-    const float4 w_lo = t == 1 ? wlo[1] : wlo[0];
-    const float4 w_hi = t == 1 ? whi[1] : whi[0];
 
-    float4 f[4];
-    if (rope) {
-      const float4* fr = reinterpret_cast<const float4*>(p.freqs + (long long)s * 256) + 4 * hl;
+    float wl[E], wh[E];
+    {
+      const float* w = t < 2 ? p.w[t] : nullptr;
 #pragma unroll
-      for (int k = 0; k < 4; ++k) f[k] = __ldg(fr + k);
+      for (int e = 0; e < E; e += 4) {
+        const float4 a = (norm && w) ? __ldg(reinterpret_cast<const float4*>(w + E * gl + e))
+                                     : make_float4(1.f, 1.f, 1.f, 1.f);
+        const float4 c = (norm && w) ? __ldg(reinterpret_cast<const float4*>(w + 64 + E * gl + e))
+                                     : make_float4(1.f, 1.f, 1.f, 1.f);
+        wl[e] = a.x; wl[e + 1] = a.y; wl[e + 2] = a.z; wl[e + 3] = a.w;
+        wh[e] = c.x; wh[e + 1] = c.y; wh[e + 2] = c.z; wh[e + 3] = c.w;
+      }
+    }
+    float4 f[E];
+    if (rope) {
+      const float4* fr = reinterpret_cast<const float4*>(p.freqs + (long long)s * 256) + E * gl;
+#pragma unroll
+      for (int k = 0; k < E; ++k) f[k] = __ldg(fr + k);
     }
 
-    for (int h0 = 0; h0 < p.H; h0 += 2 * kPairsInFlight) {
-      float4 lo[kPairsInFlight], hi[kPairsInFlight];
+    for (int h0 = 0; h0 < p.H; h0 += HB) {
+      uint4 lo[kPasses], hi[kPasses];
 #pragma unroll
-      for (int u = 0; u < kPairsInFlight; ++u) {
-        const int h = h0 + 2 * u + half;
+      for (int u = 0; u < kPasses; ++u) {
+        const int h = h0 + G * u + grp;
         if (h < p.H) {
           const Tin* row = src + (long long)h * sh;
-          lo[u] = load4<Tin>(row + 4 * hl);
-          hi[u] = load4<Tin>(row + 64 + 4 * hl);
+          lo[u] = load16<Tin>(row);
+          hi[u] = load16<Tin>(row + 64);
         } else {
-          lo[u] = hi[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+          lo[u] = hi[u] = make_uint4(0u, 0u, 0u, 0u);
         }
       }
 #pragma unroll
-      for (int u = 0; u < kPairsInFlight; ++u) {
-        const int h = h0 + 2 * u + half;
-        float4 a = lo[u], c = hi[u];
+      for (int u = 0; u < kPasses; ++u) {
+        const int h = h0 + G * u + grp;
+        float a[E], c[E];
+        widen<Tin>(lo[u], a);
+        widen<Tin>(hi[u], c);
         if (norm) {
-          float ss = a.x * a.x + a.y * a.y + a.z * a.z + a.w * a.w + c.x * c.x + c.y * c.y +
-                     c.z * c.z + c.w * c.w;
+          float ss = 0.f;
 #pragma unroll
-          for (int o = 8; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+          for (int e = 0; e < E; ++e) ss += a[e] * a[e] + c[e] * c[e];
+#pragma unroll
+          for (int o = R / 2; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
           const float inv = 1.0f / sqrtf(ss / 128.0f + p.eps);
-          a = scale4(a, inv, w_lo);
-          c = scale4(c, inv, w_hi);
+          // x * inv * w with both products rounded (the reference's order)
+#pragma unroll
+          for (int e = 0; e < E; ++e) {
+            a[e] = __fmul_rn(__fmul_rn(a[e], inv), wl[e]);
+            c[e] = __fmul_rn(__fmul_rn(c[e], inv), wh[e]);
+          }
         }
         if (rope) {
-          rot(a.x, c.x, f[0]);
-          rot(a.y, c.y, f[1]);
-          rot(a.z, c.z, f[2]);
-          rot(a.w, c.w, f[3]);
+#pragma unroll
+          for (int e = 0; e < E; ++e) rot(a[e], c[e], f[e]);
         }
         if (h < p.H) {
-          const long long orow = (((long long)b * p.H + h) * S + s) * 32;  // 8-byte units
-          dst[orow + hl] = make_uint2(pack_op<kOp>(a.x, a.y), pack_op<kOp>(a.z, a.w));
-          dst[orow + 16 + hl] = make_uint2(pack_op<kOp>(c.x, c.y), pack_op<kOp>(c.z, c.w));
+          char* orow = dst + ((((long long)b * p.H + h) * S + s) * 128 + E * gl) * 2;
+          store_op<E, kOp>(orow, a);
+          store_op<E, kOp>(orow + 128, c);
         }
       }
     }
@@ -236,9 +272,10 @@ int prologue_launch(const AnimaPrologueArgs* a, int sm_count, cudaStream_t st) {
   const void* in3[3] = {a->q, a->k, a->v};
   PrologueParams prm;
   for (int t = 0; t < 3; ++t) {
+    const int vec = 16 / esz;  // elements per 16-byte load
     for (int d = 0; d < 3; ++d)
-      if (st3[t][d] < 0 || (st3[t][d] % 4) != 0) return ANIMA_ERR_ARG;  // 4-element loads
-    if ((reinterpret_cast<uintptr_t>(in3[t]) % (4 * esz)) != 0) return ANIMA_ERR_ARG;
+      if (st3[t][d] < 0 || (st3[t][d] % vec) != 0) return ANIMA_ERR_ARG;
+    if ((reinterpret_cast<uintptr_t>(in3[t]) & 15u) != 0) return ANIMA_ERR_ARG;
     prm.in[t] = in3[t];
     prm.sb[t] = st3[t][0];
     prm.ss[t] = st3[t][1];

@@ -151,6 +151,30 @@ def test_prologue_matches_oracle_to_operand_rounding(aa, O):
         assert np.all(np.abs(g - ref) <= np.abs(ref) * 2.0 ** -10 + 1e-6)
 
 
+@pytest.mark.parametrize("in_dtype", ["f16", "bf16"])
+@pytest.mark.parametrize("H", [2, 6, 16])
+def test_prologue_16bit_strided_views(aa, O, in_dtype, H):
+    """16-bit projections read as strided views of one [B, S, 3, H, 128] GEMM output
+    (the DiT's fused QKV projection), H not a multiple of the heads one pass covers."""
+    rng = np.random.default_rng(30 + H)
+    B, side = 2, 8
+    S = side * side
+    dt = torch.float16 if in_dtype == "f16" else torch.bfloat16
+    qkv = torch.from_numpy(rng.standard_normal((B, S, 3, H, 128), dtype=np.float32)).to(dt)
+    x = qkv.float().numpy()  # the values the kernel reads
+    qw = (1 + 0.1 * rng.standard_normal(128)).astype(np.float32)
+    kw = (1 + 0.1 * rng.standard_normal(128)).astype(np.float32)
+    fr = O.rope_freqs_3d(1, side, side)
+    d = qkv.cuda()
+    qh, kh, vh = aa.prologue(d[:, :, 0], d[:, :, 1], d[:, :, 2], _dev(qw), _dev(kw), _dev(fr),
+                             op_dtype=torch.float16)
+    torch.cuda.synchronize()
+    rq, rk, rv = O.prologue(*(np.ascontiguousarray(x[:, :, i]) for i in range(3)), qw, kw, fr)
+    for got, ref in ((qh, rq), (kh, rk), (vh, rv)):
+        g = got.float().cpu().numpy().reshape(ref.shape)
+        assert np.all(np.abs(g - ref) <= np.abs(ref) * 2.0 ** -10 + 1e-6)
+
+
 def test_masked_cross_attention(aa, O):
     rng = np.random.default_rng(21)
     B, H, Sq, Skv = 6, 2, 200, 512
