@@ -335,26 +335,35 @@ __global__ void __launch_bounds__(kThreads, 1)
       constexpr uint32_t ab = kOp == ANIMA_DTYPE_BF16 ? 1u : 0u;  // idesc: 0 f16, 1 bf16
       constexpr uint32_t idesc_qk = make_idesc_f16(ab, kBM, kBN, 0);
       constexpr uint32_t idesc_pv = make_idesc_f16(ab, kBM, kD, 1);
-      const uint32_t q_base = smem_u32(sm.q[0]);    // tile i at + i * kTile
-      const uint32_t kv_base = smem_u32(sm.kv[0]);  // slot s at + s * kTile
+      // Descriptors are built once; per MMA only the start address moves (desc_plus).
+      // K-step kk of a K-major tile starts at panel kk / 4, 32 bytes per step inside it;
+      // of the MN-major V tile at row 16 * kk (2 KiB per step).
+      const uint64_t dk0 = sdesc_sw128(smem_u32(sm.kv[0]), 16, 1024);      // K, slot 0
+      const uint64_t dv0 = sdesc_sw128(smem_u32(sm.kv[0]), kPanel, 1024);  // V, slot 0
+      uint64_t dq[kNT][8];  // Q tile i, step kk: fixed for the whole kernel
+#pragma unroll
+      for (int i = 0; i < kNT; ++i)
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk)
+          dq[i][kk] = sdesc_sw128(smem_u32(sm.q[i]) + (kk >> 2) * kPanel + (kk & 3) * 32, 16, 1024);
 
       auto issue_qk = [&](int i, int slot) {
-        const uint32_t d = tmem + i * 128;
+        const uint64_t kb = desc_plus(dk0, (uint32_t)slot * kTile);
+        uint64_t b[8];
 #pragma unroll
-        for (int kk = 0; kk < kD / 16; ++kk) {
-          const uint32_t off = (kk >> 2) * kPanel + (kk & 3) * 32;
-          umma_ss(d, sdesc_sw128(q_base + i * kTile + off, 16, 1024),
-                  sdesc_sw128(kv_base + slot * kTile + off, 16, 1024), idesc_qk, kk > 0);
-        }
+        for (int kk = 0; kk < 8; ++kk) b[kk] = desc_plus(kb, (kk >> 2) * kPanel + (kk & 3) * 32);
+        umma_ss_x8(tmem + i * 128, dq[i], b, idesc_qk, 0u);
       };
       auto issue_pv = [&](int i, int slot, bool acc) {
-        const uint32_t d = tmem + 256 + i * 128;
-        const uint32_t a = tmem + i * 128;
+        const uint64_t vb = desc_plus(dv0, (uint32_t)slot * kTile);
+        uint64_t b[8];
+        uint32_t a[8];
 #pragma unroll
-        for (int kk = 0; kk < kBN / 16; ++kk) {
-          umma_ts(d, a + kk * 8, sdesc_sw128(kv_base + slot * kTile + kk * 2048, kPanel, 1024),
-                  idesc_pv, (acc || kk > 0) ? 1u : 0u);
+        for (int kk = 0; kk < 8; ++kk) {
+          b[kk] = desc_plus(vb, kk * 2048);
+          a[kk] = tmem + i * 128 + kk * 8;  // P_i, 16 keys (8 columns) per step
         }
+        umma_ts_x8(tmem + 256 + i * 128, a, b, idesc_pv, acc ? 1u : 0u);
       };
       auto wait = [&](uint64_t* bar, uint32_t parity) {
         return mbar_wait(bar, parity, abort, p.status, ANIMA_ERR_TIMEOUT);

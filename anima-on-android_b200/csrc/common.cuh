@@ -170,6 +170,54 @@ __device__ __forceinline__ void umma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64
       : "memory");
 }
 
+// Eight chained MMAs D (+)= A_k * B_k, k = 0..7 (one 128-deep K block in 16-deep steps),
+// issued from one asm block: the first accumulates iff acc0 != 0, the rest always do.
+// A single issuing thread shares its SM sub-partition with busy softmax warps, so the
+// per-MMA instruction count is what bounds the issue rate; here it is one MMA plus the
+// caller's descriptor adds.
+__device__ __forceinline__ void umma_ss_x8(uint32_t d, const uint64_t (&a)[8],
+                                           const uint64_t (&b)[8], uint32_t idesc,
+                                           uint32_t acc0) {
+  asm volatile(
+      "{\n\t.reg .pred p0, p1;\n\t"
+      "setp.ne.b32 p0, %18, 0;\n\t"
+      "setp.eq.b32 p1, %18, %18;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %9, %17, p0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %2, %10, %17, p1;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %3, %11, %17, p1;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %4, %12, %17, p1;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %5, %13, %17, p1;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %6, %14, %17, p1;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %7, %15, %17, p1;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %8, %16, %17, p1;\n\t}" ::"r"(d),
+      "l"(a[0]), "l"(a[1]), "l"(a[2]), "l"(a[3]), "l"(a[4]), "l"(a[5]), "l"(a[6]), "l"(a[7]),
+      "l"(b[0]), "l"(b[1]), "l"(b[2]), "l"(b[3]), "l"(b[4]), "l"(b[5]), "l"(b[6]), "l"(b[7]),
+      "r"(idesc), "r"(acc0)
+      : "memory");
+}
+
+// As umma_ss_x8 with A read from tensor memory at a[k].
+__device__ __forceinline__ void umma_ts_x8(uint32_t d, const uint32_t (&a)[8],
+                                           const uint64_t (&b)[8], uint32_t idesc,
+                                           uint32_t acc0) {
+  asm volatile(
+      "{\n\t.reg .pred p0, p1;\n\t"
+      "setp.ne.b32 p0, %18, 0;\n\t"
+      "setp.eq.b32 p1, %18, %18;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %9, %17, p0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%2], %10, %17, p1;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%3], %11, %17, p1;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%4], %12, %17, p1;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%5], %13, %17, p1;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%6], %14, %17, p1;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%7], %15, %17, p1;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%8], %16, %17, p1;\n\t}" ::"r"(d),
+      "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(a[4]), "r"(a[5]), "r"(a[6]), "r"(a[7]),
+      "l"(b[0]), "l"(b[1]), "l"(b[2]), "l"(b[3]), "l"(b[4]), "l"(b[5]), "l"(b[6]), "l"(b[7]),
+      "r"(idesc), "r"(acc0)
+      : "memory");
+}
+
 // Arrive once on `bar` when every tcgen05 operation issued so far by this thread is done.
 __device__ __forceinline__ void umma_commit(uint64_t* bar) {
   asm volatile(
@@ -201,6 +249,18 @@ __device__ __forceinline__ uint64_t sdesc_sw128(uint32_t saddr, uint32_t lbo_byt
   d |= 1ull << 46;  // descriptor version (sm_100)
   d |= 2ull << 61;  // SWIZZLE_128B
   return d;
+}
+
+// A descriptor moved by `bytes` (a multiple of 16).  The start-address field holds
+// address >> 4 in bits [0, 14); shared-memory addresses stay below 256 KB, so the add
+// never carries out of the field and one 32-bit add of the low word suffices.
+__device__ __forceinline__ uint64_t desc_plus(uint64_t d, uint32_t bytes) {
+  uint32_t lo, hi;
+  asm("mov.b64 {%0, %1}, %2;" : "=r"(lo), "=r"(hi) : "l"(d));
+  lo += bytes >> 4;
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "r"(lo), "r"(hi));
+  return r;
 }
 
 __device__ __forceinline__ float ex2_approx(float x) {

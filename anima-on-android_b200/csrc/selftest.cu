@@ -12,10 +12,8 @@ namespace anima {
 
 __global__ void selftest_wait_kernel(int* status, unsigned long long limit_ns) {
   __shared__ uint64_t bar;
-  __shared__ int abort_flag;
   if (threadIdx.x == 0) {
     mbar_init(&bar, 1);  // expects one arrival that never comes
-    abort_flag = 0;
     fence_barrier_init();
   }
   __syncthreads();
@@ -23,7 +21,6 @@ __global__ void selftest_wait_kernel(int* status, unsigned long long limit_ns) {
     const unsigned long long t0 = globaltimer_ns();
     while (!mbar_try_wait(&bar, 0)) {
       if (globaltimer_ns() - t0 > limit_ns) {
-        abort_flag = 1;
         atomicCAS(status, 0, ANIMA_ERR_TIMEOUT);
         break;
       }
