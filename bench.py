@@ -305,10 +305,13 @@ def run_dit(args, rank, world, local_rank):
                                f"16x{side}x{side} ({L} tokens), context 512x1024, CFG pair",
                    "global_batch": 2, "seq_len": L, "parallelism": f"heads{world}",
                    "heads_per_gpu": 16 // world, "tflops_per_gpu": round(fl / world / (ms * 1e-3) / 1e12, 1),
+                   "l2": "weights (4 GB fp16) exceed L2 every step",
                    "model_tflop_per_step": round(fl / 1e12, 2)},
         "e2e": {"value": round(e2e_ms, 3), "unit": "ms", "h2d_bytes_per_step": (hx.numel() + hcc.numel() + hcu.numel()) * 4,
                 "d2h_bytes_per_step": hout.numel() * 4},
-        "gpu_launches": args.steps * args.blocks * 4,
+        # library kernels per step: per block 2 prologues, 2 attentions, 3 LayerNorm+
+        # modulation passes, 3 gated residuals; plus the final layer's modulation
+        "gpu_launches": args.steps * (args.blocks * 10 + 1),
         "clocks": clocks.summary(t_begin, t_end),
     }
 
