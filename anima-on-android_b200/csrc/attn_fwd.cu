@@ -481,54 +481,50 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         tc_fence_after();
         uint32_t r[4][32];
-#pragma unroll
-        for (int c = 0; c < 4; ++c) tmem_ld32(tS + c * 32, r[c]);
-        tmem_ld_wait();
-
         int lim = kv_len - j * kBN;
         if (causal) lim = min(lim, grow - j * kBN + 1);
         const bool full = lim >= kBN;
-        if (!full) {
+        // S row from tensor memory; columns >= lim (padding, causal) become -inf.
+        auto load_s = [&]() {
 #pragma unroll
-          for (int c = 0; c < 4; ++c)
+          for (int c = 0; c < 4; ++c) tmem_ld32(tS + c * 32, r[c]);
+          tmem_ld_wait();
+          if (!full) {
 #pragma unroll
-            for (int e = 0; e < 32; ++e)
-              if (c * 32 + e >= lim) r[c][e] = __float_as_uint(-INFINITY);
-        }
+            for (int c = 0; c < 4; ++c)
+#pragma unroll
+              for (int e = 0; e < 32; ++e)
+                if (c * 32 + e >= lim) r[c][e] = __float_as_uint(-INFINITY);
+          }
+        };
 #define SV(e) __uint_as_float(r[(e) >> 5][(e) & 31])
         // Row max: 8 independent 3-input-max chains, then a small tree.
-        float acc[8];
+        auto row_max = [&]() {
+          float acc[8];
 #pragma unroll
-        for (int k = 0; k < 8; ++k) acc[k] = fmaxf(SV(2 * k), SV(2 * k + 1));
+          for (int k = 0; k < 8; ++k) acc[k] = fmaxf(SV(2 * k), SV(2 * k + 1));
 #pragma unroll
-        for (int e = 16; e < 128; e += 16)
+          for (int e = 16; e < 128; e += 16)
 #pragma unroll
-          for (int k = 0; k < 8; ++k) acc[k] = max3f(acc[k], SV(e + 2 * k), SV(e + 2 * k + 1));
-        const float mx = max3f(max3f(acc[0], acc[1], acc[2]), max3f(acc[3], acc[4], acc[5]),
-                               fmaxf(acc[6], acc[7]));
-        const float m_tile = mx * sl2;
-        float m_use = m, alpha = 1.f;
-        if (m == -INFINITY) {
-          m_use = m_tile;
-          alpha = 0.f;
-        } else if (m_tile > m + kRescaleThreshold) {
-          m_use = m_tile;
-          alpha = ex2_approx(m - m_tile);
-        }
-        const float neg_base = (m_use == -INFINITY) ? 0.f : -m_use;
-        const uint64_t scale2 = f2pack(sl2, sl2), base2 = f2pack(neg_base, neg_base);
+            for (int k = 0; k < 8; ++k) acc[k] = max3f(acc[k], SV(e + 2 * k), SV(e + 2 * k + 1));
+          return max3f(max3f(acc[0], acc[1], acc[2]), max3f(acc[3], acc[4], acc[5]),
+                       fmaxf(acc[6], acc[7]));
+        };
         uint64_t sum2[4];
-#pragma unroll
-        for (int k = 0; k < 4; ++k) sum2[k] = 0ull;
-        // P = 2^(s*scale*log2e - m): pairs of columns through the packed FMA pipe; in full
-        // tiles kPolyPer8 of every 8 pairs take the polynomial exp2, the rest MUFU ex2.
         uint32_t pk[2][32];
-        if (full) {
+        // P = 2^(s*scale*log2e - mu) for pairs of columns through the packed FMA pipe, the
+        // row sum and the 16-bit pack, in one pass that consumes r.  In full tiles
+        // kPolyPer8 of every 8 pairs take the polynomial exp2, the rest MUFU ex2.
+        auto exp_pass = [&](float mu) {
+          const float nb = (mu == -INFINITY) ? 0.f : -mu;
+          const uint64_t scale2 = f2pack(sl2, sl2), base2 = f2pack(nb, nb);
+#pragma unroll
+          for (int k = 0; k < 4; ++k) sum2[k] = 0ull;
 #pragma unroll
           for (int pr = 0; pr < 64; ++pr) {
             float x0, x1;
             f2unpack(fma2(f2pack(SV(2 * pr), SV(2 * pr + 1)), scale2, base2), x0, x1);
-            if ((pr & 7) < kPolyPer8) {
+            if (full && (pr & 7) < kPolyPer8) {
               exp2_poly_pair(x0, x1);
             } else {
               x0 = ex2_approx(x0);
@@ -537,23 +533,49 @@ __global__ void __launch_bounds__(kThreads, 1)
             sum2[pr & 3] = add2(sum2[pr & 3], f2pack(x0, x1));
             pk[pr >> 5][pr & 31] = pack2<kOp>(x0, x1);
           }
+        };
+        auto row_sum = [&]() {
+          float sa, sb;
+          f2unpack(add2(add2(sum2[0], sum2[1]), add2(sum2[2], sum2[3])), sa, sb);
+          return sa + sb;
+        };
+        // Online softmax with a lazy rescale: the max used for P (m_use) moves only when
+        // the tile's row max exceeds it by more than kRescaleThreshold.
+        //  * first tile of a segment: row max first, then P;
+        //  * later tiles: P with the running max m straight away.  The row sum, computed
+        //    anyway, certifies it: sum <= 2^kRescaleThreshold means every P <= 2^8, so the
+        //    tile max is within the threshold and m stays.  Otherwise (rare once the running
+        //    max has settled) the warp reloads S, takes the exact max and redoes the pass
+        //    with the max the lazy rule picks.  This removes the row-max pass from the
+        //    steady-state critical path.
+        load_s();
+        float m_use = m, alpha = 1.f, sum;
+        if (jj == 0) {
+          m_use = row_max() * sl2;
+          alpha = 0.f;  // nothing accumulated yet
+          exp_pass(m_use);
+          sum = row_sum();
         } else {
-#pragma unroll
-          for (int pr = 0; pr < 64; ++pr) {
-            float x0, x1;
-            f2unpack(fma2(f2pack(SV(2 * pr), SV(2 * pr + 1)), scale2, base2), x0, x1);
-            x0 = ex2_approx(x0);
-            x1 = ex2_approx(x1);
-            sum2[pr & 3] = add2(sum2[pr & 3], f2pack(x0, x1));
-            pk[pr >> 5][pr & 31] = pack2<kOp>(x0, x1);
+          exp_pass(m);
+          sum = row_sum();
+          const bool check = !(sum <= 256.f) || (m == -INFINITY && sum > 0.f);
+          if (__any_sync(0xffffffffu, check)) {
+            load_s();
+            const float m_tile = row_max() * sl2;
+            if (m == -INFINITY) {
+              m_use = m_tile;
+              alpha = 0.f;
+            } else if (m_tile > m + kRescaleThreshold) {
+              m_use = m_tile;
+              alpha = ex2_approx(m - m_tile);
+            }
+            exp_pass(m_use);
+            sum = row_sum();
           }
         }
         tmem_st32(tS, pk[0]);
         tmem_st32(tS + 32, pk[1]);
 #undef SV
-        float sa, sb;
-        f2unpack(add2(add2(sum2[0], sum2[1]), add2(sum2[2], sum2[3])), sa, sb);
-        const float sum = sa + sb;
         l = l * alpha + sum;
         if (__any_sync(0xffffffffu, jj > 0 && alpha != 1.f)) {
 #pragma unroll 1
