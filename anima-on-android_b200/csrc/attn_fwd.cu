@@ -6,7 +6,8 @@
 //
 // Work unit = 256 query rows (two 128-row tiles) of one (batch, head) against its keys,
 // streamed in 128-key tiles.  Two schedules share one kernel:
-//   unit mode    one CTA per unit (masked / causal calls, or at most one wave);
+//   unit mode    one CTA per unit (masked / causal calls, at most one wave, or where
+//                cutting the last round does not pay -- see plan_split);
 //   split mode   a persistent grid of one CTA per SM.  Whole units are dealt round-robin
 //                (CTA c takes units c, c+G, ...), so the CTAs in flight share heads and
 //                their K/V stay in L2; the units of the last, partial round are cut into
@@ -59,12 +60,20 @@ constexpr uint32_t kRegsSoftmax = 200;
 constexpr uint32_t kRegsControl = 104;
 constexpr uint32_t kTmemCols = 512;
 constexpr float kRescaleThreshold = 8.0f;  // log2 units
+#ifndef ANIMA_STAGGER
+#define ANIMA_STAGGER 0
+#endif
+// Cycles between the end of tile 0's first QK^T of a segment and the issue of tile 1's.
+// Issued back to back, the two tiles run one tile's MMA time (1024 cycles) apart, so
+// their softmax phases overlap and share MUFU; a larger offset can separate them.
+constexpr long long kStagger = ANIMA_STAGGER;
 #ifndef ANIMA_POLY_PER8
 #define ANIMA_POLY_PER8 0
 #endif
 // Of every 8 column pairs, how many take the FMA-pipe polynomial exp2 instead of MUFU.
-// 0 by default: on this kernel the tensor pipe is bounded by shared-memory operand
-// bandwidth, not by MUFU, and measured cycles were 1-5% lower with MUFU alone.
+// 0 by default: the extra softmax instructions take issue slots from the MMA and TMA
+// warps that share the SM sub-partitions and sit on the critical path; 1/8 measured 14 %
+// slower, 2/8 22 %.
 constexpr int kPolyPer8 = ANIMA_POLY_PER8;
 // One partial of a split unit: O [256][128] fp32 (unnormalised), then m [256], l [256].
 constexpr int kPartFloats = kUnitRows * kD + 2 * kUnitRows;
@@ -389,6 +398,13 @@ __global__ void __launch_bounds__(kThreads, 1)
             tc_fence_after();
             issue_qk(0, slot_of(ik));
             umma_commit(&sm.s_full[0]);
+            if (kStagger > 0 && n > 2) {
+              // Start tile 1 about half a period after tile 0 (see kStagger).
+              if (!(ok = wait(&sm.s_full[0], (uint32_t)g & 1u))) break;
+              const long long t_end = clock64() + kStagger;
+              while (clock64() < t_end) {
+              }
+            }
             issue_qk(1, slot_of(ik));
             umma_commit(&sm.s_full[1]);
             umma_commit(&sm.kv_empty[slot_of(ik)]);
@@ -784,6 +800,12 @@ static SplitPlan plan_split(int bh, int S_q, int S_kv, unsigned flags, int sm_co
   if (units <= sm_count || units > 0x7fffffffLL) return sp;  // one wave: nothing to balance
   const long long rounds = units / sm_count, tail = units - rounds * sm_count;
   if (tail == 0 || tail * n > 0x7fffffffLL) return sp;         // whole rounds only
+  // Cutting the last round costs segment set-up, partial stores and merges.  Measured
+  // (B=2, H=16): split loses 25 % at 2 waves (L=2048), 8 % at 2.6, breaks even at 3.5 and
+  // gains 4 % at 5.2 waves (L=6144, 13.5 % of a unit-per-CTA grid idle in its last wave),
+  // so it is the default only from four whole rounds with >= 10 % of that wave idle.
+  const bool worth = rounds >= 4 && (rounds + 1) * sm_count * 10 >= units * 11;
+  if (!(flags & ANIMA_FLAG_SPLIT) && !worth) return sp;
   sp.rounds = (int)rounds;
   sp.tail_units = (int)tail;
   sp.tail_tiles = (int)(tail * n);

@@ -344,7 +344,8 @@ def run_ours(args, rank, world, local_rank):
         if evs is not None:
             evs[1].record(stream)
         anima_attn.attention_core(qh, kh, vh, B, heads, out=out,
-                                  stream_k=(args.schedule == "auto"))
+                                  stream_k=(args.schedule == "auto"),
+                                  force_split=(args.schedule == "split"))
         if evs is not None:
             evs[2].record(stream)
 
@@ -466,9 +467,10 @@ def main():
                     help="attn: fused attention op (headline); dit: one full DiT step (config 4)")
     ap.add_argument("--blocks", type=int, default=28, help="DiT blocks (dit workload)")
     ap.add_argument("--latent", type=int, default=128, help="latent side (dit workload)")
-    ap.add_argument("--schedule", choices=["auto", "unit"], default="auto",
-                    help="auto: persistent stream-K when the call spans more than one wave; "
-                         "unit: one CTA per 256-row unit")
+    ap.add_argument("--schedule", choices=["auto", "unit", "split"], default="auto",
+                    help="auto: the library's choice (persistent split schedule only where it "
+                         "measured faster); unit: one CTA per 256-row unit; split: persistent "
+                         "split schedule for every call of more than one wave")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()

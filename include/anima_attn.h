@@ -48,6 +48,12 @@ enum { ANIMA_DTYPE_F32 = 0, ANIMA_DTYPE_BF16 = 1, ANIMA_DTYPE_F16 = 2 };
 #define ANIMA_FLAG_CAUSAL 0x10u /* top-left causal mask (col <= row)      */
 #define ANIMA_FLAG_PAIR 0x20u  /* anima_attn_fwd: run on CTA pairs (2-SM MMA), one pair per
                                   512-row unit                             */
+#define ANIMA_FLAG_SPLIT 0x40u /* anima_attn_fwd(_noalloc): use the persistent split schedule
+                                  whenever the call spans more than one wave of 256-row units.
+                                  Without it the split schedule is used only where it measured
+                                  faster than one CTA per unit: at least four whole rounds with
+                                  at least 10 % of a unit-per-CTA grid's last wave idle.
+                                  anima_attn_workspace_size takes the same flag. */
 
 /*
  * Prologue: per-head RMSNorm + RoPE + cast, one HBM pass.

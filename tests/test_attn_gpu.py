@@ -193,8 +193,8 @@ def test_masked_cross_attention(aa, O):
 
 @pytest.mark.parametrize("Sq,Skv", [(1300, 700), (4000, 3000), (1280, 128), (4096, 4096)])
 def test_stream_k_schedule_matches_unit_schedule_and_oracle(aa, O, Sq, Skv):
-    """More than one wave of 256-row units (B*H*ceil(Sq/256) > 148 SMs) runs the
-    persistent split schedule: whole units round-robin, the last round cut into key-tile
+    """More than one wave of 256-row units (B*H*ceil(Sq/256) > 148 SMs), with
+    ANIMA_FLAG_SPLIT, runs the persistent split schedule: whole units round-robin, the last round cut into key-tile
     slices merged in-kernel.  Ragged Sq/Skv exercise partial query units and partial key
     tiles; (1280, 128) has one-tile units (nothing to cut); (4096, 4096) is the bench
     shape, whose 68 last-round units are each cut across about three CTAs."""
@@ -204,9 +204,9 @@ def test_stream_k_schedule_matches_unit_schedule_and_oracle(aa, O, Sq, Skv):
     q = rng.standard_normal((B * H, Sq, 128), dtype=np.float32)
     k = rng.standard_normal((B * H, Skv, 128), dtype=np.float32)
     v = rng.standard_normal((B * H, Skv, 128), dtype=np.float32)
-    assert L.lib.anima_attn_workspace_size(B, H, Sq, Skv, 0) > 0
+    assert L.lib.anima_attn_workspace_size(B, H, Sq, Skv, L.FLAG_SPLIT) > 0
     qh, kh, vh = (_dev(t).to(torch.bfloat16) for t in (q, k, v))
-    split = aa.attention_core(qh, kh, vh, B, H, out_layout="bhsd", stream_k=True)
+    split = aa.attention_core(qh, kh, vh, B, H, out_layout="bhsd", force_split=True)
     unit = aa.attention_core(qh, kh, vh, B, H, out_layout="bhsd", stream_k=False)
     torch.cuda.synchronize()
     assert aa.status() == 0

@@ -23,7 +23,7 @@ pytestmark = pytest.mark.gpu
 torch = pytest.importorskip("torch")
 
 
-def _args(L, q, k, v, out, B, H, Sq, Skv, workspace=None):
+def _args(L, q, k, v, out, B, H, Sq, Skv, workspace=None, flags=0):
     a = L.AttnArgs()
     a.q, a.k, a.v = q.data_ptr(), k.data_ptr(), v.data_ptr()
     a.op_dtype = L.DTYPE_BF16
@@ -32,15 +32,15 @@ def _args(L, q, k, v, out, B, H, Sq, Skv, workspace=None):
     a.out_stride[:] = [out.stride(0), out.stride(2), out.stride(1)]  # [B, S, H, D]
     a.B, a.H, a.S_q, a.S_kv, a.D = B, H, Sq, Skv, 128
     a.scale = 1.0 / math.sqrt(128)
-    a.flags = 0
+    a.flags = flags
     a.kv_valid_len = None
     a.workspace = None if workspace is None else workspace.data_ptr()
     a.workspace_bytes = 0 if workspace is None else workspace.numel()
     return a
 
 
-# (4096, 4096) and (1300, 700) run the split schedule (they use the scratch); (512, 384)
-# fits in one wave and uses none.
+# With ANIMA_FLAG_SPLIT, (4096, 4096) and (1300, 700) run the split schedule (they use the
+# scratch); (512, 384) fits in one wave and uses none.
 @pytest.mark.parametrize("Sq,Skv", [(4096, 4096), (1300, 700), (512, 384)])
 def test_noalloc_entry_matches_workspace_entry_twice(Sq, Skv):
     from anima_attn import _lib as L
@@ -52,16 +52,17 @@ def test_noalloc_entry_matches_workspace_entry_twice(Sq, Skv):
     v = torch.randn(B * H, Skv, 128, device="cuda", generator=g).to(torch.bfloat16)
     stream = ct.c_void_p(torch.cuda.current_stream().cuda_stream)
 
-    need = int(L.lib.anima_attn_workspace_size(B, H, Sq, Skv, 0))
+    flags = L.FLAG_SPLIT
+    need = int(L.lib.anima_attn_workspace_size(B, H, Sq, Skv, flags))
     ws = torch.zeros(max(need, 1), dtype=torch.uint8, device="cuda")
     ref = torch.empty(B, Sq, H, 128, device="cuda")
-    a = _args(L, q, k, v, ref, B, H, Sq, Skv, ws if need else None)
+    a = _args(L, q, k, v, ref, B, H, Sq, Skv, ws if need else None, flags)
     assert L.lib.anima_attn_fwd(ct.byref(a), stream) == L.OK, L.last_error()
 
     outs = []
     for _ in range(2):
         out = torch.full((B, Sq, H, 128), float("nan"), device="cuda")
-        a = _args(L, q, k, v, out, B, H, Sq, Skv)
+        a = _args(L, q, k, v, out, B, H, Sq, Skv, flags=flags)
         assert L.lib.anima_attn_fwd_noalloc(ct.byref(a), stream) == L.OK, L.last_error()
         outs.append(out)
     torch.cuda.synchronize()
