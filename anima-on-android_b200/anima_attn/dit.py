@@ -22,12 +22,21 @@ keeps the step's latent within 1.1e-3 rel-L2 of the fp32 reference model at 2 bl
 where bf16 operands give 8.5e-3.  The attention runs on fp16 operands for the same
 reason (q and k are RMS-normalised; v is a projection of normalised activations).
 
-Head parallelism: rank r of N owns heads [r*16/N, (r+1)*16/N).  It projects q/k/v for
-those heads only, runs their attention, and one all_gather_into_tensor per attention
-(self and cross) collects every rank's head outputs before the replicated o-proj.  The
-o-proj consumes the gathered chunks directly (one GEMM per rank's column block of the
-o-proj weight, accumulated), so no transpose copy is needed.  Everything else (adaLN,
-LayerNorm, MLP, final layer) is replicated.
+Multi-GPU (N ranks; the attention is split by heads in both modes, rank r owning heads
+[r*16/N, (r+1)*16/N)):
+  shard="heads"   the layout the north star describes: every rank holds the whole residual
+                  stream, projects q/k/v for its heads only, runs their attention, and one
+                  all_gather_into_tensor per attention collects every rank's head outputs
+                  before the o-proj.  o-proj, MLP, adaLN and final layer are replicated, so
+                  only the attention's share of the step shrinks with N.
+  shard="tokens"  (default) the same head-parallel attention, with everything else split by
+                  tokens (sequence parallelism): rank r owns rows [r*R/N, (r+1)*R/N) of the
+                  R = B*L token rows.  It projects q/k/v for all heads on its rows, one
+                  all_to_all_single hands every rank its heads for all rows, attention runs
+                  per head, and a second all_to_all_single returns all heads' outputs for its
+                  own rows before the o-proj -- the part of the all-gather a rank uses.  The
+                  o-proj, MLP, LayerNorm/adaLN passes and final layer run on its rows only.
+                  Cross-attention K/V come from the (replicated, 512-token) context.
 
 Weights follow the reference's parameter names (state-dict keys of MiniTrainDIT with
 use_adaln_lora=True), so the same seeded weights load into the reference model for the
@@ -154,29 +163,45 @@ class AnimaDiT:
     """
 
     def __init__(self, cfg: DiTConfig, weights: Dict[str, torch.Tensor], rank: int = 0,
-                 world: int = 1, group=None, attn_fn: Optional[AttnFn] = None):
+                 world: int = 1, group=None, attn_fn: Optional[AttnFn] = None,
+                 shard: str = "tokens"):
         if cfg.heads % world:
             raise ValueError("heads must divide evenly over ranks")
+        if shard not in ("tokens", "heads"):
+            raise ValueError("shard must be 'tokens' or 'heads'")
         self.cfg, self.rank, self.world, self.group = cfg, rank, world, group
+        self.seq = shard == "tokens" and world > 1
         self.h_local = cfg.heads // world
         self.w = {}
-        lo = rank * self.h_local * cfg.head_dim
-        hi = lo + self.h_local * cfg.head_dim
+        cols = self.h_local * cfg.head_dim
+        lo, hi = rank * cols, (rank + 1) * cols
         for name, t in weights.items():
-            if any(name.endswith(f".{p}_proj.weight") for p in ("q", "k", "v")):
-                t = t[lo:hi].contiguous()  # this rank's heads (output rows)
             if t.dtype == torch.bfloat16:
                 t = t.to(cfg.gemm_dtype)  # GEMM operand type
             self.w[name] = t
         # One GEMM per input: self-attention [Wq; Wk; Wv] on x, cross-attention [Wk; Wv]
         # on the context.  The prologue reads q/k/v as strided views of its output.
+        #  heads mode: only this rank's heads ([3*cols, D] and [2*cols, ctx]).
+        #  tokens mode: self-attention and cross q for every head, grouped by owning rank
+        #  ([N, 3*cols, D] and [N, cols, D]) so one batched GEMM writes the all-to-all's
+        #  send buffer; cross k/v for this rank's heads only.
+        N = world
         for b in range(cfg.blocks):
             p = f"blocks.{b}."
             sa, ca = p + "self_attn.", p + "cross_attn."
-            if sa + "q_proj.weight" in self.w:
-                self.w[sa + "qkv"] = torch.cat([self.w.pop(sa + f"{c}_proj.weight") for c in "qkv"])
-            if ca + "k_proj.weight" in self.w:
-                self.w[ca + "kv"] = torch.cat([self.w.pop(ca + f"{c}_proj.weight") for c in "kv"])
+            if sa + "q_proj.weight" not in self.w:
+                continue
+            wq, wk, wv = (self.w.pop(sa + f"{c}_proj.weight") for c in "qkv")
+            if self.seq:
+                D = wq.shape[1]
+                self.w[sa + "qkv"] = torch.cat([t.view(N, cols, D) for t in (wq, wk, wv)], 1).contiguous()
+                cq = self.w.pop(ca + "q_proj.weight")
+                self.w[ca + "q_by_rank"] = cq.view(N, cols, cq.shape[1]).contiguous()
+            else:
+                self.w[sa + "qkv"] = torch.cat([wq[lo:hi], wk[lo:hi], wv[lo:hi]]).contiguous()
+                self.w[ca + "q_proj.weight"] = self.w[ca + "q_proj.weight"][lo:hi].contiguous()
+            ck, cv = (self.w.pop(ca + f"{c}_proj.weight") for c in "kv")
+            self.w[ca + "kv"] = torch.cat([ck[lo:hi], cv[lo:hi]]).contiguous()
         if attn_fn is None:
             from .ops import attention as attn_fn
         self.attn_fn = attn_fn
@@ -208,6 +233,87 @@ class AnimaDiT:
             return gate_residual_(x, gate, y)
         return x + gate * y
 
+    # ---------------------------------------------------------- tokens mode (rows)
+    def _segments(self, lo: int, hi: int, L: int):
+        """Pieces (start, end, sample) of global rows [lo, hi), one sample each, with
+        start/end relative to lo."""
+        segs, r = [], lo
+        while r < hi:
+            b = r // L
+            e = min(hi, (b + 1) * L)
+            segs.append((r - lo, e - lo, b))
+            r = e
+        return segs
+
+    def _ln_mod_rows(self, x, scale, shift, segs):
+        """_ln_mod on local rows x [n, D] whose samples are given by segs."""
+        parts = [self._ln_mod(x[s0:s1].unsqueeze(0), scale[b:b + 1], shift[b:b + 1])[0]
+                 for s0, s1, b in segs]
+        return parts[0] if len(parts) == 1 else torch.cat(parts)
+
+    def _gate_add_rows(self, x, gate, y, segs):
+        """x += gate[sample] * y on local rows; in place on CUDA."""
+        if x.is_cuda:
+            for s0, s1, b in segs:
+                self._gate_add(x[s0:s1].unsqueeze(0), gate[b:b + 1], y[s0:s1].unsqueeze(0))
+            return x
+        return torch.cat([x[s0:s1] + gate[b, 0] * y[s0:s1] for s0, s1, b in segs])
+
+    def _by_rank_linear(self, h, w):
+        """h [n, K] @ w[r]^T for every rank r -> [N, n, M] (the all-to-all send buffer)."""
+        if h.is_cuda:
+            return torch.matmul(h.to(w.dtype), w.transpose(1, 2))
+        return (h.to(w.dtype).float() @ w.float().transpose(1, 2)).to(w.dtype)
+
+    def _a2a(self, t: torch.Tensor) -> torch.Tensor:
+        """all_to_all_single over dim 0 (destination rank in, source rank out)."""
+        import torch.distributed as dist
+        out = torch.empty_like(t)
+        dist.all_to_all_single(out, t.contiguous(), group=self.group)
+        return out
+
+    def _attention_rows(self, p, h_loc, B, L, ctx, freqs):
+        """Head-parallel attention for local token rows h_loc [n, D] -> o-proj [n, D]."""
+        cfg, N = self.cfg, self.world
+        hl, hd, dt = self.h_local, cfg.head_dim, cfg.gemm_dtype
+        n = h_loc.shape[0]
+        if ctx is None:
+            qkv = self._a2a(self._by_rank_linear(h_loc, self.w[p + ".qkv"]))  # [N, n, 3*hl*hd]
+            qkv = qkv.view(B, L, 3, hl, hd)  # rows in global order: source rank r = rows r
+            q, k, v = qkv[:, :, 0], qkv[:, :, 1], qkv[:, :, 2]
+        else:
+            q = self._a2a(self._by_rank_linear(h_loc, self.w[p + ".q_by_rank"])).view(B, L, hl, hd)
+            Skv = ctx.shape[1]
+            kv = _linear(ctx, self.w[p + ".kv"], dt).view(B, Skv, 2, hl, hd)
+            k, v = kv[:, :, 0], kv[:, :, 1]
+        o = self.attn_fn(q, k, v, self.w[p + ".q_norm.weight"], self.w[p + ".k_norm.weight"],
+                         freqs if ctx is None else None, eps=cfg.eps, out_dtype=dt, op_dtype=dt)
+        # [B, L, hl, hd] = [N, n, hl*hd] by destination rank -> [N (source heads), n, hl*hd]
+        o = self._a2a(o.reshape(N, n, hl * hd))
+        o = o.permute(1, 0, 2).reshape(n, N * hl * hd)  # my rows, heads in order
+        return _linear(o, self.w[p + ".output_proj.weight"])
+
+    def _block_rows(self, b, x, emb, lora, ctx, freqs, B, L, segs):
+        p = f"blocks.{b}."
+        w = self.w
+
+        def mods(m):
+            h = _linear(F.silu(emb), w[p + f"adaln_modulation_{m}.1.weight"])
+            return (_linear(h, w[p + f"adaln_modulation_{m}.2.weight"]) + lora).chunk(3, dim=-1)
+
+        sh_sa, sc_sa, g_sa = mods("self_attn")
+        sh_ca, sc_ca, g_ca = mods("cross_attn")
+        sh_m, sc_m, g_m = mods("mlp")
+        dt = self.cfg.gemm_dtype
+        h = self._ln_mod_rows(x, sc_sa, sh_sa, segs)
+        x = self._gate_add_rows(x, g_sa, self._attention_rows(p + "self_attn", h, B, L, None, freqs), segs)
+        h = self._ln_mod_rows(x, sc_ca, sh_ca, segs)
+        x = self._gate_add_rows(x, g_ca, self._attention_rows(p + "cross_attn", h, B, L, ctx, None), segs)
+        h = self._ln_mod_rows(x, sc_m, sh_m, segs)
+        h = _linear(F.gelu(_linear(h, w[p + "mlp.layer1.weight"], dt)), w[p + "mlp.layer2.weight"])
+        return self._gate_add_rows(x, g_m, h, segs)
+
+    # ---------------------------------------------------------- heads mode
     def _gather_oproj(self, o_local: torch.Tensor, w_o: torch.Tensor) -> torch.Tensor:
         """o_local [B, S, H/N, hd] -> o-proj of all heads [B, S, hidden] (fp32)."""
         B, S = o_local.shape[:2]
@@ -279,20 +385,38 @@ class AnimaDiT:
         # "b c (t r) (h m) (w n) -> b t h w (c r m n)"
         xp = xm.reshape(B, C + 1, Tp, pt, Hp, ps, Wp, ps).permute(0, 2, 4, 6, 1, 3, 5, 7)
         xp = xp.reshape(B, Tp * Hp * Wp, (C + 1) * pt * ps * ps)
-        h = _linear(xp, w["x_embedder.proj.1.weight"])  # [B, L, hidden]
         freqs = self._rope(Tp, Hp, Wp, x.device)
         sample = timestep_sinusoid(timesteps, cfg.hidden)  # [B, 1, hidden]
         lora = _linear(F.silu(_linear(sample, w["t_embedder.1.linear_1.weight"])),
                        w["t_embedder.1.linear_2.weight"])
         emb = F.rms_norm(sample, (cfg.hidden,), w["t_embedding_norm.weight"], cfg.eps)
         ctx = context.float()
-        for b in range(cfg.blocks):
-            h = self._block(b, h, emb, lora, ctx, freqs)
         fm = _linear(_linear(F.silu(emb), w["final_layer.adaln_modulation.1.weight"]),
                      w["final_layer.adaln_modulation.2.weight"])
         shift, scale = (fm + lora[:, :, :2 * cfg.hidden]).chunk(2, dim=-1)
-        h = self._ln_mod(h, scale, shift)
-        out = _linear(h, w["final_layer.linear.weight"])  # [B, L, p*p*t*C]
+        L = Tp * Hp * Wp
+        if self.seq:
+            R = B * L
+            if R % self.world:
+                raise ValueError("B * tokens must divide evenly over ranks")
+            n = R // self.world
+            lo = self.rank * n
+            segs = self._segments(lo, lo + n, L)
+            h = _linear(xp.reshape(R, -1)[lo:lo + n], w["x_embedder.proj.1.weight"])  # [n, hidden]
+            for b in range(cfg.blocks):
+                h = self._block_rows(b, h, emb, lora, ctx, freqs, B, L, segs)
+            h = self._ln_mod_rows(h, scale, shift, segs)
+            part = _linear(h, w["final_layer.linear.weight"])  # [n, p*p*t*C]
+            import torch.distributed as dist
+            out = torch.empty((R, part.shape[1]), dtype=part.dtype, device=part.device)
+            dist.all_gather_into_tensor(out, part.contiguous(), group=self.group)
+            out = out.view(B, L, -1)
+        else:
+            h = _linear(xp, w["x_embedder.proj.1.weight"])  # [B, L, hidden]
+            for b in range(cfg.blocks):
+                h = self._block(b, h, emb, lora, ctx, freqs)
+            h = self._ln_mod(h, scale, shift)
+            out = _linear(h, w["final_layer.linear.weight"])  # [B, L, p*p*t*C]
         # "B T H W (p1 p2 t C) -> B C (T t) (H p1) (W p2)"
         out = out.reshape(B, Tp, Hp, Wp, ps, ps, pt, cfg.out_channels)
         out = out.permute(0, 7, 1, 6, 2, 4, 3, 5).reshape(B, cfg.out_channels, T, Hh, Ww)

@@ -241,7 +241,7 @@ def run_dit(args, rank, world, local_rank):
         import torch.distributed as dist
         group = dist.group.WORLD
     weights = make_weights(cfg, seed=1234, device=dev, rng_device=dev)
-    model = AnimaDiT(cfg, weights, rank=rank, world=world, group=group)
+    model = AnimaDiT(cfg, weights, rank=rank, world=world, group=group, shard=args.dit_shard)
     del weights
     side = args.latent
     g = torch.Generator(device=dev).manual_seed(4321)
@@ -303,7 +303,9 @@ def run_dit(args, rank, world, local_rank):
         "data": "synthetic (seeded latent and context, N(0,0.02) bf16-valued weights)",
         "config": {"workload": f"Anima DiT Euler+CFG step, {args.blocks} blocks, latent "
                                f"16x{side}x{side} ({L} tokens), context 512x1024, CFG pair",
-                   "global_batch": 2, "seq_len": L, "parallelism": f"heads{world}",
+                   "global_batch": 2, "seq_len": L,
+                   "parallelism": (f"heads{world}" if world == 1 or args.dit_shard == "heads"
+                                   else f"heads{world} (attention) + tokens{world} (rest), all-to-all"),
                    "heads_per_gpu": 16 // world, "tflops_per_gpu": round(fl / world / (ms * 1e-3) / 1e12, 1),
                    "l2": "weights (4 GB fp16) exceed L2 every step",
                    "model_tflop_per_step": round(fl / 1e12, 2)},
@@ -467,6 +469,10 @@ def main():
                     help="attn: fused attention op (headline); dit: one full DiT step (config 4)")
     ap.add_argument("--blocks", type=int, default=28, help="DiT blocks (dit workload)")
     ap.add_argument("--latent", type=int, default=128, help="latent side (dit workload)")
+    ap.add_argument("--dit-shard", choices=["tokens", "heads"], default="tokens",
+                    help="dit workload on N GPUs: heads = all-gather of head outputs before a "
+                         "replicated o-proj; tokens = rows split over ranks, all-to-all around "
+                         "the head-parallel attention")
     ap.add_argument("--schedule", choices=["auto", "unit", "split"], default="auto",
                     help="auto: the library's choice (persistent split schedule only where it "
                          "measured faster); unit: one CTA per 256-row unit; split: persistent "

@@ -43,7 +43,7 @@ def test_harness_matches_reference_model_cpu():
     assert rel_l2(out, g["x_next"]) <= LATENT_REL_L2
 
 
-def _rank_main(rank, world, port, q):
+def _rank_main(rank, world, port, q, shard):
     import sys
     import torch.distributed as dist
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
@@ -54,7 +54,7 @@ def _rank_main(rank, world, port, q):
         g, blocks, wseed, x, cc, cu = _load("small")
         cfg = DiTConfig(blocks=blocks)
         model = AnimaDiT(cfg, make_weights(cfg, seed=wseed), rank=rank, world=world,
-                         attn_fn=cpu_attention)
+                         attn_fn=cpu_attention, shard=shard)
         with torch.no_grad():
             out = _step(model, g, x, cc, cu, "cpu").numpy()
         if rank == 0:
@@ -63,15 +63,17 @@ def _rank_main(rank, world, port, q):
         dist.destroy_process_group()
 
 
-def test_head_parallel_two_ranks_matches_reference_model_cpu():
-    """Two gloo ranks, 8 heads each, one all_gather_into_tensor per attention before the
-    o-proj, against the reference model's latent (same bar as one rank)."""
+@pytest.mark.parametrize("shard", ["tokens", "heads"])
+def test_head_parallel_two_ranks_matches_reference_model_cpu(shard):
+    """Two gloo ranks, 8 heads each, against the reference model's latent (same bar as one
+    rank).  heads: one all_gather_into_tensor per attention before a replicated o-proj;
+    tokens: rows split over the ranks, all_to_all_single into and out of the attention."""
     import torch.multiprocessing as mp
     g, blocks, wseed, x, cc, cu = _load("small")
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    port = 29600 + os.getpid() % 200
-    procs = [ctx.Process(target=_rank_main, args=(r, 2, port, q)) for r in range(2)]
+    port = 29600 + os.getpid() % 200 + (0 if shard == "tokens" else 7)
+    procs = [ctx.Process(target=_rank_main, args=(r, 2, port, q, shard)) for r in range(2)]
     for p in procs:
         p.start()
     out = q.get(timeout=600)
