@@ -433,3 +433,39 @@ class AnimaDiT:
         v = self.forward(xb, t, ctx)
         v_cfg = v[0:1] + cfg_scale * (v[1:2] - v[0:1])
         return x + v_cfg[:, :, 0] * (sigma_next - sigma)
+
+
+class StepGraph:
+    """One ``AnimaDiT.euler_cfg_step`` captured as a CUDA graph.
+
+    A step issues about fifty launches per block (GEMMs, the library's kernels, torch
+    elementwise ops and, on N GPUs, the collectives); once the per-GPU work of a step drops
+    to a few milliseconds, issuing them from Python costs more than running them.  Replaying
+    the captured graph issues the whole step at once.  The graph owns static copies of the
+    latent and both contexts: ``__call__`` copies new values into them (on the current
+    stream), replays, and returns the static output tensor (overwritten by the next call).
+    ``sigma``, ``sigma_next`` and ``cfg_scale`` are fixed at capture.  On N ranks every rank
+    must build and replay its graph in the same order (the collectives are captured), and
+    drop it before the process group is destroyed."""
+
+    def __init__(self, model: "AnimaDiT", x, sigma: float, sigma_next: float, ctx_cond,
+                 ctx_uncond, cfg_scale: float, warmup: int = 2):
+        self.x, self.cc, self.cu = x.clone(), ctx_cond.clone(), ctx_uncond.clone()
+        args = (sigma, sigma_next)
+        side = torch.cuda.Stream()
+        side.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(side):  # first calls allocate caches outside the capture
+            for _ in range(warmup):
+                model.euler_cfg_step(self.x, *args, self.cc, self.cu, cfg_scale)
+        torch.cuda.current_stream().wait_stream(side)
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph):
+            self.out = model.euler_cfg_step(self.x, *args, self.cc, self.cu, cfg_scale)
+
+    def __call__(self, x=None, ctx_cond=None, ctx_uncond=None):
+        for dst, src in ((self.x, x), (self.cc, ctx_cond), (self.cu, ctx_uncond)):
+            if src is not None:
+                dst.copy_(src, non_blocking=True)
+        self.graph.replay()
+        return self.out
+

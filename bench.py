@@ -257,16 +257,24 @@ def run_dit(args, rank, world, local_rank):
         torch.cuda.synchronize()
 
     with torch.no_grad():
+        if args.graph:
+            from anima_attn.dit import StepGraph
+            graph = StepGraph(model, x, 0.5, 0.0, cc, cu, 5.0)
+            run_step = lambda xx=None, c1=None, c2=None: graph(xx, c1, c2)
+        else:
+            graph = None
+            run_step = lambda xx=None, c1=None, c2=None: model.euler_cfg_step(
+                x if xx is None else xx, 0.5, 0.0, cc if c1 is None else c1, cu if c2 is None else c2, 5.0)
         clocks = ClockSampler(local_rank)
         with clocks:
             for _ in range(args.warmup):
-                model.euler_cfg_step(x, 0.5, 0.0, cc, cu, 5.0)
+                run_step()
             barrier()
             e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             t_begin = time.perf_counter()
             e0.record(stream)
             for _ in range(args.steps):
-                model.euler_cfg_step(x, 0.5, 0.0, cc, cu, 5.0)
+                run_step()
             e1.record(stream)
             torch.cuda.synchronize()
             t_end = time.perf_counter()
@@ -278,7 +286,7 @@ def run_dit(args, rank, world, local_rank):
 
         def host_step():
             dx, dcc, dcu = (t.to(dev, non_blocking=True) for t in (hx, hcc, hcu))
-            hout.copy_(model.euler_cfg_step(dx, 0.5, 0.0, dcc, dcu, 5.0), non_blocking=True)
+            hout.copy_(run_step(dx, dcc, dcu), non_blocking=True)
             torch.cuda.synchronize()
 
         host_step()
@@ -288,6 +296,7 @@ def run_dit(args, rank, world, local_rank):
         for _ in range(n_e2e):
             host_step()
         e2e_ms = (time.perf_counter() - t0) / n_e2e * 1e3
+        del graph, run_step  # a graph holding NCCL calls goes before the process group
     t = torch.tensor([ms, e2e_ms], device=dev, dtype=torch.float64)
     if world > 1:
         import torch.distributed as dist
@@ -308,6 +317,7 @@ def run_dit(args, rank, world, local_rank):
                                    else f"heads{world} (attention) + tokens{world} (rest), all-to-all"),
                    "heads_per_gpu": 16 // world, "tflops_per_gpu": round(fl / world / (ms * 1e-3) / 1e12, 1),
                    "l2": "weights (4 GB fp16) exceed L2 every step",
+                   "cuda_graph": bool(args.graph),
                    "model_tflop_per_step": round(fl / 1e12, 2)},
         "e2e": {"value": round(e2e_ms, 3), "unit": "ms", "h2d_bytes_per_step": (hx.numel() + hcc.numel() + hcu.numel()) * 4,
                 "d2h_bytes_per_step": hout.numel() * 4},
@@ -469,6 +479,9 @@ def main():
                     help="attn: fused attention op (headline); dit: one full DiT step (config 4)")
     ap.add_argument("--blocks", type=int, default=28, help="DiT blocks (dit workload)")
     ap.add_argument("--latent", type=int, default=128, help="latent side (dit workload)")
+    ap.add_argument("--graph", type=int, choices=[0, 1], default=1,
+                    help="dit workload: replay the step as one captured CUDA graph (1) or issue "
+                         "it op by op from Python (0)")
     ap.add_argument("--dit-shard", choices=["tokens", "heads"], default="tokens",
                     help="dit workload on N GPUs: heads = all-gather of head outputs before a "
                          "replicated o-proj; tokens = rows split over ranks, all-to-all around "

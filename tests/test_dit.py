@@ -133,3 +133,24 @@ def test_gate_residual_kernel_vs_torch():
     out = gate_residual_(x, gate, y)
     assert out.data_ptr() == x.data_ptr()
     torch.testing.assert_close(out, ref, rtol=1e-6, atol=1e-6)
+
+
+@pytest.mark.gpu
+def test_step_graph_replay_matches_eager_step():
+    """StepGraph (the step captured as one CUDA graph) gives the eager step's latent, also
+    after new inputs are copied into its static buffers."""
+    from anima_attn.dit import AnimaDiT, DiTConfig, StepGraph, make_weights
+    g, blocks, wseed, x, cc, cu = _load("small")
+    cfg = DiTConfig(blocks=blocks)
+    torch.cuda.set_device(0)
+    model = AnimaDiT(cfg, make_weights(cfg, seed=wseed, device="cuda"))
+    T = lambda a: torch.from_numpy(a).cuda()
+    s, sn, c = float(g["sigma"]), float(g["sigma_next"]), float(g["cfg"])
+    with torch.no_grad():
+        graph = StepGraph(model, T(x), s, sn, T(cc), T(cu), c)
+        for scale in (1.0, 0.5):
+            xs = T(x) * scale
+            eager = model.euler_cfg_step(xs, s, sn, T(cc), T(cu), c).cpu().numpy()
+            replay = graph(xs).cpu().numpy()
+            assert rel_l2(replay, eager) <= 1e-6
+        assert rel_l2(graph(T(x)).cpu().numpy(), g["x_next"]) <= LATENT_REL_L2
