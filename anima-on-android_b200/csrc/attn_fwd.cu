@@ -663,46 +663,67 @@ __global__ void __launch_bounds__(kThreads, 1)
         wg_sync(1 + i);
         if (sm.last[i]) {
           __threadfence();
-          float mx = -INFINITY;
-          for (int c = c0; c <= c1; ++c) {
+          // Merge row by row: warp `quarter` takes the tile's rows [32 quarter, 32 quarter + 32),
+          // its 32 lanes spread over a row's 128 columns, so every partial load and output
+          // store is one coalesced 512-byte row; four rows are in flight per pass.
+          const int q0 = (sg.unit % p.nqb) * kUnitRows;
+          const int hh = bh % p.H;
+          auto part_of = [&](int c) {
             const int lo_c = slice_lo(p, c);
-            const float* pc = p.part + ((long long)c * 2 + (max(t0, lo_c) == lo_c ? 0 : 1)) * kPartFloats;
-            mx = fmaxf(mx, __ldcg(pc + kUnitRows * kD + r));
-          }
-          float den = 0.f;
-          for (int c = c0; c <= c1; ++c) {
-            const int lo_c = slice_lo(p, c);
-            const float* pc = p.part + ((long long)c * 2 + (max(t0, lo_c) == lo_c ? 0 : 1)) * kPartFloats;
-            den += exp2f(__ldcg(pc + kUnitRows * kD + r) - mx) * __ldcg(pc + kUnitRows * kD + kUnitRows + r);
-          }
-          const float inv = den > 0.f ? 1.f / den : 0.f;
-          char* out_row = reinterpret_cast<char*>(p.out) +
-                          ((long long)b * p.ob + (long long)(bh % p.H) * p.oh +
-                           (long long)grow * p.os) *
-                              (kOut == ANIMA_DTYPE_F32 ? 4 : 2);
+            return p.part + ((long long)c * 2 + (max(t0, lo_c) == lo_c ? 0 : 1)) * kPartFloats;
+          };
 #pragma unroll 1
-          for (int ch = 0; ch < 4; ++ch) {
-            float acc[32];
+          for (int rr = 0; rr < 32; rr += 4) {
+            const int r0 = i * kBM + quarter * 32 + rr;
+            float mx[4], den[4];
+            float4 acc[4];
 #pragma unroll
-            for (int e = 0; e < 32; ++e) acc[e] = 0.f;
+            for (int k = 0; k < 4; ++k) {
+              mx[k] = -INFINITY;
+              den[k] = 0.f;
+              acc[k] = make_float4(0.f, 0.f, 0.f, 0.f);
+            }
             for (int c = c0; c <= c1; ++c) {
-              const int lo_c = slice_lo(p, c);
-              const float* pc = p.part + ((long long)c * 2 + (max(t0, lo_c) == lo_c ? 0 : 1)) * kPartFloats;
-              const float w = exp2f(__ldcg(pc + kUnitRows * kD + r) - mx);
-              const float4* src = reinterpret_cast<const float4*>(pc + (long long)r * kD + ch * 32);
+              const float* pc = part_of(c);
 #pragma unroll
-              for (int e = 0; e < 8; ++e) {
-                const float4 v4 = __ldcg(src + e);
-                acc[4 * e] += w * v4.x;
-                acc[4 * e + 1] += w * v4.y;
-                acc[4 * e + 2] += w * v4.z;
-                acc[4 * e + 3] += w * v4.w;
+              for (int k = 0; k < 4; ++k) mx[k] = fmaxf(mx[k], __ldcg(pc + kUnitRows * kD + r0 + k));
+            }
+            for (int c = c0; c <= c1; ++c) {
+              const float* pc = part_of(c);
+              float mc[4], lc[4];
+              float4 v[4];
+#pragma unroll
+              for (int k = 0; k < 4; ++k) {
+                mc[k] = __ldcg(pc + kUnitRows * kD + r0 + k);
+                lc[k] = __ldcg(pc + kUnitRows * kD + kUnitRows + r0 + k);
+                v[k] = __ldcg(reinterpret_cast<const float4*>(pc + (long long)(r0 + k) * kD) + lane);
+              }
+#pragma unroll
+              for (int k = 0; k < 4; ++k) {
+                const float w = exp2f(mc[k] - mx[k]);
+                den[k] += w * lc[k];
+                acc[k].x += w * v[k].x;
+                acc[k].y += w * v[k].y;
+                acc[k].z += w * v[k].z;
+                acc[k].w += w * v[k].w;
               }
             }
-            uint32_t o[32];
 #pragma unroll
-            for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(acc[e]);
-            if (grow < p.S_q) store_row<kOut>(out_row, o, ch, inv);
+            for (int k = 0; k < 4; ++k) {
+              const int grow_k = q0 + r0 + k;
+              if (grow_k >= p.S_q) continue;
+              const float inv = den[k] > 0.f ? 1.f / den[k] : 0.f;
+              const long long off =
+                  (long long)b * p.ob + (long long)hh * p.oh + (long long)grow_k * p.os + lane * 4;
+              if (kOut == ANIMA_DTYPE_F32) {
+                *reinterpret_cast<float4*>(reinterpret_cast<float*>(p.out) + off) =
+                    make_float4(acc[k].x * inv, acc[k].y * inv, acc[k].z * inv, acc[k].w * inv);
+              } else {
+                *reinterpret_cast<uint2*>(reinterpret_cast<uint16_t*>(p.out) + off) =
+                    make_uint2(pack2<kOut>(acc[k].x * inv, acc[k].y * inv),
+                               pack2<kOut>(acc[k].z * inv, acc[k].w * inv));
+              }
+            }
           }
           if (row == 0) p.sem[ut * kNT + i] = 0;  // leave the counter zero for the next call
         }
