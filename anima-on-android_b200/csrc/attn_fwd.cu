@@ -60,13 +60,6 @@ constexpr uint32_t kRegsSoftmax = 200;
 constexpr uint32_t kRegsControl = 104;
 constexpr uint32_t kTmemCols = 512;
 constexpr float kRescaleThreshold = 8.0f;  // log2 units
-#ifndef ANIMA_STAGGER
-#define ANIMA_STAGGER 0
-#endif
-// Cycles between the end of tile 0's first QK^T of a segment and the issue of tile 1's.
-// Issued back to back, the two tiles run one tile's MMA time (1024 cycles) apart, so
-// their softmax phases overlap and share MUFU; a larger offset can separate them.
-constexpr long long kStagger = ANIMA_STAGGER;
 #ifndef ANIMA_POLY_PER8
 #define ANIMA_POLY_PER8 0
 #endif
@@ -398,13 +391,6 @@ __global__ void __launch_bounds__(kThreads, 1)
             tc_fence_after();
             issue_qk(0, slot_of(ik));
             umma_commit(&sm.s_full[0]);
-            if (kStagger > 0 && n > 2) {
-              // Start tile 1 about half a period after tile 0 (see kStagger).
-              if (!(ok = wait(&sm.s_full[0], (uint32_t)g & 1u))) break;
-              const long long t_end = clock64() + kStagger;
-              while (clock64() < t_end) {
-              }
-            }
             issue_qk(1, slot_of(ik));
             umma_commit(&sm.s_full[1]);
             umma_commit(&sm.kv_empty[slot_of(ik)]);
