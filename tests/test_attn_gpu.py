@@ -83,6 +83,30 @@ def test_fused_host_entry_vs_reference_composition(aa):
     _ok(got, g["out"].transpose(0, 2, 1, 3))
 
 
+@pytest.mark.parametrize("B,H,Sq,Skv,masked", [(3, 6, 160, 200, True), (9, 1, 96, 96, False),
+                                                (2, 16, 64, 64, False)])
+def test_host_entry_chunks_vs_oracle(aa, O, B, H, Sq, Skv, masked):
+    """anima_rt_run_attention pipelines the call over (batch rows x head group) chunks;
+    odd B and H, a short last chunk (B=9, H=1 -> chunks of 2 rows) and per-sample key
+    padding all map back to the right output rows."""
+    from anima_attn import _lib as L
+    rng = np.random.default_rng(B * 100 + H)
+    q = rng.standard_normal((B, Sq, H, 128), dtype=np.float32)
+    k = rng.standard_normal((B, Skv, H, 128), dtype=np.float32)
+    v = rng.standard_normal((B, Skv, H, 128), dtype=np.float32)
+    qw = (1 + 0.1 * rng.standard_normal(128)).astype(np.float32)
+    valid = rng.integers(1, Skv + 1, size=B).astype(np.int32) if masked else None
+    out = np.zeros((B, Sq, H, 128), dtype=np.float32)
+    ok = L.lib.anima_rt_run_attention(
+        q.ctypes.data, k.ctypes.data, v.ctypes.data, qw.ctypes.data, None, None,
+        None if valid is None else valid.ctypes.data, out.ctypes.data, B, Sq, Skv, H, 128,
+        ct.c_float(1e-6), ct.c_float(128 ** -0.5), ct.c_uint(L.FLAG_QNORM))
+    assert ok, L.last_error()
+    rq, rk, rv = O.prologue(q, k, v, qw, None)  # [B, H, S, D]
+    ref = O.sdpa_varlen(rq, rk, rv, valid) if masked else O.sdpa(rq, rk, rv)
+    _ok(out.transpose(0, 2, 1, 3), ref)
+
+
 def test_numpyrt_run_sdpa_shapes(aa):
     from anima_attn.compat import NumpyRT
     g = golden("sdpa_ragged.npz")
