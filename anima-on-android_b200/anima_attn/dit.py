@@ -156,8 +156,11 @@ AttnFn = Callable[..., torch.Tensor]
 class AnimaDiT:
     """Inference forward of the Anima DiT with this library's attention.
 
-    ``weights`` is a make_weights() dict (full model; a rank slices its head rows).
-    ``group``: torch.distributed process group for head parallelism (None = 1 GPU).
+    ``weights`` is a make_weights() dict (full model; a rank slices what it needs).
+    ``rank`` / ``world`` / ``group``: this rank, the number of ranks and their
+    torch.distributed process group (world 1 = one GPU, no collectives).
+    ``shard``: "tokens" (default) or "heads", the multi-GPU layouts of the module
+    docstring; both split the attention by head.
     ``attn_fn`` replaces the attention op (signature of anima_attn.attention); tests on
     CPU pass a reference implementation, the product uses the B200 kernels.
     """

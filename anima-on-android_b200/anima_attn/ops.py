@@ -172,7 +172,7 @@ def attention_core(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, B: int, H:
     a.flags = flags
     a.kv_valid_len = _ptr(vl)
     ws = None
-    if stream_k and not pair:
+    if (stream_k or force_split) and not pair:
         ws = _workspace(q.device, int(L.lib.anima_attn_workspace_size(B, H, Sq, Skv, flags)))
     a.workspace = _ptr(ws)
     a.workspace_bytes = 0 if ws is None else ws.numel()
