@@ -24,7 +24,7 @@ reason (q and k are RMS-normalised; v is a projection of normalised activations)
 
 Multi-GPU (N ranks; the attention is split by heads in both modes, rank r owning heads
 [r*16/N, (r+1)*16/N)):
-  shard="heads"   the layout the north star describes: every rank holds the whole residual
+  shard="heads"   the layout specified for this step: every rank holds the whole residual
                   stream, projects q/k/v for its heads only, runs their attention, and one
                   all_gather_into_tensor per attention collects every rank's head outputs
                   before the o-proj.  o-proj, MLP, adaLN and final layer are replicated, so

@@ -6,7 +6,7 @@
 One step = one fused attention call of one DiT block over one synthetic batch:
 per-head q/k RMSNorm + 3D RoPE + bf16 cast (prologue kernel) and the tcgen05 flash
 attention (attention kernel), B=2 (CFG pair) x 16 heads x L tokens x D=128, inputs
-resident in HBM.  The default L=4096 is BASELINE config 5's north-star point
+resident in HBM.  The default L=4096 is the 4096-token point of the sequence-length sweep
 (1024x1024 image); other configs are parity tests, not bench lines.
 
 metric  : attention TFLOP/s (4*B*H*L^2*D per step / step time), whole job.
@@ -227,7 +227,7 @@ def dit_flops(blocks=28, L=4096, B=2, ctx=512, hidden=2048, mlp=8192, ctx_dim=10
 
 
 def run_dit(args, rank, world, local_rank):
-    """One Euler+CFG step of the Anima DiT: latent 16x128x128 (4096
+    """One Euler+CFG step of the Anima DiT (the full-step configuration): latent 16x128x128 (4096
     tokens), 28 blocks, hidden 2048, 16 heads, CFG pair batched (B=2), sigma 0.5 -> 0,
     cfg 5; heads split over the ranks, one NCCL all-gather per attention."""
     import torch

@@ -48,7 +48,7 @@ def max_abs(a, b):
     return float(np.abs(np.asarray(a, np.float64) - np.asarray(b, np.float64)).max())
 
 
-# Parity bar stated by the task's north star: per output, rel-L2 <= 5e-3 and
+# Parity bar for this path: per output, rel-L2 <= 5e-3 and
 # max-abs <= 2e-2 against the reference's fp32 SDPA.
 ATTN_REL_L2 = 5e-3
 ATTN_MAX_ABS = 2e-2

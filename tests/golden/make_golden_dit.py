@@ -1,4 +1,4 @@
-"""Golden latents for BASELINE config 4 (one Euler+CFG DiT step) from the reference model.
+"""Golden latents for one full Euler+CFG DiT step, from the reference model.
 
     python tests/golden/make_golden_dit.py [small|full]
 

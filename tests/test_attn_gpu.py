@@ -1,6 +1,6 @@
 """Parity of the B200 kernels with the reference (oracle + golden fixtures), on a GPU.
 
-Bar (north star): rel-L2 <= 5e-3 and max-abs <= 2e-2 per attention output against the
+Bar: rel-L2 <= 5e-3 and max-abs <= 2e-2 per attention output against the
 reference's fp32 flash SDPA; the RoPE drop-in is bit-exact; the RMSNorm drop-in agrees
 to fp32 rounding (its sum is a tree, the reference's is sequential).
 """
@@ -244,7 +244,7 @@ def test_stream_k_schedule_matches_unit_schedule_and_oracle(aa, O, Sq, Skv):
     assert rel_l2(s_np, u_np) < ATTN_REL_L2
 
 
-# ------------------------------------------------------------------ BASELINE configs
+# ------------------------------------------------------------------ benchmark configurations
 def test_config1_self_attention_256(aa, O):
     rng = np.random.default_rng(0)
     q, k, v = (rng.standard_normal((2, 16, 256, 128), dtype=np.float32) for _ in range(3))

@@ -1,4 +1,4 @@
-"""The DiT step harness against the reference model.
+"""The DiT step harness (one full Euler+CFG step) against the reference model.
 
 CPU tests: the harness's block arithmetic, patching, timestep/adaLN-LoRA and CFG step,
 with a CPU attention injected, against the reference MiniTrainDIT (tests/golden/
@@ -13,7 +13,7 @@ import torch
 
 from conftest import GOLDEN, rel_l2
 
-LATENT_REL_L2 = 1e-2  # north star: denoised latent after one full step
+LATENT_REL_L2 = 1e-2  # required bar: denoised latent after one full step
 
 
 def _load(which):
