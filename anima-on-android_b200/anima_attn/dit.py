@@ -9,10 +9,11 @@ library:
   Attention               src/predict2.py:91-214   (q/k/v projections, per-head q/k
                           RMSNorm, RoPE on self-attention, SDPA, o-proj)
   EulerSampler step       anima_rt/scripts/sampling.py:115-140 (CFG pair, Euler update)
-The attention of every block (norm, RoPE, SDPA) runs in this library's kernels, and so
-do the two fused HBM passes around it: LayerNorm + adaLN modulation + 16-bit cast
-(anima_dit_ln_modulate) and the gated residual update (anima_dit_gate_residual).  GEMMs
-and GELU run in PyTorch.  The residual stream stays fp32; GEMMs take 16-bit operands with
+The attention of every block (norm, RoPE, SDPA) runs in this library's kernels, and so do
+the HBM passes around it: each gated residual update fused with the LayerNorm + adaLN
+modulation + 16-bit cast that follows it (anima_dit_gate_residual_ln_modulate; the first
+LayerNorm of the step alone, anima_dit_ln_modulate) and the exact GELU of the MLP
+(anima_dit_gelu).  GEMMs run in PyTorch (cuBLAS).  The residual stream stays fp32; GEMMs take 16-bit operands with
 fp32 accumulation.  A GEMM whose consumer rounds to the operand type anyway (q/k/v into
 the attention prologue, MLP layer 1 into GELU and layer 2) writes 16-bit output; the others
 write fp32.
@@ -228,13 +229,44 @@ class AnimaDiT:
         h = F.layer_norm(x, (x.shape[-1],), eps=self.cfg.eps) * (1 + scale) + shift
         return h.to(self.cfg.gemm_dtype)
 
-    @staticmethod
-    def _gate_add(x, gate, y):
-        """x + gate * y; in place on CUDA (x is this forward's own residual buffer)."""
+    def _add_ln(self, x, pending, scale, shift):
+        """Apply a pending gated residual (gate, y) to x, then LayerNorm + modulate it:
+        returns (x, h).  Every gated residual of a block is followed by the next sub-block's
+        (or the final layer's) LayerNorm, so on CUDA the two run as one pass over the
+        residual stream with x updated in place (x is this forward's own buffer)."""
+        if pending is None:
+            return x, self._ln_mod(x, scale, shift)
+        gate, y = pending
         if x.is_cuda:
-            from .ops import gate_residual_
-            return gate_residual_(x, gate, y)
-        return x + gate * y
+            from .ops import gate_residual_ln_modulate_
+            return x, gate_residual_ln_modulate_(x, gate, y, scale, shift, self.cfg.eps,
+                                                 out_dtype=self.cfg.gemm_dtype)
+        x = x + gate * y
+        return x, self._ln_mod(x, scale, shift)
+
+    @staticmethod
+    def _gelu(h):
+        """Exact GELU (nn.GELU, predict2.py:45) on the 16-bit MLP hidden layer, in place on
+        CUDA; fp32 arithmetic either way."""
+        if h.is_cuda and h.numel() % 8 == 0 and h.is_contiguous():
+            from .ops import gelu_
+            return gelu_(h)
+        return F.gelu(h.float()).to(h.dtype)
+
+    def _mods(self, p, emb, lora):
+        """adaLN-LoRA modulation (shift, scale, gate) of the three sub-blocks of block p."""
+        w = self.w
+
+        def mods(m):
+            h = _linear(F.silu(emb), w[p + f"adaln_modulation_{m}.1.weight"])
+            return (_linear(h, w[p + f"adaln_modulation_{m}.2.weight"]) + lora).chunk(3, dim=-1)
+
+        return mods("self_attn"), mods("cross_attn"), mods("mlp")
+
+    def _mlp(self, p, h):
+        dt = self.cfg.gemm_dtype
+        hid = self._gelu(_linear(h, self.w[p + "mlp.layer1.weight"], dt))
+        return _linear(hid, self.w[p + "mlp.layer2.weight"])
 
     # ---------------------------------------------------------- tokens mode (rows)
     def _segments(self, lo: int, hi: int, L: int):
@@ -254,13 +286,17 @@ class AnimaDiT:
                  for s0, s1, b in segs]
         return parts[0] if len(parts) == 1 else torch.cat(parts)
 
-    def _gate_add_rows(self, x, gate, y, segs):
-        """x += gate[sample] * y on local rows; in place on CUDA."""
-        if x.is_cuda:
-            for s0, s1, b in segs:
-                self._gate_add(x[s0:s1].unsqueeze(0), gate[b:b + 1], y[s0:s1].unsqueeze(0))
-            return x
-        return torch.cat([x[s0:s1] + gate[b, 0] * y[s0:s1] for s0, s1, b in segs])
+    def _add_ln_rows(self, x, pending, scale, shift, segs):
+        """_add_ln on local rows x [n, D] whose samples are given by segs."""
+        if pending is None:
+            return x, self._ln_mod_rows(x, scale, shift, segs)
+        gate, y = pending
+        if not x.is_cuda:
+            x = torch.cat([x[s0:s1] + gate[b, 0] * y[s0:s1] for s0, s1, b in segs])
+            return x, self._ln_mod_rows(x, scale, shift, segs)
+        parts = [self._add_ln(x[s0:s1].unsqueeze(0), (gate[b:b + 1], y[s0:s1].unsqueeze(0)),
+                              scale[b:b + 1], shift[b:b + 1])[1][0] for s0, s1, b in segs]
+        return x, parts[0] if len(parts) == 1 else torch.cat(parts)
 
     def _by_rank_linear(self, h, w):
         """h [n, K] @ w[r]^T for every rank r -> [N, n, M] (the all-to-all send buffer)."""
@@ -296,25 +332,17 @@ class AnimaDiT:
         o = o.permute(1, 0, 2).reshape(n, N * hl * hd)  # my rows, heads in order
         return _linear(o, self.w[p + ".output_proj.weight"])
 
-    def _block_rows(self, b, x, emb, lora, ctx, freqs, B, L, segs):
+    def _block_rows(self, b, x, pending, emb, lora, ctx, freqs, B, L, segs):
+        """One block on local rows.  pending: the previous block's MLP residual (gate, y),
+        applied together with this block's first LayerNorm; returns (x, pending)."""
         p = f"blocks.{b}."
-        w = self.w
-
-        def mods(m):
-            h = _linear(F.silu(emb), w[p + f"adaln_modulation_{m}.1.weight"])
-            return (_linear(h, w[p + f"adaln_modulation_{m}.2.weight"]) + lora).chunk(3, dim=-1)
-
-        sh_sa, sc_sa, g_sa = mods("self_attn")
-        sh_ca, sc_ca, g_ca = mods("cross_attn")
-        sh_m, sc_m, g_m = mods("mlp")
-        dt = self.cfg.gemm_dtype
-        h = self._ln_mod_rows(x, sc_sa, sh_sa, segs)
-        x = self._gate_add_rows(x, g_sa, self._attention_rows(p + "self_attn", h, B, L, None, freqs), segs)
-        h = self._ln_mod_rows(x, sc_ca, sh_ca, segs)
-        x = self._gate_add_rows(x, g_ca, self._attention_rows(p + "cross_attn", h, B, L, ctx, None), segs)
-        h = self._ln_mod_rows(x, sc_m, sh_m, segs)
-        h = _linear(F.gelu(_linear(h, w[p + "mlp.layer1.weight"], dt)), w[p + "mlp.layer2.weight"])
-        return self._gate_add_rows(x, g_m, h, segs)
+        (sh_sa, sc_sa, g_sa), (sh_ca, sc_ca, g_ca), (sh_m, sc_m, g_m) = self._mods(p, emb, lora)
+        x, h = self._add_ln_rows(x, pending, sc_sa, sh_sa, segs)
+        y = self._attention_rows(p + "self_attn", h, B, L, None, freqs)
+        x, h = self._add_ln_rows(x, (g_sa, y), sc_ca, sh_ca, segs)
+        y = self._attention_rows(p + "cross_attn", h, B, L, ctx, None)
+        x, h = self._add_ln_rows(x, (g_ca, y), sc_m, sh_m, segs)
+        return x, (g_m, self._mlp(p, h))
 
     # ---------------------------------------------------------- heads mode
     def _gather_oproj(self, o_local: torch.Tensor, w_o: torch.Tensor) -> torch.Tensor:
@@ -353,26 +381,16 @@ class AnimaDiT:
                          op_dtype=cfg.gemm_dtype)
         return self._gather_oproj(o, self.w[p + ".output_proj.weight"])
 
-    def _block(self, b: int, x, emb, lora, ctx, freqs):
+    def _block(self, b: int, x, pending, emb, lora, ctx, freqs):
+        """One block on the whole residual stream [B, L, D]; pending as in _block_rows."""
         p = f"blocks.{b}."
-        w = self.w
-
-        def mods(m):
-            h = _linear(F.silu(emb), w[p + f"adaln_modulation_{m}.1.weight"])
-            return (_linear(h, w[p + f"adaln_modulation_{m}.2.weight"]) + lora).chunk(3, dim=-1)
-
-        sh_sa, sc_sa, g_sa = mods("self_attn")
-        sh_ca, sc_ca, g_ca = mods("cross_attn")
-        sh_m, sc_m, g_m = mods("mlp")
-        dt = self.cfg.gemm_dtype
-        h = self._ln_mod(x, sc_sa, sh_sa)
-        x = self._gate_add(x, g_sa, self._attention(p + "self_attn", h, None, freqs))
-        h = self._ln_mod(x, sc_ca, sh_ca)
-        x = self._gate_add(x, g_ca, self._attention(p + "cross_attn", h, ctx, None))
-        h = self._ln_mod(x, sc_m, sh_m)
-        # GELU in fp32 arithmetic on the 16-bit layer-1 output; layer 2 reads 16-bit anyway
-        h = _linear(F.gelu(_linear(h, w[p + "mlp.layer1.weight"], dt)), w[p + "mlp.layer2.weight"])
-        return self._gate_add(x, g_m, h)
+        (sh_sa, sc_sa, g_sa), (sh_ca, sc_ca, g_ca), (sh_m, sc_m, g_m) = self._mods(p, emb, lora)
+        x, h = self._add_ln(x, pending, sc_sa, sh_sa)
+        y = self._attention(p + "self_attn", h, None, freqs)
+        x, h = self._add_ln(x, (g_sa, y), sc_ca, sh_ca)
+        y = self._attention(p + "cross_attn", h, ctx, None)
+        x, h = self._add_ln(x, (g_ca, y), sc_m, sh_m)
+        return x, (g_m, self._mlp(p, h))
 
     # ------------------------------------------------------------------ forward
     def forward(self, x: torch.Tensor, timesteps: torch.Tensor, context: torch.Tensor):
@@ -406,9 +424,10 @@ class AnimaDiT:
             lo = self.rank * n
             segs = self._segments(lo, lo + n, L)
             h = _linear(xp.reshape(R, -1)[lo:lo + n], w["x_embedder.proj.1.weight"])  # [n, hidden]
+            pending = None
             for b in range(cfg.blocks):
-                h = self._block_rows(b, h, emb, lora, ctx, freqs, B, L, segs)
-            h = self._ln_mod_rows(h, scale, shift, segs)
+                h, pending = self._block_rows(b, h, pending, emb, lora, ctx, freqs, B, L, segs)
+            h = self._add_ln_rows(h, pending, scale, shift, segs)[1]
             part = _linear(h, w["final_layer.linear.weight"])  # [n, p*p*t*C]
             import torch.distributed as dist
             out = torch.empty((R, part.shape[1]), dtype=part.dtype, device=part.device)
@@ -416,9 +435,10 @@ class AnimaDiT:
             out = out.view(B, L, -1)
         else:
             h = _linear(xp, w["x_embedder.proj.1.weight"])  # [B, L, hidden]
+            pending = None
             for b in range(cfg.blocks):
-                h = self._block(b, h, emb, lora, ctx, freqs)
-            h = self._ln_mod(h, scale, shift)
+                h, pending = self._block(b, h, pending, emb, lora, ctx, freqs)
+            h = self._add_ln(h, pending, scale, shift)[1]
             out = _linear(h, w["final_layer.linear.weight"])  # [B, L, p*p*t*C]
         # "B T H W (p1 p2 t C) -> B C (T t) (H p1) (W p2)"
         out = out.reshape(B, Tp, Hp, Wp, ps, ps, pt, cfg.out_channels)

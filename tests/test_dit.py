@@ -154,3 +154,36 @@ def test_step_graph_replay_matches_eager_step():
             replay = graph(xs).cpu().numpy()
             assert rel_l2(replay, eager) <= 1e-6
         assert rel_l2(graph(T(x)).cpu().numpy(), g["x_next"]) <= LATENT_REL_L2
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("out_dtype", [torch.float16, torch.bfloat16])
+def test_gate_residual_ln_modulate_kernel_vs_torch(out_dtype):
+    """anima_dit_gate_residual_ln_modulate: x += gate*y in place, then the modulated
+    LayerNorm of the updated x, against fp32 torch."""
+    from anima_attn.ops import gate_residual_ln_modulate_
+    g = torch.Generator(device="cuda").manual_seed(9)
+    B, S, D = 2, 517, 2048
+    x = torch.randn(B, S, D, device="cuda", generator=g) * 2
+    y = torch.randn(B, S, D, device="cuda", generator=g)
+    mods = torch.randn(B, 1, 6 * D, device="cuda", generator=g) * 0.3
+    gate, _, _ = mods[:, :, :3 * D].chunk(3, dim=-1)
+    sh, sc, _ = mods[:, :, 3 * D:].chunk(3, dim=-1)
+    x_ref = x + gate * y
+    ref = torch.nn.functional.layer_norm(x_ref, (D,), eps=1e-6) * (1 + sc) + sh
+    h = gate_residual_ln_modulate_(x, gate, y, sc, sh, 1e-6, out_dtype=out_dtype)
+    torch.testing.assert_close(x, x_ref, rtol=1e-6, atol=1e-5)
+    tol = 2 ** -8 if out_dtype == torch.float16 else 2 ** -5
+    assert ((h.float() - ref).abs() / ref.abs().clamp_min(1.0)).max().item() <= tol
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+def test_gelu_kernel_vs_torch(dtype):
+    from anima_attn.ops import gelu_
+    g = torch.Generator(device="cuda").manual_seed(10)
+    x = (torch.randn(1024, 520, device="cuda", generator=g) * 3).to(dtype)
+    ref = torch.nn.functional.gelu(x.float())
+    out = gelu_(x.clone())
+    ulp = 2 ** -10 if dtype == torch.float16 else 2 ** -7  # one 16-bit ulp, relative
+    assert ((out.float() - ref).abs() <= ref.abs() * ulp + 1e-3 * ulp).all()
