@@ -65,8 +65,9 @@ SIGNATURES = {
     "anima_dit_ln_modulate": ([_P, _P, _P, ct.c_int64, _P, ct.c_int, ct.c_int64, ct.c_int, ct.c_int,
                                ct.c_float, _P], ct.c_int),
     "anima_dit_gate_residual": ([_P, _P, ct.c_int64, _P, ct.c_int64, ct.c_int, ct.c_int, _P], ct.c_int),
-    "anima_dit_gate_residual_ln_modulate": ([_P, _P, ct.c_int64, _P, _P, _P, ct.c_int64, _P, ct.c_int,
-                                             ct.c_int64, ct.c_int, ct.c_int, ct.c_float, _P], ct.c_int),
+    "anima_dit_gate_residual_ln_modulate": ([_P, _P, ct.c_int64, _P, ct.c_int, _P, _P, ct.c_int64, _P,
+                                             ct.c_int, ct.c_int64, ct.c_int, ct.c_int, ct.c_float, _P],
+                                            ct.c_int),
     "anima_dit_gelu": ([_P, _P, ct.c_int, ct.c_int64, _P], ct.c_int),
     "anima_attn_device_info": ([ct.POINTER(ct.c_int), ct.POINTER(ct.c_int)], ct.c_int),
     "anima_attn_version": ([], ct.c_char_p),

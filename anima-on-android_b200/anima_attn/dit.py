@@ -14,9 +14,9 @@ the HBM passes around it: each gated residual update fused with the LayerNorm + 
 modulation + 16-bit cast that follows it (anima_dit_gate_residual_ln_modulate; the first
 LayerNorm of the step alone, anima_dit_ln_modulate) and the exact GELU of the MLP
 (anima_dit_gelu).  GEMMs run in PyTorch (cuBLAS).  The residual stream stays fp32; GEMMs take 16-bit operands with
-fp32 accumulation.  A GEMM whose consumer rounds to the operand type anyway (q/k/v into
-the attention prologue, MLP layer 1 into GELU and layer 2) writes 16-bit output; the others
-write fp32.
+fp32 accumulation.  The projections, MLP layers and o-proj write 16-bit output (their
+consumers are the attention prologue, GELU, the next GEMM, or the fused residual pass, which
+adds them into the fp32 residual stream); the adaLN and final-layer GEMMs write fp32.
 The operand type is fp16 by default: the weights are bf16 values (exact in fp16 unless
 below 2^-14), the GEMM inputs are normalised activations, and fp16's 10-bit mantissa
 keeps the step's latent within 1.1e-3 rel-L2 of the fp32 reference model at 2 blocks,
@@ -266,7 +266,7 @@ class AnimaDiT:
     def _mlp(self, p, h):
         dt = self.cfg.gemm_dtype
         hid = self._gelu(_linear(h, self.w[p + "mlp.layer1.weight"], dt))
-        return _linear(hid, self.w[p + "mlp.layer2.weight"])
+        return _linear(hid, self.w[p + "mlp.layer2.weight"], dt)
 
     # ---------------------------------------------------------- tokens mode (rows)
     def _segments(self, lo: int, hi: int, L: int):
@@ -330,7 +330,7 @@ class AnimaDiT:
         # [B, L, hl, hd] = [N, n, hl*hd] by destination rank -> [N (source heads), n, hl*hd]
         o = self._a2a(o.reshape(N, n, hl * hd))
         o = o.permute(1, 0, 2).reshape(n, N * hl * hd)  # my rows, heads in order
-        return _linear(o, self.w[p + ".output_proj.weight"])
+        return _linear(o, self.w[p + ".output_proj.weight"], dt)
 
     def _block_rows(self, b, x, pending, emb, lora, ctx, freqs, B, L, segs):
         """One block on local rows.  pending: the previous block's MLP residual (gate, y),
@@ -350,7 +350,7 @@ class AnimaDiT:
         B, S = o_local.shape[:2]
         cols = self.h_local * self.cfg.head_dim
         if self.world == 1:
-            return _linear(o_local.reshape(B, S, cols), w_o)
+            return _linear(o_local.reshape(B, S, cols), w_o, self.cfg.gemm_dtype)
         import torch.distributed as dist
         # gathered along dim 0 ([world * B, S, H/N, hd]); viewed as [world, B, ...]
         full = torch.empty((self.world * B,) + tuple(o_local.shape[1:]), dtype=o_local.dtype,

@@ -255,19 +255,21 @@ def gate_residual_ln_modulate_(x: torch.Tensor, gate: torch.Tensor, y: torch.Ten
                                scale: torch.Tensor, shift: torch.Tensor, eps: float = 1e-6,
                                out_dtype=torch.float16) -> torch.Tensor:
     """x += gate * y in place, then LayerNorm(x) * (1 + scale) + shift -> out_dtype, in one
-    pass.  x, y [B, L, D] fp32 contiguous; gate/scale/shift [B, 1, D] views with D contiguous
-    (scale and shift with a common batch stride)."""
+    pass.  x [B, L, D] fp32 contiguous, y of x's shape (fp32, fp16 or bf16) contiguous;
+    gate/scale/shift [B, 1, D] views with D contiguous (scale and shift with a common batch
+    stride)."""
     _check_cuda(x, gate, y, scale, shift)
     B, Lr, D = x.shape
     if not (x.is_contiguous() and y.is_contiguous()) or x.dtype != torch.float32 or \
-            y.dtype != torch.float32 or y.shape != x.shape:
-        raise ValueError("x and y must be contiguous float32 of one shape")
+            y.dtype not in _TORCH_DT or y.shape != x.shape:
+        raise ValueError("x (float32) and y must be contiguous tensors of one shape")
     if gate.stride(-1) != 1 or scale.stride(-1) != 1 or shift.stride(-1) != 1 or \
             scale.stride(0) != shift.stride(0):
         raise ValueError("gate/scale/shift rows must be contiguous, scale/shift one batch stride")
     h = torch.empty((B, Lr, D), device=x.device, dtype=out_dtype)
     L.check(L.lib.anima_dit_gate_residual_ln_modulate(
-        _ptr(x), _ptr(gate), gate.stride(0), _ptr(y), _ptr(scale), _ptr(shift), scale.stride(0),
+        _ptr(x), _ptr(gate), gate.stride(0), _ptr(y), _TORCH_DT[y.dtype], _ptr(scale), _ptr(shift),
+        scale.stride(0),
         _ptr(h), _TORCH_DT[out_dtype], B * Lr, Lr, D, float(eps), ct.c_void_p(_stream())),
         "anima_dit_gate_residual_ln_modulate")
     return h

@@ -25,10 +25,10 @@ int ln_modulate_launch(const float* x, const float* scale, const float* shift, l
 int gate_residual_launch(float* x, const float* gate, long long gate_stride, const float* y,
                          long long rows, int rows_per_b, int D, int sm_count, cudaStream_t st);
 int gate_residual_ln_modulate_launch(float* x, const float* gate, long long gate_stride,
-                                     const float* y, const float* scale, const float* shift,
-                                     long long mod_stride, void* h, int out_dtype, long long rows,
-                                     int rows_per_b, int D, float eps, int sm_count,
-                                     cudaStream_t st);
+                                     const void* y, int y_dtype, const float* scale,
+                                     const float* shift, long long mod_stride, void* h,
+                                     int out_dtype, long long rows, int rows_per_b, int D,
+                                     float eps, int sm_count, cudaStream_t st);
 int gelu16_launch(const void* x, void* y, int dtype, long long n, int sm_count, cudaStream_t st);
 int attn_fwd_launch_noalloc(const AnimaAttnArgs* a, int* status, int sm_count, cudaStream_t st,
                             const char** why);
@@ -449,9 +449,10 @@ int anima_dit_gate_residual(float* x, const float* gate, int64_t gate_stride_b, 
 }
 
 int anima_dit_gate_residual_ln_modulate(float* x, const float* gate, int64_t gate_stride_b,
-                                        const float* y, const float* scale, const float* shift,
-                                        int64_t mod_stride_b, void* h, int out_dtype, int64_t rows,
-                                        int rows_per_b, int D, float eps, void* stream) {
+                                        const void* y, int y_dtype, const float* scale,
+                                        const float* shift, int64_t mod_stride_b, void* h,
+                                        int out_dtype, int64_t rows, int rows_per_b, int D,
+                                        float eps, void* stream) {
   if (!x || !gate || !y || !scale || !shift || !h || rows < 0 || rows_per_b <= 0 ||
       gate_stride_b % 4 || mod_stride_b % 4)
     return ANIMA_ERR_ARG;
@@ -461,9 +462,9 @@ int anima_dit_gate_residual_ln_modulate(float* x, const float* gate, int64_t gat
   int rc = ANIMA_OK;
   DeviceState* d = current_device(&rc);
   if (!d) return rc;
-  return gate_residual_ln_modulate_launch(x, gate, gate_stride_b, y, scale, shift, mod_stride_b,
-                                          h, out_dtype, rows, rows_per_b, D, eps, d->sm_count,
-                                          static_cast<cudaStream_t>(stream));
+  return gate_residual_ln_modulate_launch(x, gate, gate_stride_b, y, y_dtype, scale, shift,
+                                          mod_stride_b, h, out_dtype, rows, rows_per_b, D, eps,
+                                          d->sm_count, static_cast<cudaStream_t>(stream));
 }
 
 int anima_dit_gelu(const void* x, void* y, int dtype, int64_t n, void* stream) {

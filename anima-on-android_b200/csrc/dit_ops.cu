@@ -92,14 +92,34 @@ __global__ void __launch_bounds__(256)
   }
 }
 
+// Four consecutive elements of y as fp32 (y fp32, fp16 or bf16).
+template <int kY>
+__device__ __forceinline__ float4 load_y4(const void* y, long long idx4) {
+  if constexpr (kY == ANIMA_DTYPE_F32) {
+    return reinterpret_cast<const float4*>(y)[idx4];
+  } else {
+    const uint2 u = reinterpret_cast<const uint2*>(y)[idx4];
+    float2 a, b;
+    if constexpr (kY == ANIMA_DTYPE_F16) {
+      a = __half22float2(*reinterpret_cast<const __half2*>(&u.x));
+      b = __half22float2(*reinterpret_cast<const __half2*>(&u.y));
+    } else {
+      a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.x));
+      b = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.y));
+    }
+    return make_float4(a.x, a.y, b.x, b.y);
+  }
+}
+
 // Fused: x[r] += gate[b] * y[r] (fp32, in place), then h[r] = LayerNorm(x[r]) * (1 +
 // scale[b]) + shift[b] as 16-bit -- the gated residual of one sub-block followed by the
 // LayerNorm + modulation that opens the next.  One warp per row; the updated row stays in
-// registers for the norm, so x is read once instead of twice.
-template <int kD, int kOut>
+// registers for the norm, so x is read once instead of twice.  y (the GEMM output being
+// added) may be fp32 or the 16-bit operand type.
+template <int kD, int kOut, int kY>
 __global__ void __launch_bounds__(256)
     gate_residual_ln_modulate_kernel(float* __restrict__ x, const float* __restrict__ gate,
-                                     long long gate_stride, const float* __restrict__ y,
+                                     long long gate_stride, const void* __restrict__ y,
                                      const float* __restrict__ scale,
                                      const float* __restrict__ shift, long long mod_stride,
                                      void* h, long long rows, int rows_per_b, float eps) {
@@ -110,13 +130,13 @@ __global__ void __launch_bounds__(256)
   for (long long r = w0; r < rows; r += nw) {
     const long long b = r / rows_per_b;
     float4* xr = reinterpret_cast<float4*>(x + r * kD);
-    const float4* yr = reinterpret_cast<const float4*>(y + r * kD);
     const float4* gr = reinterpret_cast<const float4*>(gate + b * gate_stride);
     float4 v[kV];
     float s = 0.f;
 #pragma unroll
     for (int k = 0; k < kV; ++k) {
-      const float4 a = xr[lane + 32 * k], c = yr[lane + 32 * k], g = __ldg(gr + lane + 32 * k);
+      const float4 a = xr[lane + 32 * k], g = __ldg(gr + lane + 32 * k);
+      const float4 c = load_y4<kY>(y, r * (kD / 4) + lane + 32 * k);
       v[k] = make_float4(a.x + g.x * c.x, a.y + g.y * c.y, a.z + g.z * c.z, a.w + g.w * c.w);
       xr[lane + 32 * k] = v[k];
       s += (v[k].x + v[k].y) + (v[k].z + v[k].w);
@@ -200,22 +220,43 @@ int gate_residual_launch(float* x, const float* gate, long long gate_stride, con
   return cudaGetLastError() == cudaSuccess ? ANIMA_OK : ANIMA_ERR_CUDA;
 }
 
+template <int kOut>
+static int grlm_t(float* x, const float* gate, long long gate_stride, const void* y, int y_dtype,
+                  const float* scale, const float* shift, long long mod_stride, void* h,
+                  long long rows, int rows_per_b, float eps, int grid, cudaStream_t st) {
+  switch (y_dtype) {
+    case ANIMA_DTYPE_F32:
+      gate_residual_ln_modulate_kernel<2048, kOut, ANIMA_DTYPE_F32><<<grid, 256, 0, st>>>(
+          x, gate, gate_stride, y, scale, shift, mod_stride, h, rows, rows_per_b, eps);
+      break;
+    case ANIMA_DTYPE_F16:
+      gate_residual_ln_modulate_kernel<2048, kOut, ANIMA_DTYPE_F16><<<grid, 256, 0, st>>>(
+          x, gate, gate_stride, y, scale, shift, mod_stride, h, rows, rows_per_b, eps);
+      break;
+    case ANIMA_DTYPE_BF16:
+      gate_residual_ln_modulate_kernel<2048, kOut, ANIMA_DTYPE_BF16><<<grid, 256, 0, st>>>(
+          x, gate, gate_stride, y, scale, shift, mod_stride, h, rows, rows_per_b, eps);
+      break;
+    default:
+      return ANIMA_ERR_ARG;
+  }
+  return cudaGetLastError() == cudaSuccess ? ANIMA_OK : ANIMA_ERR_CUDA;
+}
+
 int gate_residual_ln_modulate_launch(float* x, const float* gate, long long gate_stride,
-                                     const float* y, const float* scale, const float* shift,
-                                     long long mod_stride, void* h, int out_dtype, long long rows,
-                                     int rows_per_b, int D, float eps, int sm_count,
-                                     cudaStream_t st) {
+                                     const void* y, int y_dtype, const float* scale,
+                                     const float* shift, long long mod_stride, void* h,
+                                     int out_dtype, long long rows, int rows_per_b, int D,
+                                     float eps, int sm_count, cudaStream_t st) {
   if (D != 2048) return ANIMA_ERR_SHAPE;
   const int grid = grid_cap(rows, 8, sm_count, 16);
   if (out_dtype == ANIMA_DTYPE_F16)
-    gate_residual_ln_modulate_kernel<2048, ANIMA_DTYPE_F16><<<grid, 256, 0, st>>>(
-        x, gate, gate_stride, y, scale, shift, mod_stride, h, rows, rows_per_b, eps);
-  else if (out_dtype == ANIMA_DTYPE_BF16)
-    gate_residual_ln_modulate_kernel<2048, ANIMA_DTYPE_BF16><<<grid, 256, 0, st>>>(
-        x, gate, gate_stride, y, scale, shift, mod_stride, h, rows, rows_per_b, eps);
-  else
-    return ANIMA_ERR_ARG;
-  return cudaGetLastError() == cudaSuccess ? ANIMA_OK : ANIMA_ERR_CUDA;
+    return grlm_t<ANIMA_DTYPE_F16>(x, gate, gate_stride, y, y_dtype, scale, shift, mod_stride, h,
+                                   rows, rows_per_b, eps, grid, st);
+  if (out_dtype == ANIMA_DTYPE_BF16)
+    return grlm_t<ANIMA_DTYPE_BF16>(x, gate, gate_stride, y, y_dtype, scale, shift, mod_stride, h,
+                                    rows, rows_per_b, eps, grid, st);
+  return ANIMA_ERR_ARG;
 }
 
 int gelu16_launch(const void* x, void* y, int dtype, long long n, int sm_count, cudaStream_t st) {

@@ -164,13 +164,15 @@ int anima_dit_gate_residual(float* x, const float* gate, int64_t gate_stride_b, 
                             int64_t rows, int rows_per_b, int D, void* stream);
 /* anima_dit_gate_residual_ln_modulate: the two above back to back in one pass -- x += gate[b]*y
  *   in place, then h = LayerNorm(x) * (1 + scale[b]) + shift[b] as out_dtype (a sub-block's
- *   gated residual followed by the next sub-block's modulated LayerNorm, predict2.py:536-563).
+ *   gated residual followed by the next sub-block's modulated LayerNorm, predict2.py:536-563);
+ *   y of y_dtype (F32, F16 or BF16).
  * anima_dit_gelu: exact GELU (predict2.py:45, nn.GELU) on n 16-bit values (dtype F16 or BF16),
  *   n a multiple of 8, x and y 16-byte aligned (y may equal x). */
 int anima_dit_gate_residual_ln_modulate(float* x, const float* gate, int64_t gate_stride_b,
-                                        const float* y, const float* scale, const float* shift,
-                                        int64_t mod_stride_b, void* h, int out_dtype, int64_t rows,
-                                        int rows_per_b, int D, float eps, void* stream);
+                                        const void* y, int y_dtype, const float* scale,
+                                        const float* shift, int64_t mod_stride_b, void* h,
+                                        int out_dtype, int64_t rows, int rows_per_b, int D,
+                                        float eps, void* stream);
 int anima_dit_gelu(const void* x, void* y, int dtype, int64_t n, void* stream);
 
 /* Self-test of the bounded-wait path (no reference counterpart): launches one block

@@ -157,15 +157,17 @@ def test_step_graph_replay_matches_eager_step():
 
 
 @pytest.mark.gpu
-@pytest.mark.parametrize("out_dtype", [torch.float16, torch.bfloat16])
-def test_gate_residual_ln_modulate_kernel_vs_torch(out_dtype):
+@pytest.mark.parametrize("out_dtype,y_dtype", [(torch.float16, torch.float32),
+                                               (torch.bfloat16, torch.float32),
+                                               (torch.float16, torch.float16)])
+def test_gate_residual_ln_modulate_kernel_vs_torch(out_dtype, y_dtype):
     """anima_dit_gate_residual_ln_modulate: x += gate*y in place, then the modulated
-    LayerNorm of the updated x, against fp32 torch."""
+    LayerNorm of the updated x, against fp32 torch (y as the GEMM wrote it)."""
     from anima_attn.ops import gate_residual_ln_modulate_
     g = torch.Generator(device="cuda").manual_seed(9)
     B, S, D = 2, 517, 2048
     x = torch.randn(B, S, D, device="cuda", generator=g) * 2
-    y = torch.randn(B, S, D, device="cuda", generator=g)
+    y = torch.randn(B, S, D, device="cuda", generator=g).to(y_dtype)
     mods = torch.randn(B, 1, 6 * D, device="cuda", generator=g) * 0.3
     gate, _, _ = mods[:, :, :3 * D].chunk(3, dim=-1)
     sh, sc, _ = mods[:, :, 3 * D:].chunk(3, dim=-1)
