@@ -321,9 +321,10 @@ def run_dit(args, rank, world, local_rank):
                    "model_tflop_per_step": round(fl / 1e12, 2)},
         "e2e": {"value": round(e2e_ms, 3), "unit": "ms", "h2d_bytes_per_step": (hx.numel() + hcc.numel() + hcu.numel()) * 4,
                 "d2h_bytes_per_step": hout.numel() * 4},
-        # library kernels per step: per block 2 prologues, 2 attentions, 3 fused residual +
-        # LayerNorm passes, 1 GELU; plus the final layer's fused pass and the first LayerNorm
-        "gpu_launches": args.steps * (args.blocks * 8 + 2),
+        # library kernels per step: per block 2 prologues, 2 attentions, 3 LayerNorm passes
+        # (fused with the preceding residual update except the step's first), 1 GELU; plus
+        # the final layer's fused pass
+        "gpu_launches": args.steps * (args.blocks * 8 + 1),
         "clocks": clocks.summary(t_begin, t_end),
     }
 
