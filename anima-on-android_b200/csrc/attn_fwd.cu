@@ -651,51 +651,53 @@ __global__ void __launch_bounds__(kThreads, 1)
           __threadfence();
           // Merge row by row: warp `quarter` takes the tile's rows [32 quarter, 32 quarter + 32),
           // its 32 lanes spread over a row's 128 columns, so every partial load and output
-          // store is one coalesced 512-byte row; four rows are in flight per pass.
+          // store is one coalesced 512-byte row.
           const int q0 = (sg.unit % p.nqb) * kUnitRows;
           const int hh = bh % p.H;
           auto part_of = [&](int c) {
             const int lo_c = slice_lo(p, c);
             return p.part + ((long long)c * 2 + (max(t0, lo_c) == lo_c ? 0 : 1)) * kPartFloats;
           };
+          // One online pass over the partials (running max M, rescaled sum and O), eight
+          // rows per pass and two partials per loop trip, so each L2 round trip carries
+          // dozens of loads.
+          constexpr int kR = 8;
 #pragma unroll 1
-          for (int rr = 0; rr < 32; rr += 4) {
+          for (int rr = 0; rr < 32; rr += kR) {
             const int r0 = i * kBM + quarter * 32 + rr;
-            float mx[4], den[4];
-            float4 acc[4];
+            float mx[kR], den[kR];
+            float4 acc[kR];
 #pragma unroll
-            for (int k = 0; k < 4; ++k) {
+            for (int k = 0; k < kR; ++k) {
               mx[k] = -INFINITY;
               den[k] = 0.f;
               acc[k] = make_float4(0.f, 0.f, 0.f, 0.f);
             }
+#pragma unroll 2
             for (int c = c0; c <= c1; ++c) {
               const float* pc = part_of(c);
+              float mc[kR], lc[kR];
+              float4 v[kR];
 #pragma unroll
-              for (int k = 0; k < 4; ++k) mx[k] = fmaxf(mx[k], __ldcg(pc + kUnitRows * kD + r0 + k));
-            }
-            for (int c = c0; c <= c1; ++c) {
-              const float* pc = part_of(c);
-              float mc[4], lc[4];
-              float4 v[4];
-#pragma unroll
-              for (int k = 0; k < 4; ++k) {
+              for (int k = 0; k < kR; ++k) {
                 mc[k] = __ldcg(pc + kUnitRows * kD + r0 + k);
                 lc[k] = __ldcg(pc + kUnitRows * kD + kUnitRows + r0 + k);
                 v[k] = __ldcg(reinterpret_cast<const float4*>(pc + (long long)(r0 + k) * kD) + lane);
               }
 #pragma unroll
-              for (int k = 0; k < 4; ++k) {
-                const float w = exp2f(mc[k] - mx[k]);
-                den[k] += w * lc[k];
-                acc[k].x += w * v[k].x;
-                acc[k].y += w * v[k].y;
-                acc[k].z += w * v[k].z;
-                acc[k].w += w * v[k].w;
+              for (int k = 0; k < kR; ++k) {
+                const float mn = fmaxf(mx[k], mc[k]);
+                const float a = exp2f(mx[k] - mn), w = exp2f(mc[k] - mn);
+                mx[k] = mn;
+                den[k] = den[k] * a + lc[k] * w;
+                acc[k].x = acc[k].x * a + v[k].x * w;
+                acc[k].y = acc[k].y * a + v[k].y * w;
+                acc[k].z = acc[k].z * a + v[k].z * w;
+                acc[k].w = acc[k].w * a + v[k].w * w;
               }
             }
 #pragma unroll
-            for (int k = 0; k < 4; ++k) {
+            for (int k = 0; k < kR; ++k) {
               const int grow_k = q0 + r0 + k;
               if (grow_k >= p.S_q) continue;
               const float inv = den[k] > 0.f ? 1.f / den[k] : 0.f;
@@ -807,11 +809,13 @@ static SplitPlan plan_split(int bh, int S_q, int S_kv, unsigned flags, int sm_co
   if (units <= sm_count || units > 0x7fffffffLL) return sp;  // one wave: nothing to balance
   const long long rounds = units / sm_count, tail = units - rounds * sm_count;
   if (tail == 0 || tail * n > 0x7fffffffLL) return sp;         // whole rounds only
-  // Cutting the last round costs segment set-up, partial stores and merges.  Measured
-  // (B=2, H=16): split loses 25 % at 2 waves (L=2048), 8 % at 2.6, breaks even at 3.5 and
-  // gains 4 % at 5.2 waves (L=6144, 13.5 % of a unit-per-CTA grid idle in its last wave),
-  // so it is the default only from four whole rounds with >= 10 % of that wave idle.
-  const bool worth = rounds >= 4 && (rounds + 1) * sm_count * 10 >= units * 11;
+  // Cutting the last round saves the idle share of the unit grid's last wave, (sm - tail)/sm
+  // of one unit's time, and costs segment set-up, partial stores and merges, which do not
+  // grow with the unit's n key tiles.  Measured (B=2, H=16, bf16): that cost is about
+  // 0.12 + 8/n unit times (0.57 at n=16, 0.33 at n=32, 0.28 at n=48), so split is the
+  // default when the idle share exceeds it: +5.6 % at L=4096, +9.6 % at 6144, and unit mode
+  // kept at L=2048 where split would lose 15 %.
+  const bool worth = (sm_count - tail) * n * 100 > (long long)sm_count * (12 * n + 800);
   if (!(flags & ANIMA_FLAG_SPLIT) && !worth) return sp;
   sp.rounds = (int)rounds;
   sp.tail_units = (int)tail;
