@@ -68,7 +68,8 @@ constexpr float kRescaleThreshold = 8.0f;  // log2 units
 // warps that share the SM sub-partitions and sit on the critical path; 1/8 measured 14 %
 // slower, 2/8 22 %.
 constexpr int kPolyPer8 = ANIMA_POLY_PER8;
-// One partial of a split unit: O [256][128] fp32 (unnormalised), then m [256], l [256].
+// One partial of a split unit: O fp32 (unnormalised) quad-major, [32 column quads][256 rows]
+// [4], so 32 consecutive rows of one quad are 512 contiguous bytes; then m [256], l [256].
 constexpr int kPartFloats = kUnitRows * kD + 2 * kUnitRows;
 constexpr int kMinSliceTiles = 4;       // shortest key-tile slice of the last round
 constexpr int kSemBytes = 4096;         // arrival counters at the start of the workspace
@@ -76,6 +77,7 @@ constexpr int kSemBytes = 4096;         // arrival counters at the start of the 
 struct Smem {
   uint8_t q[kNT][kTile];
   uint8_t kv[kStages][kTile];
+  float4 stage[8][256];  // per softmax warp: one 32 x 32 fp32 block on its way to global
   uint64_t q_full, q_empty;
   uint64_t kv_full[kStages];
   uint64_t kv_empty[kStages];
@@ -86,7 +88,6 @@ struct Smem {
   uint64_t mma_done;
   uint32_t tmem_base;
   int abort;
-  int last[kNT];  // warpgroup i merges the cut unit it just finished
 };
 
 constexpr size_t kSmemBytes = sizeof(Smem) + 1024;  // + slack to align the base to 1 KB
@@ -215,25 +216,59 @@ __device__ __forceinline__ uint32_t pack2(float lo, float hi) {
   return kOp == ANIMA_DTYPE_BF16 ? pack_bf16x2(lo, hi) : pack_f16x2(lo, hi);
 }
 
+// True in every thread of softmax warpgroup barrier `id` if `v` is true in any of them.
+__device__ __forceinline__ bool wg_any(int id, bool v) {
+  uint32_t r;
+  asm volatile(
+      "{\n .reg .pred p, q;\n setp.ne.u32 p, %1, 0;\n bar.red.or.pred q, %2, %3, p;\n"
+      " selp.u32 %0, 1, 0, q;\n}"
+      : "=r"(r)
+      : "r"((uint32_t)v), "r"(id), "r"(kBM)
+      : "memory");
+  return r != 0;
+}
+
+// Stores columns [32 c, 32 c + 32) of the warp's 32 output rows; lane = row on entry (its
+// values v, scaled by inv).  The block goes through the warp's 4 KB staging buffer
+// (16-byte chunks XOR-swizzled by row, so neither the row-wise writes nor the transposed
+// reads conflict on banks) and leaves as whole row segments: 4 rows x 128 B per fp32 store
+// instruction, 8 rows x 64 B for 16-bit, instead of 32 scattered 16-byte pieces.  Rows
+// >= nvalid are not written.
 template <int kOut>
-__device__ __forceinline__ void store_row(char* out_row, const uint32_t (&o)[32], int c,
-                                          float inv) {
+__device__ __forceinline__ void store_block(char* out_w, long long row_bytes, int nvalid,
+                                            const float (&v)[32], int c, float inv,
+                                            float4* stage, int lane) {
   if (kOut == ANIMA_DTYPE_F32) {
-    float4* dst = reinterpret_cast<float4*>(out_row) + c * 8;
 #pragma unroll
     for (int e = 0; e < 8; ++e)
-      dst[e] = make_float4(__uint_as_float(o[4 * e]) * inv, __uint_as_float(o[4 * e + 1]) * inv,
-                           __uint_as_float(o[4 * e + 2]) * inv, __uint_as_float(o[4 * e + 3]) * inv);
+      stage[lane * 8 + (e ^ (lane & 7))] =
+          make_float4(v[4 * e] * inv, v[4 * e + 1] * inv, v[4 * e + 2] * inv, v[4 * e + 3] * inv);
+    __syncwarp();
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const int r = 4 * k + (lane >> 3), q = lane & 7;
+      const float4 x = stage[r * 8 + (q ^ (r & 7))];
+      if (r < nvalid)
+        *reinterpret_cast<float4*>(out_w + r * row_bytes + (c * 32 + q * 4) * 4) = x;
+    }
   } else {
-    uint4* dst = reinterpret_cast<uint4*>(out_row) + c * 4;
+    uint4* st = reinterpret_cast<uint4*>(stage);
 #pragma unroll
     for (int e = 0; e < 4; ++e)
-      dst[e] = make_uint4(
-          pack2<kOut>(__uint_as_float(o[8 * e]) * inv, __uint_as_float(o[8 * e + 1]) * inv),
-          pack2<kOut>(__uint_as_float(o[8 * e + 2]) * inv, __uint_as_float(o[8 * e + 3]) * inv),
-          pack2<kOut>(__uint_as_float(o[8 * e + 4]) * inv, __uint_as_float(o[8 * e + 5]) * inv),
-          pack2<kOut>(__uint_as_float(o[8 * e + 6]) * inv, __uint_as_float(o[8 * e + 7]) * inv));
+      st[lane * 4 + (e ^ ((lane >> 1) & 3))] = make_uint4(
+          pack2<kOut>(v[8 * e] * inv, v[8 * e + 1] * inv),
+          pack2<kOut>(v[8 * e + 2] * inv, v[8 * e + 3] * inv),
+          pack2<kOut>(v[8 * e + 4] * inv, v[8 * e + 5] * inv),
+          pack2<kOut>(v[8 * e + 6] * inv, v[8 * e + 7] * inv));
+    __syncwarp();
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const int r = 8 * k + (lane >> 2), q = lane & 3;
+      const uint4 x = st[r * 4 + (q ^ ((r >> 1) & 3))];
+      if (r < nvalid) *reinterpret_cast<uint4*>(out_w + r * row_bytes + (c * 32 + q * 8) * 2) = x;
+    }
   }
+  __syncwarp();  // the buffer is free for the next block
 }
 
 template <int kOp, int kOut>
@@ -602,118 +637,118 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (!(ok = __all_sync(0xffffffffu, got))) break;
         tc_fence_after();
       }
+      // The warp's first output row, and how many of its 32 rows exist.
+      constexpr int kEsize = kOut == ANIMA_DTYPE_F32 ? 4 : 2;
+      const long long row_bytes = p.os * kEsize;
+      char* const out_w = reinterpret_cast<char*>(p.out) +
+                          ((long long)b * p.ob + (long long)(bh % p.H) * p.oh +
+                           (long long)(grow - lane) * p.os) *
+                              kEsize;
+      const int nvalid = p.S_q - (grow - lane);
+      float4* const stage = sm.stage[warp];
       if (sg.full) {
         const float inv = (l > 0.f) ? 1.f / l : 0.f;
-        char* out_row = reinterpret_cast<char*>(p.out) +
-                        ((long long)b * p.ob + (long long)(bh % p.H) * p.oh +
-                         (long long)grow * p.os) *
-                            (kOut == ANIMA_DTYPE_F32 ? 4 : 2);
 #pragma unroll 1
         for (int c = 0; c < 4; ++c) {
-          uint32_t o[32];
+          float v[32];
           if (n > 0) {
+            uint32_t o[32];
             tmem_ld32(tO + c * 32, o);
             tmem_ld_wait();
+#pragma unroll
+            for (int e = 0; e < 32; ++e) v[e] = __uint_as_float(o[e]);
           } else {
 #pragma unroll
-            for (int e = 0; e < 32; ++e) o[e] = 0u;
+            for (int e = 0; e < 32; ++e) v[e] = 0.f;
           }
-          if (grow < p.S_q) store_row<kOut>(out_row, o, c, inv);
+          store_block<kOut>(out_w, row_bytes, nvalid, v, c, inv, stage, lane);
         }
       } else {
-        // A slice of a cut unit: write the raw O row, the running max it is relative to,
-        // and the running sum; then count this tile's arrival.  The warpgroup that
-        // completes the count merges every slice of the tile:
-        //   out = sum_s 2^(m_s - M) O_s / sum_s 2^(m_s - M) l_s,  M = max_s m_s.
+        // A slice of a cut unit.  The warpgroup that completes the unit tile's arrival
+        // count merges every slice of it,
+        //   out = sum_s 2^(m_s - M) O_s / sum_s 2^(m_s - M) l_s,  M = max_s m_s,
+        // its own slice straight from tensor memory and the others from their partials.
+        // A warpgroup that finds every other slice already counted is last before it
+        // stores anything, and skips its own partial.
         const int ut = sg.unit - p.tail_base;
         const int r = i * kBM + row;
-        float* part = p.part + ((long long)blockIdx.x * 2 + sg.slot) * kPartFloats;
-        char* prow = reinterpret_cast<char*>(part + (long long)r * kD);
-#pragma unroll 1
-        for (int c = 0; c < 4; ++c) {
-          uint32_t o[32];
-          tmem_ld32(tO + c * 32, o);
-          tmem_ld_wait();
-          store_row<ANIMA_DTYPE_F32>(prow, o, c, 1.f);
-        }
-        part[kUnitRows * kD + r] = m;
-        part[kUnitRows * kD + kUnitRows + r] = l;
         const int t0 = ut * p.n_kv, t1 = t0 + p.n_kv;
         const int c0 = slice_of(p, t0), c1 = slice_of(p, t1 - 1);
-        __threadfence();
-        wg_sync(1 + i);
-        if (row == 0) {
-          const int prev = atomicAdd(&p.sem[ut * kNT + i], 1);
-          sm.last[i] = (prev == c1 - c0) ? 1 : 0;
-        }
-        wg_sync(1 + i);
-        if (sm.last[i]) {
-          __threadfence();
-          // Merge row by row: warp `quarter` takes the tile's rows [32 quarter, 32 quarter + 32),
-          // its 32 lanes spread over a row's 128 columns, so every partial load and output
-          // store is one coalesced 512-byte row.
-          const int q0 = (sg.unit % p.nqb) * kUnitRows;
-          const int hh = bh % p.H;
-          auto part_of = [&](int c) {
-            const int lo_c = slice_lo(p, c);
-            return p.part + ((long long)c * 2 + (max(t0, lo_c) == lo_c ? 0 : 1)) * kPartFloats;
-          };
-          // One online pass over the partials (running max M, rescaled sum and O), eight
-          // rows per pass and two partials per loop trip, so each L2 round trip carries
-          // dozens of loads.
-          constexpr int kR = 8;
+        const int me = blockIdx.x;
+        int* const cnt = &p.sem[ut * kNT + i];
+        auto part_of = [&](int c) {
+          const int lo_c = slice_lo(p, c);
+          return p.part + ((long long)c * 2 + (max(t0, lo_c) == lo_c ? 0 : 1)) * kPartFloats;
+        };
+        bool last = wg_any(1 + i, row == 0 && *reinterpret_cast<volatile int*>(cnt) == c1 - c0);
+        if (!last) {
+          float* const part = part_of(me);
+          float4* const dst = reinterpret_cast<float4*>(part) + r;
 #pragma unroll 1
-          for (int rr = 0; rr < 32; rr += kR) {
-            const int r0 = i * kBM + quarter * 32 + rr;
-            float mx[kR], den[kR];
-            float4 acc[kR];
+          for (int c = 0; c < 4; ++c) {
+            uint32_t o[32];
+            tmem_ld32(tO + c * 32, o);
+            tmem_ld_wait();
 #pragma unroll
-            for (int k = 0; k < kR; ++k) {
-              mx[k] = -INFINITY;
-              den[k] = 0.f;
-              acc[k] = make_float4(0.f, 0.f, 0.f, 0.f);
-            }
-#pragma unroll 2
-            for (int c = c0; c <= c1; ++c) {
-              const float* pc = part_of(c);
-              float mc[kR], lc[kR];
-              float4 v[kR];
-#pragma unroll
-              for (int k = 0; k < kR; ++k) {
-                mc[k] = __ldcg(pc + kUnitRows * kD + r0 + k);
-                lc[k] = __ldcg(pc + kUnitRows * kD + kUnitRows + r0 + k);
-                v[k] = __ldcg(reinterpret_cast<const float4*>(pc + (long long)(r0 + k) * kD) + lane);
-              }
-#pragma unroll
-              for (int k = 0; k < kR; ++k) {
-                const float mn = fmaxf(mx[k], mc[k]);
-                const float a = exp2f(mx[k] - mn), w = exp2f(mc[k] - mn);
-                mx[k] = mn;
-                den[k] = den[k] * a + lc[k] * w;
-                acc[k].x = acc[k].x * a + v[k].x * w;
-                acc[k].y = acc[k].y * a + v[k].y * w;
-                acc[k].z = acc[k].z * a + v[k].z * w;
-                acc[k].w = acc[k].w * a + v[k].w * w;
-              }
-            }
-#pragma unroll
-            for (int k = 0; k < kR; ++k) {
-              const int grow_k = q0 + r0 + k;
-              if (grow_k >= p.S_q) continue;
-              const float inv = den[k] > 0.f ? 1.f / den[k] : 0.f;
-              const long long off =
-                  (long long)b * p.ob + (long long)hh * p.oh + (long long)grow_k * p.os + lane * 4;
-              if (kOut == ANIMA_DTYPE_F32) {
-                *reinterpret_cast<float4*>(reinterpret_cast<float*>(p.out) + off) =
-                    make_float4(acc[k].x * inv, acc[k].y * inv, acc[k].z * inv, acc[k].w * inv);
-              } else {
-                *reinterpret_cast<uint2*>(reinterpret_cast<uint16_t*>(p.out) + off) =
-                    make_uint2(pack2<kOut>(acc[k].x * inv, acc[k].y * inv),
-                               pack2<kOut>(acc[k].z * inv, acc[k].w * inv));
-              }
-            }
+            for (int e = 0; e < 8; ++e)
+              dst[(c * 8 + e) * kUnitRows] =
+                  make_float4(__uint_as_float(o[4 * e]), __uint_as_float(o[4 * e + 1]),
+                              __uint_as_float(o[4 * e + 2]), __uint_as_float(o[4 * e + 3]));
           }
-          if (row == 0) p.sem[ut * kNT + i] = 0;  // leave the counter zero for the next call
+          part[kUnitRows * kD + r] = m;
+          part[kUnitRows * kD + kUnitRows + r] = l;
+          __threadfence();
+          wg_sync(1 + i);
+          int prev = 0;
+          if (row == 0) prev = atomicAdd(cnt, 1);
+          last = wg_any(1 + i, row == 0 && prev == c1 - c0);
+        }
+        if (last) {
+          __threadfence();
+          const int nothers = c1 - c0;  // this CTA is one of the unit's slices
+          auto other = [&](int k) { return c0 + k + (c0 + k >= me ? 1 : 0); };
+          // Pass 1: M and the denominator over all slices of this row.
+          float M = m, den = l;
+#pragma unroll 2
+          for (int k = 0; k < nothers; ++k) {
+            const float* pc = part_of(other(k));
+            const float mc = __ldcg(pc + kUnitRows * kD + r);
+            const float lc = __ldcg(pc + kUnitRows * kD + kUnitRows + r);
+            const float mn = fmaxf(M, mc);
+            den = den * exp2f(M - mn) + lc * exp2f(mc - mn);
+            M = mn;
+          }
+          const float inv = den > 0.f ? 1.f / den : 0.f;
+          const float w_own = exp2f(m - M) * inv;
+          // Pass 2, 32 columns at a time: own O from tensor memory, every other slice's
+          // quad-major rows (one 512-byte run per warp load).
+#pragma unroll 1
+          for (int c = 0; c < 4; ++c) {
+            uint32_t o[32];
+            tmem_ld32(tO + c * 32, o);
+            tmem_ld_wait();
+            float v[32];
+#pragma unroll
+            for (int e = 0; e < 32; ++e) v[e] = __uint_as_float(o[e]) * w_own;
+#pragma unroll 2
+            for (int k = 0; k < nothers; ++k) {
+              const float* pc = part_of(other(k));
+              const float wc = exp2f(__ldcg(pc + kUnitRows * kD + r) - M) * inv;
+              const float4* src = reinterpret_cast<const float4*>(pc) + c * 8 * kUnitRows + r;
+              float4 x[8];
+#pragma unroll
+              for (int e = 0; e < 8; ++e) x[e] = __ldcg(src + e * kUnitRows);
+#pragma unroll
+              for (int e = 0; e < 8; ++e) {
+                v[4 * e] += wc * x[e].x;
+                v[4 * e + 1] += wc * x[e].y;
+                v[4 * e + 2] += wc * x[e].z;
+                v[4 * e + 3] += wc * x[e].w;
+              }
+            }
+            store_block<kOut>(out_w, row_bytes, nvalid, v, c, 1.f, stage, lane);
+          }
+          if (row == 0) *cnt = 0;  // leave the counter zero for the next call
         }
       }
       if (n > 0) {
@@ -811,11 +846,11 @@ static SplitPlan plan_split(int bh, int S_q, int S_kv, unsigned flags, int sm_co
   if (tail == 0 || tail * n > 0x7fffffffLL) return sp;         // whole rounds only
   // Cutting the last round saves the idle share of the unit grid's last wave, (sm - tail)/sm
   // of one unit's time, and costs segment set-up, partial stores and merges, which do not
-  // grow with the unit's n key tiles.  Measured (B=2, H=16, bf16): that cost is about
-  // 0.12 + 8/n unit times (0.57 at n=16, 0.33 at n=32, 0.28 at n=48), so split is the
-  // default when the idle share exceeds it: +5.6 % at L=4096, +9.6 % at 6144, and unit mode
-  // kept at L=2048 where split would lose 15 %.
-  const bool worth = (sm_count - tail) * n * 100 > (long long)sm_count * (12 * n + 800);
+  // grow with the unit's n key tiles.  Split is the default when the idle share exceeds
+  // 0.15 + 5/n: with B=2, H=16, bf16 that picks the faster schedule at every length measured
+  // (split at L = 2560, 3072, 4096, 5120, 6144; unit at 2048, 8192, 16384, where the idle
+  // share is 0.27, 0.08 and 0.16).
+  const bool worth = (sm_count - tail) * n * 100 > (long long)sm_count * (15 * n + 500);
   if (!(flags & ANIMA_FLAG_SPLIT) && !worth) return sp;
   sp.rounds = (int)rounds;
   sp.tail_units = (int)tail;
