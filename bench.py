@@ -240,7 +240,11 @@ def run_dit(args, rank, world, local_rank):
     if world > 1:
         import torch.distributed as dist
         group = dist.group.WORLD
-    weights = make_weights(cfg, seed=1234, device=dev, rng_device=dev)
+    if args.weights:
+        from anima_attn.checkpoint import load_dit_weights
+        weights = load_dit_weights(args.weights, cfg, device=dev)
+    else:
+        weights = make_weights(cfg, seed=1234, device=dev, rng_device=dev)
     model = AnimaDiT(cfg, weights, rank=rank, world=world, group=group, shard=args.dit_shard)
     del weights
     side = args.latent
@@ -309,7 +313,9 @@ def run_dit(args, rank, world, local_rank):
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 3),
         "higher_is_better": False, "scaling": "strong", "vs_baseline": None,
         "dtype": "fp16 GEMM/attention operands, fp32 activations",
-        "data": "synthetic (seeded latent and context, N(0,0.02) bf16-valued weights)",
+        "data": ("synthetic (seeded latent and context, N(0,0.02) bf16-valued weights)"
+                 if not args.weights else
+                 f"synthetic latent and context; weights from {os.path.basename(args.weights)}"),
         "config": {"workload": f"Anima DiT Euler+CFG step, {args.blocks} blocks, latent "
                                f"16x{side}x{side} ({L} tokens), context 512x1024, CFG pair",
                    "global_batch": 2, "seq_len": L,
@@ -483,6 +489,8 @@ def main():
     ap.add_argument("--graph", type=int, choices=[0, 1], default=1,
                     help="dit workload: replay the step as one captured CUDA graph (1) or issue "
                          "it op by op from Python (0)")
+    ap.add_argument("--weights", default=None,
+                    help="dit workload: safetensors checkpoint of the model (default: seeded weights)")
     ap.add_argument("--dit-shard", choices=["tokens", "heads"], default="tokens",
                     help="dit workload on N GPUs: heads = all-gather of head outputs before a "
                          "replicated o-proj; tokens = rows split over ranks, all-to-all around "
