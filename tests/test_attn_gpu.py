@@ -244,6 +244,34 @@ def test_stream_k_schedule_matches_unit_schedule_and_oracle(aa, O, Sq, Skv):
     assert rel_l2(s_np, u_np) < ATTN_REL_L2
 
 
+@pytest.mark.parametrize("out_dtype", ["bf16", "f16"])
+def test_split_schedule_16bit_strided_output(aa, O, out_dtype):
+    """Split schedule writing 16-bit output into a token-major [B, S, H, D] tensor (row
+    stride H*D): the epilogue's staged block stores and the merge of cut units both write
+    through it.  S_q = 1200 leaves the last unit's last warps with 16 and 0 valid rows, and
+    S_kv = 777 a partial key tile."""
+    from anima_attn import _lib as L
+    B, H, Sq, Skv = 2, 16, 1200, 777
+    rng = np.random.default_rng(11)
+    q = rng.standard_normal((B * H, Sq, 128), dtype=np.float32)
+    k = rng.standard_normal((B * H, Skv, 128), dtype=np.float32)
+    v = rng.standard_normal((B * H, Skv, 128), dtype=np.float32)
+    assert L.lib.anima_attn_workspace_size(B, H, Sq, Skv, L.FLAG_SPLIT) > 0
+    tdt = {"bf16": torch.bfloat16, "f16": torch.float16}[out_dtype]
+    qh, kh, vh = (_dev(t).to(torch.bfloat16) for t in (q, k, v))
+    split = aa.attention_core(qh, kh, vh, B, H, out_dtype=tdt, force_split=True)
+    unit = aa.attention_core(qh, kh, vh, B, H, out_dtype=tdt, stream_k=False)
+    torch.cuda.synchronize()
+    assert aa.status() == 0
+    s_np = split.float().cpu().numpy().transpose(0, 2, 1, 3)  # -> [B, H, S, D]
+    u_np = unit.float().cpu().numpy().transpose(0, 2, 1, 3)
+    rows = np.concatenate([np.arange(0, 40), np.arange(1140, 1200)])
+    ref = O.sdpa(q[:, rows], k, v, threads=8).reshape(B, H, len(rows), 128)
+    _ok(s_np[:, :, rows], ref, rel=8e-3)  # 16-bit output adds its rounding
+    _ok(u_np[:, :, rows], ref, rel=8e-3)
+    assert rel_l2(s_np, u_np) < 8e-3
+
+
 # ------------------------------------------------------------------ benchmark configurations
 def test_config1_self_attention_256(aa, O):
     rng = np.random.default_rng(0)
