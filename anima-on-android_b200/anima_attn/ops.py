@@ -120,16 +120,16 @@ def attention_core(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, B: int, H:
                    scale: Optional[float] = None, kv_valid_len: Optional[torch.Tensor] = None,
                    causal: bool = False, out: Optional[torch.Tensor] = None,
                    out_layout: str = "bshd", out_dtype=torch.float32,
-                   stream_k: bool = True, pair: bool = False,
-                   force_split: bool = False) -> torch.Tensor:
+                   schedule: str = "auto", pair: bool = False) -> torch.Tensor:
     """tcgen05 flash attention on 16-bit head-major operands.
 
     q [B*H, S_q, 128], k/v [B*H, S_kv, 128] contiguous bf16/fp16.  Returns (or fills)
     ``out`` in ``out_layout`` "bshd" [B, S_q, H, D] or "bhsd" [B, H, S_q, D].
     ``kv_valid_len`` int32 [B] masks keys >= kv_valid_len[b] (cross-attention padding).
-    ``stream_k`` lets the library pick the persistent split schedule (with a cached
-    workspace) where it is faster; False forces one CTA per 256-row unit;
-    ``force_split`` uses the split schedule for every call of more than one wave.
+    ``schedule`` for calls of more than one wave of 256-row units: "auto" lets the library
+    choose (a cached workspace is passed for the cut last round); "unit" one CTA per unit;
+    "whole" a persistent grid of whole units; "split" the persistent grid with the last
+    round cut into key-tile slices.
     ``pair`` runs the CTA-pair kernel (2-SM MMA, one pair per 512-row unit).
     """
     _check_cuda(q, k, v)
@@ -153,8 +153,10 @@ def attention_core(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, B: int, H:
     if out.stride(3) != 1:
         raise ValueError("output head dimension must be contiguous")
     flags = (L.FLAG_CAUSAL if causal else 0) | (L.FLAG_PAIR if pair else 0)
-    if force_split:
-        flags |= L.FLAG_SPLIT
+    if schedule not in ("auto", "unit", "whole", "split"):
+        raise ValueError("schedule must be 'auto', 'unit', 'whole' or 'split'")
+    flags |= {"auto": 0, "unit": L.FLAG_UNIT, "whole": L.FLAG_WHOLE,
+              "split": L.FLAG_SPLIT}[schedule]
     vl = None
     if kv_valid_len is not None:
         vl = kv_valid_len.to(device=q.device, dtype=torch.int32).contiguous()
@@ -172,7 +174,7 @@ def attention_core(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, B: int, H:
     a.flags = flags
     a.kv_valid_len = _ptr(vl)
     ws = None
-    if (stream_k or force_split) and not pair:
+    if schedule in ("auto", "split") and not pair:
         ws = _workspace(q.device, int(L.lib.anima_attn_workspace_size(B, H, Sq, Skv, flags)))
     a.workspace = _ptr(ws)
     a.workspace_bytes = 0 if ws is None else ws.numel()

@@ -5,13 +5,14 @@
 // (batch, head), D = 128.
 //
 // Work unit = 256 query rows (two 128-row tiles) of one (batch, head) against its keys,
-// streamed in 128-key tiles.  Two schedules share one kernel:
-//   unit mode    one CTA per unit (masked / causal calls, at most one wave, or where
-//                cutting the last round does not pay -- see plan_split);
-//   split mode   a persistent grid of one CTA per SM.  Whole units are dealt round-robin
+// streamed in 128-key tiles.  Three schedules share one kernel (plan_split chooses):
+//   unit         one CTA per unit (masked / causal calls, at most one wave, and long
+//                units, where the hardware's dynamic hand-out of CTAs balances best);
+//   whole        a persistent grid of one CTA per SM.  Whole units are dealt round-robin
 //                (CTA c takes units c, c+G, ...), so the CTAs in flight share heads and
-//                their K/V stay in L2; the units of the last, partial round are cut into
-//                equal slices of key tiles spread over all CTAs, so that round is not
+//                their K/V stay in L2, and a CTA moves to its next unit without start-up;
+//   cut          whole-unit rounds as above, and the units of the last, partial round cut
+//                into equal slices of key tiles spread over all CTAs, so that round is not
 //                left half idle.  A CTA holding a slice writes an fp32 partial (O, running
 //                max, running sum); the last warpgroup to finish a cut unit, told by an
 //                arrival counter, merges the partials and writes the output.  No CTA waits
@@ -102,9 +103,10 @@ struct Params {
   long long ob, oh, os;
   int* status;
   int nqb;             // query units per (batch, head)
-  int split;           // 1: split mode (persistent, last round cut into slices)
+  int units;           // B * H * nqb
+  int split;           // 1: persistent grid (whole-unit rounds, then the cut last round)
   int n_kv;            // key tiles per unit (split mode)
-  int rounds;          // whole-unit rounds: CTA c owns units c + r * gridDim.x
+  int rounds;          // whole-unit rounds: CTA c owns units c + r * gridDim.x (< units)
   int tail_base;       // first unit of the cut last round (rounds * gridDim.x)
   int tail_tiles;      // key-tile steps of the last round
   int tail_ctas;       // CTAs sharing the last round (<= gridDim.x)
@@ -176,12 +178,15 @@ struct SegIter {
     const int n = p.n_kv;
     if (r < p.rounds) {
       s.unit = blockIdx.x + r * gridDim.x;
-      s.k0 = 0;
-      s.k1 = n;
-      s.full = 1;
-      s.slot = 0;
       ++r;
-      return true;
+      if (s.unit < p.units) {
+        s.k0 = 0;
+        s.k1 = n;
+        s.full = 1;
+        s.slot = 0;
+        return true;
+      }
+      r = p.rounds;  // the last whole round leaves this CTA out
     }
     if (t >= hi) return false;
     const int ut = t / n;
@@ -830,28 +835,48 @@ static int launch_t(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensor
   return cudaGetLastError() == cudaSuccess ? ANIMA_OK : ANIMA_ERR_CUDA;
 }
 
-// Split-mode plan for a call: whole-unit rounds plus the last round cut into slices.
+// Schedule of a call: one CTA per unit, or a persistent grid of whole-unit rounds, or
+// whole-unit rounds plus the last round cut into slices (needs `bytes` of workspace).
+enum { kSchedUnit = 0, kSchedWhole = 1, kSchedCut = 2 };
 struct SplitPlan {
-  int rounds, tail_units, tail_tiles, tail_ctas;
-  size_t bytes;  // workspace: counters + partial slots (0: use unit mode)
+  int mode, rounds, tail_units, tail_tiles, tail_ctas;
+  size_t bytes;  // workspace: counters + partial slots (kSchedCut only)
 };
 
-static SplitPlan plan_split(int bh, int S_q, int S_kv, unsigned flags, int sm_count) {
-  SplitPlan sp = {0, 0, 0, 0, 0};
-  if (flags & (ANIMA_FLAG_MASK | ANIMA_FLAG_CAUSAL) || sm_count < 2) return sp;
+// allow_cut = false plans for a call without a usable workspace.
+static SplitPlan plan_split(int bh, int S_q, int S_kv, unsigned flags, int sm_count,
+                            bool allow_cut = true) {
+  SplitPlan sp = {kSchedUnit, 0, 0, 0, 0, 0};
+  if (flags & (ANIMA_FLAG_MASK | ANIMA_FLAG_CAUSAL | ANIMA_FLAG_UNIT) || sm_count < 2)
+    return sp;  // masked / causal units differ in length: the hardware balances them
   const long long units = (long long)bh * ((S_q + attn::kUnitRows - 1) / attn::kUnitRows);
   const long long n = (S_kv + attn::kBN - 1) / attn::kBN;
-  if (units <= sm_count || units > 0x7fffffffLL) return sp;  // one wave: nothing to balance
+  if (units <= sm_count || units > 0x7fffffffLL) return sp;  // one wave
   const long long rounds = units / sm_count, tail = units - rounds * sm_count;
-  if (tail == 0 || tail * n > 0x7fffffffLL) return sp;         // whole rounds only
+  // Persistent grid of whole units: a CTA moves from unit to unit without its start-up
+  // (TMEM allocation, barrier set-up, the first Q and K loads from DRAM) and with the next
+  // unit's K/V already streaming, ~1.5 key-tile steps less overhead per unit than one CTA
+  // per unit; but the units are dealt statically, while the hardware hands one-CTA units
+  // to whichever SM is free, and that balance is worth ~4 %.  Measured (B=2, H=16):
+  // whole units win for short units (n = 4: +13 %, 8: +9 %, 16: +3-4 %, 32: +1 %) and lose
+  // for long ones (48: -0.7 %, 64: -1.5 %, 128: -3.4 %), so without a cut the plan takes
+  // whole units up to n = 32 key tiles and one CTA per unit beyond.
+  SplitPlan whole = sp;
+  whole.mode = kSchedWhole;
+  whole.rounds = (int)((units + sm_count - 1) / sm_count);
+  if (flags & ANIMA_FLAG_WHOLE) return whole;
+  const SplitPlan nocut = (n <= 32) ? whole : sp;
+  if (!allow_cut || tail == 0 || tail * n > 0x7fffffffLL) return nocut;  // whole rounds
+  if (2LL * tail * (long long)sizeof(int) > attn::kSemBytes) return nocut;
   // Cutting the last round saves the idle share of the unit grid's last wave, (sm - tail)/sm
   // of one unit's time, and costs segment set-up, partial stores and merges, which do not
-  // grow with the unit's n key tiles.  Split is the default when the idle share exceeds
-  // 0.15 + 5/n: with B=2, H=16, bf16 that picks the faster schedule at every length measured
-  // (split at L = 2560, 3072, 4096, 5120, 6144; unit at 2048, 8192, 16384, where the idle
-  // share is 0.27, 0.08 and 0.16).
+  // grow with the unit's n key tiles.  The cut is the default when the idle share exceeds
+  // 0.15 + 5/n: with B=2, H=16, bf16 that picks the faster schedule at every shape measured
+  // (cut at L = 2560, 3072, 4096, 5120, 6144 and S_q x S_kv = 4096 x 2048; not at 2048,
+  // 8192, 16384, where the idle share is 0.27, 0.08 and 0.16, nor at 4096 x 512 / 1024).
   const bool worth = (sm_count - tail) * n * 100 > (long long)sm_count * (15 * n + 500);
-  if (!(flags & ANIMA_FLAG_SPLIT) && !worth) return sp;
+  if (!(flags & ANIMA_FLAG_SPLIT) && !worth) return nocut;
+  sp.mode = kSchedCut;
   sp.rounds = (int)rounds;
   sp.tail_units = (int)tail;
   sp.tail_tiles = (int)(tail * n);
@@ -859,7 +884,6 @@ static SplitPlan plan_split(int bh, int S_q, int S_kv, unsigned flags, int sm_co
   if (ctas > sm_count) ctas = sm_count;
   if (ctas < 1) ctas = 1;
   sp.tail_ctas = (int)ctas;
-  if (2LL * tail * (long long)sizeof(int) > attn::kSemBytes) return SplitPlan{0, 0, 0, 0, 0};
   sp.bytes = attn::kSemBytes + (size_t)ctas * 2 * attn::kPartFloats * sizeof(float);
   return sp;
 }
@@ -898,15 +922,17 @@ int attn_fwd_launch(const AnimaAttnArgs* a, int* status, int sm_count, cudaStrea
   prm.n_kv = (a->S_kv + attn::kBN - 1) / attn::kBN;
   const long long units = (long long)bh * prm.nqb;
   if (units > 0x7fffffffLL) return ANIMA_ERR_SHAPE;
-  const SplitPlan sp = plan_split(bh, a->S_q, a->S_kv, a->flags, sm_count);
-  prm.split = (sp.bytes > 0 && a->workspace && a->workspace_bytes >= sp.bytes &&
-               (reinterpret_cast<uintptr_t>(a->workspace) & 255u) == 0)
-                  ? 1
-                  : 0;
+  prm.units = (int)units;
+  SplitPlan sp = plan_split(bh, a->S_q, a->S_kv, a->flags, sm_count);
+  if (sp.mode == kSchedCut &&
+      !(a->workspace && a->workspace_bytes >= sp.bytes &&
+        (reinterpret_cast<uintptr_t>(a->workspace) & 255u) == 0))
+    sp = plan_split(bh, a->S_q, a->S_kv, a->flags, sm_count, false);
+  prm.split = sp.mode != kSchedUnit ? 1 : 0;
   prm.rounds = sp.rounds;
-  prm.tail_base = sp.rounds * sm_count;
-  prm.tail_tiles = sp.tail_tiles;
-  prm.tail_ctas = sp.tail_ctas;
+  prm.tail_base = sp.mode == kSchedCut ? sp.rounds * sm_count : (int)units;
+  prm.tail_tiles = sp.mode == kSchedCut ? sp.tail_tiles : 0;
+  prm.tail_ctas = sp.mode == kSchedCut ? sp.tail_ctas : 0;
   prm.sem = static_cast<int*>(a->workspace);
   prm.part = reinterpret_cast<float*>(static_cast<char*>(a->workspace) + attn::kSemBytes);
   const int grid = prm.split ? sm_count : (int)units;

@@ -363,8 +363,7 @@ def run_ours(args, rank, world, local_rank):
         if evs is not None:
             evs[1].record(stream)
         anima_attn.attention_core(qh, kh, vh, B, heads, out=out,
-                                  stream_k=(args.schedule == "auto"),
-                                  force_split=(args.schedule == "split"))
+                                  schedule=args.schedule)
         if evs is not None:
             evs[2].record(stream)
 
@@ -495,10 +494,11 @@ def main():
                     help="dit workload on N GPUs: heads = all-gather of head outputs before a "
                          "replicated o-proj; tokens = rows split over ranks, all-to-all around "
                          "the head-parallel attention")
-    ap.add_argument("--schedule", choices=["auto", "unit", "split"], default="auto",
-                    help="auto: the library's choice (persistent split schedule only where it "
-                         "measured faster); unit: one CTA per 256-row unit; split: persistent "
-                         "split schedule for every call of more than one wave")
+    ap.add_argument("--schedule", choices=["auto", "unit", "whole", "split"], default="auto",
+                    help="attention schedule for calls of more than one wave of 256-row units: "
+                         "auto: the library's choice; unit: one CTA per unit; whole: persistent "
+                         "grid of whole units; split: persistent grid, last round cut into "
+                         "key-tile slices")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()

@@ -48,12 +48,13 @@ enum { ANIMA_DTYPE_F32 = 0, ANIMA_DTYPE_BF16 = 1, ANIMA_DTYPE_F16 = 2 };
 #define ANIMA_FLAG_CAUSAL 0x10u /* top-left causal mask (col <= row)      */
 #define ANIMA_FLAG_PAIR 0x20u  /* anima_attn_fwd: run on CTA pairs (2-SM MMA), one pair per
                                   512-row unit                             */
-#define ANIMA_FLAG_SPLIT 0x40u /* anima_attn_fwd(_noalloc): use the persistent split schedule
-                                  whenever the call spans more than one wave of 256-row units.
-                                  Without it the split schedule is used only where it measured
-                                  faster than one CTA per unit: at least four whole rounds with
-                                  at least 10 % of a unit-per-CTA grid's last wave idle.
-                                  anima_attn_workspace_size takes the same flag. */
+/* Schedule overrides of anima_attn_fwd(_noalloc) for calls that span more than one wave of
+ * 256-row units (the library's own choice is described at `workspace` below):            */
+#define ANIMA_FLAG_SPLIT 0x40u /* persistent grid with the last round cut into key-tile slices
+                                  (needs the workspace; anima_attn_workspace_size takes the
+                                  same flag)                                               */
+#define ANIMA_FLAG_UNIT 0x80u  /* one CTA per 256-row unit                                */
+#define ANIMA_FLAG_WHOLE 0x100u /* persistent grid, whole units only (no workspace)       */
 
 /*
  * Prologue: per-head RMSNorm + RoPE + cast, one HBM pass.
@@ -93,14 +94,17 @@ typedef struct AnimaPrologueArgs {
  *   [B, S_q, H, D] (feeds the o-proj):     {S_q*H*D, D, H*D}
  * kv_valid_len: device int32 [B], used with ANIMA_FLAG_MASK (keys >= valid are masked;
  * a sample with 0 valid keys gets a zero output).
+ * Schedule: a call of at most one wave of 256-row units, or a masked or causal call,
+ * launches one CTA per unit.  Otherwise the kernel runs persistently, one CTA per SM taking
+ * whole units round-robin, which saves the per-CTA start-up and pipeline drain of every
+ * unit; where it measured faster, the last partial round is also cut into equal slices of
+ * key tiles whose fp32 partials are merged in-kernel, which needs the workspace.
  * workspace: optional device scratch of workspace_bytes, 256-byte aligned, ZERO-FILLED
- * before its first use.  When it holds anima_attn_workspace_size() bytes and the call
- * spans more than one wave of 256-row units, the kernel runs persistently (one CTA per
- * SM): whole units round-robin, and the last partial round cut into equal slices of
- * key tiles whose fp32 partials are merged in-kernel; otherwise it launches one CTA per
- * unit.  The kernel leaves the workspace's counters (its first 4 KiB) at zero, so a
- * zero-filled workspace can be reused; after an ANIMA_ERR_TIMEOUT, zero it again.
- * Calls that share a workspace must be ordered on one stream.
+ * before its first use; anima_attn_workspace_size() gives the size the cut needs (0 when
+ * the call does not cut).  Without it the call runs whole units only.  The kernel leaves
+ * the workspace's counters (its first 4 KiB) at zero, so a zero-filled workspace can be
+ * reused; after an ANIMA_ERR_TIMEOUT, zero it again.  Calls that share a workspace must be
+ * ordered on one stream.
  */
 typedef struct AnimaAttnArgs {
   const void* q;

@@ -216,12 +216,14 @@ def test_masked_cross_attention(aa, O):
 
 
 @pytest.mark.parametrize("Sq,Skv", [(1300, 700), (4000, 3000), (1280, 128), (4096, 4096)])
-def test_stream_k_schedule_matches_unit_schedule_and_oracle(aa, O, Sq, Skv):
-    """More than one wave of 256-row units (B*H*ceil(Sq/256) > 148 SMs), with
-    ANIMA_FLAG_SPLIT, runs the persistent split schedule: whole units round-robin, the last round cut into key-tile
-    slices merged in-kernel.  Ragged Sq/Skv exercise partial query units and partial key
-    tiles; (1280, 128) has one-tile units (nothing to cut); (4096, 4096) is the bench
-    shape, whose 68 last-round units are each cut across about three CTAs."""
+def test_schedules_match_each_other_and_oracle(aa, O, Sq, Skv):
+    """More than one wave of 256-row units (B*H*ceil(Sq/256) > 148 SMs) in all three
+    schedules: one CTA per unit (ANIMA_FLAG_UNIT), the persistent grid of whole units
+    (ANIMA_FLAG_WHOLE; its last round leaves CTAs idle), and the persistent grid with the
+    last round cut into key-tile slices merged in-kernel (ANIMA_FLAG_SPLIT).  Ragged Sq/Skv
+    exercise partial query units and partial key tiles; (1280, 128) has one-tile units
+    (nothing to cut); (4096, 4096) is the bench shape, whose 68 last-round units are each
+    cut across about three CTAs."""
     from anima_attn import _lib as L
     B, H = 2, 16
     rng = np.random.default_rng(Sq + Skv)
@@ -230,11 +232,14 @@ def test_stream_k_schedule_matches_unit_schedule_and_oracle(aa, O, Sq, Skv):
     v = rng.standard_normal((B * H, Skv, 128), dtype=np.float32)
     assert L.lib.anima_attn_workspace_size(B, H, Sq, Skv, L.FLAG_SPLIT) > 0
     qh, kh, vh = (_dev(t).to(torch.bfloat16) for t in (q, k, v))
-    split = aa.attention_core(qh, kh, vh, B, H, out_layout="bhsd", force_split=True)
-    unit = aa.attention_core(qh, kh, vh, B, H, out_layout="bhsd", stream_k=False)
+    split = aa.attention_core(qh, kh, vh, B, H, out_layout="bhsd", schedule="split")
+    unit = aa.attention_core(qh, kh, vh, B, H, out_layout="bhsd", schedule="unit")
+    whole = aa.attention_core(qh, kh, vh, B, H, out_layout="bhsd", schedule="whole")
     torch.cuda.synchronize()
     assert aa.status() == 0
     s_np, u_np = split.cpu().numpy(), unit.cpu().numpy()
+    # Whole units compute exactly what one CTA per unit computes.
+    assert np.array_equal(whole.cpu().numpy(), u_np)
     rows = np.sort(rng.choice(Sq, size=min(Sq, 160), replace=False))
     ref = O.sdpa(q[:, rows], k, v, threads=8).reshape(B, H, len(rows), 128)
     # Each schedule rounds P to bf16 relative to the running max its CTA saw, so the two
@@ -259,8 +264,8 @@ def test_split_schedule_16bit_strided_output(aa, O, out_dtype):
     assert L.lib.anima_attn_workspace_size(B, H, Sq, Skv, L.FLAG_SPLIT) > 0
     tdt = {"bf16": torch.bfloat16, "f16": torch.float16}[out_dtype]
     qh, kh, vh = (_dev(t).to(torch.bfloat16) for t in (q, k, v))
-    split = aa.attention_core(qh, kh, vh, B, H, out_dtype=tdt, force_split=True)
-    unit = aa.attention_core(qh, kh, vh, B, H, out_dtype=tdt, stream_k=False)
+    split = aa.attention_core(qh, kh, vh, B, H, out_dtype=tdt, schedule="split")
+    unit = aa.attention_core(qh, kh, vh, B, H, out_dtype=tdt, schedule="unit")
     torch.cuda.synchronize()
     assert aa.status() == 0
     s_np = split.float().cpu().numpy().transpose(0, 2, 1, 3)  # -> [B, H, S, D]
