@@ -16,7 +16,7 @@ LIB_PATH = os.environ.get("ANIMA_ATTN_LIB", os.path.join(HERE, "libanima_attn.so
 OK, ERR_ARG, ERR_SHAPE, ERR_CUDA, ERR_TIMEOUT, ERR_UNSUPPORTED, ERR_NOMEM = 0, -1, -2, -3, -4, -5, -6
 DTYPE_F32, DTYPE_BF16, DTYPE_F16 = 0, 1, 2
 FLAG_QNORM, FLAG_KNORM, FLAG_ROPE, FLAG_MASK, FLAG_CAUSAL, FLAG_PAIR = 0x1, 0x2, 0x4, 0x8, 0x10, 0x20
-FLAG_SPLIT, FLAG_UNIT, FLAG_WHOLE = 0x40, 0x80, 0x100
+FLAG_SPLIT, FLAG_UNIT, FLAG_WHOLE, FLAG_KV64 = 0x40, 0x80, 0x100, 0x200
 
 ERR_NAMES = {OK: "ok", ERR_ARG: "bad argument", ERR_SHAPE: "unsupported shape",
              ERR_CUDA: "CUDA error", ERR_TIMEOUT: "device-side wait timed out",

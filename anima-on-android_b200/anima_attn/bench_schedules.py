@@ -1,6 +1,6 @@
 """Times the attention kernel's three schedules on given shapes (needs a B200).
 
-    python -m anima_attn.bench_schedules [--rounds R] SQ:SKV [SQ:SKV ...]
+    python -m anima_attn.bench_schedules [--rounds R] [--kv64] SQ:SKV [SQ:SKV ...]
 
 For each shape (B=2, H=16, bf16 operands, fp32 output) it runs the call with
 ANIMA_FLAG_UNIT (one CTA per 256-row unit), ANIMA_FLAG_WHOLE (persistent grid, whole
@@ -8,7 +8,7 @@ units), ANIMA_FLAG_SPLIT (persistent grid, last round cut into key-tile slices) 
 override (the library's choice), interleaved over R rounds so that clock drift hits all
 alike, and prints the median TFLOP/s of each.  The outputs of the schedules are checked
 against each other first.  Use it to see which schedule a shape gets and what the others
-would give.
+would give.  --kv64 times the 64-key-tile kernel (ANIMA_FLAG_KV64) instead of the default.
 """
 from __future__ import annotations
 
@@ -22,11 +22,13 @@ import torch
 from . import _lib as L
 
 
-def time_shape(Sq: int, Skv: int, rounds: int, B: int = 2, H: int = 16) -> dict:
+def time_shape(Sq: int, Skv: int, rounds: int, B: int = 2, H: int = 16,
+               kernel_flags: int = 0) -> dict:
     q = torch.randn(B * H, Sq, 128, device="cuda", dtype=torch.bfloat16)
     k, v = (torch.randn(B * H, Skv, 128, device="cuda", dtype=torch.bfloat16) for _ in range(2))
     out = torch.empty(B, Sq, H, 128, device="cuda")
-    ws = torch.zeros(max(1, int(L.lib.anima_attn_workspace_size(B, H, Sq, Skv, L.FLAG_SPLIT))),
+    ws = torch.zeros(max(1, int(L.lib.anima_attn_workspace_size(B, H, Sq, Skv,
+                                                                L.FLAG_SPLIT | kernel_flags))),
                      dtype=torch.uint8, device="cuda")
     st = ct.c_void_p(torch.cuda.current_stream().cuda_stream)
     flags = {"unit": L.FLAG_UNIT, "whole": L.FLAG_WHOLE, "split": L.FLAG_SPLIT, "auto": 0}
@@ -39,7 +41,7 @@ def time_shape(Sq: int, Skv: int, rounds: int, B: int = 2, H: int = 16) -> dict:
         a.out_stride[:] = [out.stride(0), out.stride(2), out.stride(1)]
         a.B, a.H, a.S_q, a.S_kv, a.D = B, H, Sq, Skv, 128
         a.scale = 1 / math.sqrt(128)
-        a.flags = flags[f]
+        a.flags = flags[f] | kernel_flags
         a.kv_valid_len = None
         a.workspace, a.workspace_bytes = ws.data_ptr(), ws.numel()
         return a
@@ -72,12 +74,13 @@ def time_shape(Sq: int, Skv: int, rounds: int, B: int = 2, H: int = 16) -> dict:
 def main(argv=None):
     ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
     ap.add_argument("--rounds", type=int, default=3)
+    ap.add_argument("--kv64", action="store_true", help="the 64-key-tile kernel")
     ap.add_argument("shapes", nargs="+", help="SQ:SKV")
     a = ap.parse_args(argv)
     torch.cuda.set_device(0)
     for s in a.shapes:
         Sq, Skv = (int(x) for x in s.split(":"))
-        med = time_shape(Sq, Skv, a.rounds)
+        med = time_shape(Sq, Skv, a.rounds, kernel_flags=L.FLAG_KV64 if a.kv64 else 0)
         print(f"{Sq:6d}x{Skv:<6d} " + "  ".join(f"{f} {t:7.1f}" for f, t in med.items()), flush=True)
 
 

@@ -120,7 +120,8 @@ def attention_core(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, B: int, H:
                    scale: Optional[float] = None, kv_valid_len: Optional[torch.Tensor] = None,
                    causal: bool = False, out: Optional[torch.Tensor] = None,
                    out_layout: str = "bshd", out_dtype=torch.float32,
-                   schedule: str = "auto", pair: bool = False) -> torch.Tensor:
+                   schedule: str = "auto", pair: bool = False,
+                   kv64: bool = False) -> torch.Tensor:
     """tcgen05 flash attention on 16-bit head-major operands.
 
     q [B*H, S_q, 128], k/v [B*H, S_kv, 128] contiguous bf16/fp16.  Returns (or fills)
@@ -131,6 +132,8 @@ def attention_core(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, B: int, H:
     "whole" a persistent grid of whole units; "split" the persistent grid with the last
     round cut into key-tile slices.
     ``pair`` runs the CTA-pair kernel (2-SM MMA, one pair per 512-row unit).
+    ``kv64`` runs the 64-key-tile kernel, whose P has tensor-memory columns of its own so a
+    query tile's next QK^T overlaps its softmax.
     """
     _check_cuda(q, k, v)
     BH, Sq, D = q.shape
@@ -153,6 +156,8 @@ def attention_core(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, B: int, H:
     if out.stride(3) != 1:
         raise ValueError("output head dimension must be contiguous")
     flags = (L.FLAG_CAUSAL if causal else 0) | (L.FLAG_PAIR if pair else 0)
+    if kv64:
+        flags |= L.FLAG_KV64
     if schedule not in ("auto", "unit", "whole", "split"):
         raise ValueError("schedule must be 'auto', 'unit', 'whole' or 'split'")
     flags |= {"auto": 0, "unit": L.FLAG_UNIT, "whole": L.FLAG_WHOLE,

@@ -55,6 +55,10 @@ enum { ANIMA_DTYPE_F32 = 0, ANIMA_DTYPE_BF16 = 1, ANIMA_DTYPE_F16 = 2 };
                                   same flag)                                               */
 #define ANIMA_FLAG_UNIT 0x80u  /* one CTA per 256-row unit                                */
 #define ANIMA_FLAG_WHOLE 0x100u /* persistent grid, whole units only (no workspace)       */
+/* Kernel choice of anima_attn_fwd(_noalloc): */
+#define ANIMA_FLAG_KV64 0x200u /* 64-key tiles with P in tensor-memory columns of its own,
+                                  so a query tile's next QK^T overlaps its softmax (the
+                                  default kernel uses 128-key tiles with P over S)       */
 
 /*
  * Prologue: per-head RMSNorm + RoPE + cast, one HBM pass.

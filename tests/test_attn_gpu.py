@@ -249,6 +249,51 @@ def test_schedules_match_each_other_and_oracle(aa, O, Sq, Skv):
     assert rel_l2(s_np, u_np) < ATTN_REL_L2
 
 
+KV64_CASES = [  # (B, H, Sq, Skv, causal, masked, schedule, out_dtype)
+    (1, 1, 1, 1, False, False, "auto", "f32"), (1, 2, 7, 9, False, False, "auto", "f32"),
+    (1, 2, 127, 65, False, False, "auto", "f32"), (2, 3, 300, 1000, False, False, "auto", "bf16"),
+    (1, 2, 256, 256, True, False, "auto", "f32"), (1, 1, 200, 333, True, False, "auto", "f16"),
+    (3, 2, 160, 200, False, True, "auto", "f32"),
+    (2, 16, 1300, 700, False, False, "unit", "f32"), (2, 16, 1300, 700, False, False, "whole", "f32"),
+    (2, 16, 1300, 700, False, False, "split", "f32"), (2, 16, 4096, 512, False, False, "auto", "f16"),
+    (2, 16, 4096, 4096, False, False, "auto", "f32"), (2, 16, 1200, 777, False, False, "split", "bf16"),
+]
+
+
+@pytest.mark.parametrize("B,H,Sq,Skv,causal,masked,schedule,out_dtype", KV64_CASES)
+def test_kv64_kernel_matches_oracle(aa, O, B, H, Sq, Skv, causal, masked, schedule, out_dtype):
+    """The 64-key-tile kernel (ANIMA_FLAG_KV64: P in tensor-memory columns of its own, the
+    next QK^T issued while the softmax runs): ragged and one-row shapes, causal and
+    key-padding masks, the three schedules (the cut slices counted in 64-key tiles) and
+    16-bit output, against the oracle on sampled rows and against the default kernel."""
+    rng = np.random.default_rng(B * 7919 + Sq * 31 + Skv)
+    q = rng.standard_normal((B * H, Sq, 128), dtype=np.float32)
+    k = rng.standard_normal((B * H, Skv, 128), dtype=np.float32)
+    v = rng.standard_normal((B * H, Skv, 128), dtype=np.float32)
+    valid = rng.integers(1, Skv + 1, size=B).astype(np.int32) if masked else None
+    tdt = {"bf16": torch.bfloat16, "f16": torch.float16, "f32": torch.float32}[out_dtype]
+    qh, kh, vh = (_dev(t).to(torch.bfloat16) for t in (q, k, v))
+    kw = dict(out_layout="bhsd", out_dtype=tdt, causal=causal, schedule=schedule,
+              kv_valid_len=None if valid is None else _dev(valid))
+    got = aa.attention_core(qh, kh, vh, B, H, kv64=True, **kw)
+    base = aa.attention_core(qh, kh, vh, B, H, **kw)
+    torch.cuda.synchronize()
+    assert aa.status() == 0
+    g_np, b_np = got.float().cpu().numpy(), base.float().cpu().numpy()
+    rows = np.unique(np.concatenate([np.arange(min(Sq, 48)), np.arange(max(0, Sq - 48), Sq),
+                                     rng.choice(Sq, size=min(Sq, 64), replace=False)]))
+    qr, kr, vr = (t.reshape(B, H, -1, 128) for t in (q, k, v))
+    if masked:
+        ref = O.sdpa_varlen(qr, kr, vr, valid)[:, :, rows]
+    elif causal:
+        ref = O.sdpa(qr, kr, vr, causal=True)[:, :, rows]
+    else:
+        ref = O.sdpa(q[:, rows], k, v, threads=8).reshape(B, H, len(rows), 128)
+    tol = ATTN_REL_L2 if out_dtype == "f32" else 8e-3
+    _ok(g_np[:, :, rows], ref, rel=tol)
+    assert rel_l2(g_np, b_np) < tol
+
+
 @pytest.mark.parametrize("out_dtype", ["bf16", "f16"])
 def test_split_schedule_16bit_strided_output(aa, O, out_dtype):
     """Split schedule writing 16-bit output into a token-major [B, S, H, D] tensor (row
