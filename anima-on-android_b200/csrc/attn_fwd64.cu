@@ -10,11 +10,14 @@
 //     S_i  [0, 64)     fp32 scores of one 64-key tile
 //     P_i  [64, 96) and [96, 128)   16-bit pairs, two buffers used by alternate steps
 //     O_i  [128, 256)  fp32 accumulator
-// The softmax copies S_i(j) into registers and signals s_free at once, so the MMA warp
-// issues QK^T_i(j+1) while the softmax of step j still runs; PV_i(j) follows when P_i(j)
-// is stored (p_full).  The softmax keeps its scores in registers for the rare re-check of
-// the running max, and waits for PV_i(j-1) (pv_done) only before it rescales O_i or
-// stores P_i(j) -- by then that PV has long finished.
+// The softmax copies S_i(j) into registers and signals s_free at once, so QK^T_i(j+1) is
+// issued while the softmax of step j still runs; PV_i(j) follows when P_i(j) is stored.
+// Each query tile has its own MMA-issuing thread (warp 9 for tile 0, warp 11 for tile 1),
+// so neither tile's MMAs queue behind the other's softmax.  The softmax keeps its scores
+// in registers for the rare re-check of the running max, and waits for PV_i(j-1) only
+// when it must rescale O_i.  P buffer b has its own p_full / pv_done barriers, completed
+// once per use of the buffer (every other step): a softmax that runs a step ahead of the
+// MMA thread can then never advance a barrier by two phases before it is waited on.
 //
 // Per 64-key step and query tile the tensor pipe runs QK^T (M128 N64 K128: 8 MMAs) and
 // PV (M128 N128 K64: 4 MMAs), 256 cycles each.  K and V tiles are 16 KB; the ring holds 8.
@@ -33,6 +36,7 @@ constexpr int kQTile = 2 * kQPanel;       // [128 rows][128 x 16-bit] = 32 KB
 constexpr int kKvPanel = 64 * 128;        // K/V: [64 rows][64 x 16-bit] = 8 KB
 constexpr int kKvTile = 2 * kKvPanel;     // [64 rows][128 x 16-bit] = 16 KB
 constexpr int kColS = 0, kColP = 64, kColO = 128, kTileCols = 256;
+constexpr int kMmaWarp1 = 11;             // MMA issuer of query tile 1 (warp 9: tile 0)
 
 struct Smem {
   uint8_t q[kNT][kQTile];
@@ -43,8 +47,8 @@ struct Smem {
   uint64_t kv_empty[kStages];
   uint64_t s_full[kNT];   // QK^T_i done: S_i holds the step's scores
   uint64_t s_free[kNT];   // the softmax has S_i in registers: S_i may be rewritten
-  uint64_t p_full[kNT];   // P_i of the step stored
-  uint64_t pv_done[kNT];  // PV_i of the step done
+  uint64_t p_full[kNT][2];   // P_i stored in buffer b (steps b, b+2, ...)
+  uint64_t pv_done[kNT][2];  // PV_i that read buffer b done
   uint64_t o_full[kNT];   // the segment's last PV_i done: O_i final
   uint64_t o_empty[kNT];  // the epilogue has read O_i
   uint64_t mma_done;
@@ -88,20 +92,22 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (threadIdx.x == 0) {
     mbar_init(&sm.q_full, 1);
-    mbar_init(&sm.q_empty, 1);
+    mbar_init(&sm.q_empty, kNT);
     for (int s = 0; s < kStages; ++s) {
       mbar_init(&sm.kv_full[s], 1);
-      mbar_init(&sm.kv_empty[s], 1);
+      mbar_init(&sm.kv_empty[s], kNT);  // one commit from each tile's MMA thread
     }
     for (int i = 0; i < kNT; ++i) {
       mbar_init(&sm.s_full[i], 1);
       mbar_init(&sm.s_free[i], kBM);
-      mbar_init(&sm.p_full[i], kBM);
-      mbar_init(&sm.pv_done[i], 1);
+      for (int b = 0; b < 2; ++b) {
+        mbar_init(&sm.p_full[i][b], kBM);
+        mbar_init(&sm.pv_done[i][b], 1);
+      }
       mbar_init(&sm.o_full[i], 1);
       mbar_init(&sm.o_empty[i], kBM);
     }
-    mbar_init(&sm.mma_done, 1);
+    mbar_init(&sm.mma_done, kNT);
     sm.abort = 0;
     fence_barrier_init();
   }
@@ -171,8 +177,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         ++a;
       }
       if (a > 0) drain_wait(&sm.q_full, (uint32_t)(a - 1) & 1u);
-    } else if (warp == kMmaWarp && lane == 0) {
-      // ---------------------------------------------------------- MMA issuer
+    } else if ((warp == kMmaWarp || warp == kMmaWarp1) && lane == 0) {
+      // ---------------------------------------------------------- MMA issuer of tile i
+      const int i = warp == kMmaWarp ? 0 : 1;
       constexpr uint32_t ab = kOp == ANIMA_DTYPE_BF16 ? 1u : 0u;  // idesc: 0 f16, 1 bf16
       constexpr uint32_t idesc_qk = make_idesc_f16(ab, kBM, kBN, 0);
       constexpr uint32_t idesc_pv = make_idesc_f16(ab, kBM, kD, 1);
@@ -181,31 +188,31 @@ __global__ void __launch_bounds__(kThreads, 1)
       // 64-dimension panels are kKvPanel apart.
       const uint64_t dk0 = sdesc_sw128(smem_u32(sm.kv[0]), 16, 1024);
       const uint64_t dv0 = sdesc_sw128(smem_u32(sm.kv[0]), kKvPanel, 1024);
-      uint64_t dq[kNT][8];
+      uint64_t dq[8];
 #pragma unroll
-      for (int i = 0; i < kNT; ++i)
-#pragma unroll
-        for (int kk = 0; kk < 8; ++kk)
-          dq[i][kk] =
-              sdesc_sw128(smem_u32(sm.q[i]) + (kk >> 2) * kQPanel + (kk & 3) * 32, 16, 1024);
+      for (int kk = 0; kk < 8; ++kk)
+        dq[kk] = sdesc_sw128(smem_u32(sm.q[i]) + (kk >> 2) * kQPanel + (kk & 3) * 32, 16, 1024);
+      const uint32_t tS = tmem + i * kTileCols + kColS;
+      const uint32_t tP = tmem + i * kTileCols + kColP;
+      const uint32_t tO = tmem + i * kTileCols + kColO;
 
-      auto issue_qk = [&](int i, int slot) {
+      auto issue_qk = [&](int slot) {
         const uint64_t kb = desc_plus(dk0, (uint32_t)slot * kKvTile);
         uint64_t b[8];
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk) b[kk] = desc_plus(kb, (kk >> 2) * kKvPanel + (kk & 3) * 32);
-        umma_ss_x8(tmem + i * kTileCols + kColS, dq[i], b, idesc_qk, 0u);
+        umma_ss_x8(tS, dq, b, idesc_qk, 0u);
       };
-      auto issue_pv = [&](int i, int slot, int buf, bool acc) {
+      auto issue_pv = [&](int slot, int buf, bool acc) {
         const uint64_t vb = desc_plus(dv0, (uint32_t)slot * kKvTile);
         uint64_t b[4];
         uint32_t a[4];
 #pragma unroll
         for (int kk = 0; kk < 4; ++kk) {
           b[kk] = desc_plus(vb, kk * 2048);
-          a[kk] = tmem + i * kTileCols + kColP + buf * 32 + kk * 8;  // 16 keys per step
+          a[kk] = tP + buf * 32 + kk * 8;  // 16 keys per step
         }
-        umma_ts_x4(tmem + i * kTileCols + kColO, a, b, idesc_pv, acc ? 1u : 0u);
+        umma_ts_x4(tO, a, b, idesc_pv, acc ? 1u : 0u);
       };
       auto wait = [&](uint64_t* bar, uint32_t parity) {
         return mbar_wait(bar, parity, abort, p.status, ANIMA_ERR_TIMEOUT);
@@ -223,18 +230,15 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (n <= 0) continue;
         const uint32_t pa = (uint32_t)(a - 1) & 1u;  // parity of the previous segment
         if (!(ok = wait(&sm.q_full, (uint32_t)a & 1u))) break;
-        // Scores of the segment's first key tile, once each tile's softmax has taken the
-        // previous step's scores into registers.
+        // Scores of the segment's first key tile, once the softmax has taken the previous
+        // step's scores into registers.
         {
           const int ik = 2 * g;
           if (!(ok = wait(&sm.kv_full[slot_of(ik)], par_of(ik)))) break;
-          for (int i = 0; i < kNT && ok; ++i) {
-            if (g > 0 && !(ok = wait(&sm.s_free[i], (uint32_t)(g - 1) & 1u))) break;
-            tc_fence_after();
-            issue_qk(i, slot_of(ik));
-            umma_commit(&sm.s_full[i]);
-          }
-          if (!ok) break;
+          if (g > 0 && !(ok = wait(&sm.s_free[i], (uint32_t)(g - 1) & 1u))) break;
+          tc_fence_after();
+          issue_qk(slot_of(ik));
+          umma_commit(&sm.s_full[i]);
           umma_commit(&sm.kv_empty[slot_of(ik)]);
           if (n == 1) umma_commit(&sm.q_empty);
         }
@@ -242,45 +246,32 @@ __global__ void __launch_bounds__(kThreads, 1)
           const int gj = g + jj;
           const int ik = 2 * (gj + 1), iv = 2 * gj + 1;
           const bool more = jj + 1 < n;
-          const uint32_t pg = (uint32_t)gj & 1u;
-          // tile 0: next scores, then this step's P V
+          // next scores, then this step's P V
           if (more) {
-            ok = wait(&sm.kv_full[slot_of(ik)], par_of(ik)) && wait(&sm.s_free[0], pg);
+            ok = wait(&sm.kv_full[slot_of(ik)], par_of(ik)) && wait(&sm.s_free[i], (uint32_t)gj & 1u);
             if (!ok) break;
             tc_fence_after();
-            issue_qk(0, slot_of(ik));
-            umma_commit(&sm.s_full[0]);
-          }
-          ok = wait(&sm.kv_full[slot_of(iv)], par_of(iv)) && wait(&sm.p_full[0], pg);
-          if (ok && jj == 0 && a > 0) ok = wait(&sm.o_empty[0], pa);
-          if (!ok) break;
-          tc_fence_after();
-          issue_pv(0, slot_of(iv), gj & 1, jj > 0);
-          umma_commit(&sm.pv_done[0]);
-          if (!more) umma_commit(&sm.o_full[0]);
-          // tile 1
-          if (more) {
-            if (!(ok = wait(&sm.s_free[1], pg))) break;
-            tc_fence_after();
-            issue_qk(1, slot_of(ik));
-            umma_commit(&sm.s_full[1]);
+            issue_qk(slot_of(ik));
+            umma_commit(&sm.s_full[i]);
             umma_commit(&sm.kv_empty[slot_of(ik)]);
             if (jj + 2 == n) umma_commit(&sm.q_empty);  // the segment's last QK^T issued
           }
-          ok = wait(&sm.p_full[1], pg);
-          if (ok && jj == 0 && a > 0) ok = wait(&sm.o_empty[1], pa);
+          ok = wait(&sm.kv_full[slot_of(iv)], par_of(iv)) &&
+               wait(&sm.p_full[i][gj & 1], (uint32_t)(gj >> 1) & 1u);
+          if (ok && jj == 0 && a > 0) ok = wait(&sm.o_empty[i], pa);
           if (!ok) break;
           tc_fence_after();
-          issue_pv(1, slot_of(iv), gj & 1, jj > 0);
-          umma_commit(&sm.pv_done[1]);
+          issue_pv(slot_of(iv), gj & 1, jj > 0);
+          umma_commit(&sm.pv_done[i][gj & 1]);
           umma_commit(&sm.kv_empty[slot_of(iv)]);
-          if (!more) umma_commit(&sm.o_full[1]);
+          if (!more) umma_commit(&sm.o_full[i]);
         }
         if (!ok) break;
         g += n;
         ++a;
       }
-      // Let every MMA this thread issued retire before TMEM is released.
+      // Let every MMA this thread issued retire (and the other issuer's) before TMEM is
+      // released.
       umma_commit(&sm.mma_done);
       drain_wait(&sm.mma_done, 0);
     }
@@ -414,11 +405,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
 #undef SV
         l = l * alpha + sum;
-        // PV_i of the previous step must be done before O_i is rescaled or the P buffer
-        // of this step (last read two steps ago) is rewritten.
-        if (g > 0) {
-          const bool got2 = mbar_wait(&sm.pv_done[i], (uint32_t)(g - 1) & 1u, abort, p.status,
-                                      ANIMA_ERR_TIMEOUT);
+        // The P buffer of this step was last read by PV_i(g-2).  (Its completion is also
+        // implied by S_i(g): the tile's MMA thread issued QK^T_i(g) after PV_i(g-2), and
+        // its MMAs run in order; the wait never stalls.)
+        if (g >= 2) {
+          const bool got2 = mbar_wait(&sm.pv_done[i][g & 1], (uint32_t)((g - 2) >> 1) & 1u,
+                                      abort, p.status, ANIMA_ERR_TIMEOUT);
           if (!__all_sync(0xffffffffu, got2)) {
             ok = false;
             break;
@@ -426,6 +418,14 @@ __global__ void __launch_bounds__(kThreads, 1)
           tc_fence_after();
         }
         if (__any_sync(0xffffffffu, jj > 0 && alpha != 1.f)) {
+          // O_i must hold PV_i(g-1) before it is rescaled.
+          const bool got3 = mbar_wait(&sm.pv_done[i][(g - 1) & 1], (uint32_t)((g - 1) >> 1) & 1u,
+                                      abort, p.status, ANIMA_ERR_TIMEOUT);
+          if (!__all_sync(0xffffffffu, got3)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
 #pragma unroll 1
           for (int c = 0; c < 4; ++c) {
             uint32_t o[32];
@@ -439,7 +439,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         tmem_st32(tP + (g & 1) * 32, pk);
         tmem_st_wait();
         tc_fence_before();
-        mbar_arrive(&sm.p_full[i]);
+        mbar_arrive(&sm.p_full[i][g & 1]);
         m = m_use;
       }
       if (!ok) break;
