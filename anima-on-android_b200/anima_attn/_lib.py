@@ -60,6 +60,7 @@ SIGNATURES = {
     "anima_attn_fwd": ([ct.POINTER(AttnArgs), _P], ct.c_int),
     "anima_attn_fwd_noalloc": ([ct.POINTER(AttnArgs), _P], ct.c_int),
     "anima_attn_workspace_size": ([ct.c_int] * 4 + [ct.c_uint], ct.c_uint64),
+    "anima_attn_schedule": ([ct.c_int] * 4 + [ct.c_uint, ct.c_int], ct.c_int),
     "anima_attn_status": ([_P, ct.c_int], ct.c_int),
     "anima_attn_selftest_timeout": ([ct.c_uint, _P], ct.c_int),
     "anima_dit_ln_modulate": ([_P, _P, _P, ct.c_int64, _P, ct.c_int, ct.c_int64, ct.c_int, ct.c_int,

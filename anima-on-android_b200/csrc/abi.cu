@@ -18,6 +18,7 @@ namespace anima {
 int attn_fwd_launch(const AnimaAttnArgs* a, int* status, int sm_count, cudaStream_t st);
 int attn_fwd_pair_launch(const AnimaAttnArgs* a, int* status, cudaStream_t st);
 size_t attn_workspace_bytes(int B, int H, int S_q, int S_kv, unsigned flags, int sm_count);
+int attn_schedule_mode(int B, int H, int S_q, int S_kv, unsigned flags, int sm_count);
 int selftest_wait_launch(int* status, unsigned timeout_us, cudaStream_t st);
 int ln_modulate_launch(const float* x, const float* scale, const float* shift, long long mod_stride,
                        void* y, int out_dtype, long long rows, int rows_per_b, int D, float eps,
@@ -402,6 +403,19 @@ uint64_t anima_attn_workspace_size(int B, int H, int S_q, int S_kv, unsigned fla
   DeviceState* d = current_device(&rc);
   if (!d || B <= 0 || H <= 0 || S_q <= 0 || S_kv <= 0) return 0;
   return attn_workspace_bytes(B, H, S_q, S_kv, flags, d->sm_count);
+}
+
+int anima_attn_schedule(int B, int H, int S_q, int S_kv, unsigned flags, int sm_count) {
+  if (B <= 0 || H <= 0 || S_q <= 0 || S_kv <= 0 || (long long)B * H > 0x7fffffffLL)
+    return ANIMA_ERR_SHAPE;
+  if (sm_count <= 0) {
+    int rc = ANIMA_OK;
+    DeviceState* d = current_device(&rc);
+    if (!d) return rc;
+    sm_count = d->sm_count;
+  }
+  if (flags & ANIMA_FLAG_PAIR) return ANIMA_SCHED_UNIT;
+  return attn_schedule_mode(B, H, S_q, S_kv, flags, sm_count);
 }
 
 int anima_attn_status(void* stream, int reset) {

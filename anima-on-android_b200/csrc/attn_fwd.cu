@@ -582,6 +582,13 @@ size_t attn_workspace_bytes(int B, int H, int S_q, int S_kv, unsigned flags, int
   return plan_split(B * H, S_q, S_kv, flags, sm_count).bytes;
 }
 
+int attn_schedule_mode(int B, int H, int S_q, int S_kv, unsigned flags, int sm_count) {
+  static_assert(kSchedUnit == ANIMA_SCHED_UNIT && kSchedWhole == ANIMA_SCHED_WHOLE &&
+                    kSchedCut == ANIMA_SCHED_CUT,
+                "schedule codes of the header");
+  return plan_split(B * H, S_q, S_kv, flags, sm_count).mode;
+}
+
 int attn_fwd_launch(const AnimaAttnArgs* a, int* status, int sm_count, cudaStream_t st) {
   if (a->D != attn::kD) return ANIMA_ERR_SHAPE;
   if (a->op_dtype != ANIMA_DTYPE_BF16 && a->op_dtype != ANIMA_DTYPE_F16) return ANIMA_ERR_ARG;

@@ -440,6 +440,11 @@ def run_ours(args, rank, world, local_rank):
 
     peaks = load_peaks()
     achieved = flops_rank / (att_ms * 1e-3) / 1e12
+    # The schedule that ran (the library's planner, given the workspace attention_core passes).
+    sched_flags = {"auto": 0, "unit": L.FLAG_UNIT, "whole": L.FLAG_WHOLE, "split": L.FLAG_SPLIT}
+    sms = torch.cuda.get_device_properties(dev).multi_processor_count
+    sched_run = {0: "unit", 1: "whole", 2: "cut"}.get(
+        L.lib.anima_attn_schedule(B, heads, L_, L_, sched_flags[args.schedule], sms), "error")
     traffic = load_traffic(L_).get("attn_fwd")
     pro_bytes = (3 * B * L_ * heads * D * 4) + (3 * B * L_ * heads * D * 2)
     res = {
@@ -454,7 +459,7 @@ def run_ours(args, rank, world, local_rank):
                    "parallelism": f"{args.shard}{world}",
                    "l2": f"inputs {3 * B * L_ * heads * D * 4 / 2**20:.0f} MiB fp32 > 126 MB L2",
                    "attn_ms": round(att_ms, 4), "prologue_ms": round(pro_ms, 4),
-                   "schedule": args.schedule,
+                   "schedule": args.schedule, "schedule_run": sched_run,
                    "prologue_gbs": round(pro_bytes / (pro_ms * 1e-3) / 1e9, 1),
                    "pct_of_dense_bf16_peak": round(100 * value / world / peaks["tflops"], 2)},
         "roofline": {"bound": "tensor", "achieved": round(achieved, 2), "peak": peaks["tflops"],

@@ -151,8 +151,19 @@ int anima_attn_fwd(const AnimaAttnArgs* args, void* stream);
 int anima_attn_fwd_noalloc(const AnimaAttnArgs* args, void* stream);
 
 /* Workspace bytes anima_attn_fwd can use for this shape on the current device
- * (0 when the one-CTA-per-unit schedule is used anyway). */
+ * (0 when the call does not cut its last round; see anima_attn_schedule). */
 uint64_t anima_attn_workspace_size(int B, int H, int S_q, int S_kv, unsigned flags);
+
+/* The schedule anima_attn_fwd(_noalloc) runs for this call when it is given the workspace
+ * it asks for: ANIMA_SCHED_UNIT (one CTA per 256-row unit), ANIMA_SCHED_WHOLE (persistent
+ * grid of whole units) or ANIMA_SCHED_CUT (persistent grid, last round cut into key-tile
+ * slices; without the workspace such a call runs ANIMA_SCHED_WHOLE for units of at most
+ * 4096 keys, else ANIMA_SCHED_UNIT).  ANIMA_FLAG_PAIR calls run the CTA-pair kernel and
+ * report ANIMA_SCHED_UNIT.  sm_count <= 0 takes the current device's SM count; a positive
+ * one needs no GPU.  Negative ANIMA_ERR_* on bad arguments.  Host arithmetic only; it has
+ * no counterpart in the reference, whose CPU attention has a single schedule. */
+enum { ANIMA_SCHED_UNIT = 0, ANIMA_SCHED_WHOLE = 1, ANIMA_SCHED_CUT = 2 };
+int anima_attn_schedule(int B, int H, int S_q, int S_kv, unsigned flags, int sm_count);
 
 /* Device status word of the current device: 0, or the first ANIMA_ERR_* a kernel
  * recorded.  Synchronises `stream`; clears the word when reset != 0. */

@@ -104,3 +104,32 @@ def test_rmsnorm_before_init_returns_false_like_reference():
 
 def test_version_string():
     assert "sm_100a" in anima_attn.version()
+
+
+# (S_q, S_kv, flags) -> schedule anima_attn_fwd runs on a 148-SM B200 with B=2, H=16: the
+# choices measured fastest and listed with the planner (csrc/attn_fwd.cu, plan_split).
+SCHEDULES = [
+    (2048, 2048, 0, "whole"), (2560, 2560, 0, "cut"), (3072, 3072, 0, "cut"),
+    (4096, 4096, 0, "cut"), (5120, 5120, 0, "cut"), (6144, 6144, 0, "cut"),
+    (8192, 8192, 0, "unit"), (16384, 16384, 0, "unit"), (4096, 512, 0, "whole"),
+    (4096, 1024, 0, "whole"), (4096, 2048, 0, "cut"),
+    (1024, 1024, 0, "unit"),                                 # 128 units: one wave
+    (4096, 4096, L.FLAG_MASK, "unit"), (4096, 4096, L.FLAG_CAUSAL, "unit"),
+    (4096, 4096, L.FLAG_UNIT, "unit"), (4096, 4096, L.FLAG_WHOLE, "whole"),
+    (2048, 2048, L.FLAG_SPLIT, "cut"), (8192, 8192, L.FLAG_SPLIT, "cut"),
+    (4096, 4096, L.FLAG_PAIR, "unit"), (4096, 4096, L.FLAG_KV64, "cut"),
+    (4096, 512, L.FLAG_KV64, "whole"),
+]
+SCHED_CODE = {"unit": 0, "whole": 1, "cut": 2}
+
+
+@pytest.mark.parametrize("Sq,Skv,flags,want", SCHEDULES)
+def test_schedule_choice(Sq, Skv, flags, want):
+    """The schedule query runs the launcher's own planner on the host (no GPU needed when
+    the SM count is given)."""
+    assert L.lib.anima_attn_schedule(2, 16, Sq, Skv, flags, 148) == SCHED_CODE[want]
+
+
+def test_schedule_query_rejects_bad_shapes():
+    assert L.lib.anima_attn_schedule(0, 16, 4096, 4096, 0, 148) < 0
+    assert L.lib.anima_attn_schedule(2, 16, 4096, -1, 0, 148) < 0
