@@ -17,6 +17,7 @@ OK, ERR_ARG, ERR_SHAPE, ERR_CUDA, ERR_TIMEOUT, ERR_UNSUPPORTED, ERR_NOMEM = 0, -
 DTYPE_F32, DTYPE_BF16, DTYPE_F16 = 0, 1, 2
 FLAG_QNORM, FLAG_KNORM, FLAG_ROPE, FLAG_MASK, FLAG_CAUSAL, FLAG_PAIR = 0x1, 0x2, 0x4, 0x8, 0x10, 0x20
 FLAG_SPLIT, FLAG_UNIT, FLAG_WHOLE, FLAG_KV64 = 0x40, 0x80, 0x100, 0x200
+SCHED_UNIT, SCHED_WHOLE, SCHED_CUT = 0, 1, 2
 
 ERR_NAMES = {OK: "ok", ERR_ARG: "bad argument", ERR_SHAPE: "unsupported shape",
              ERR_CUDA: "CUDA error", ERR_TIMEOUT: "device-side wait timed out",
@@ -52,6 +53,12 @@ SIGNATURES = {
     "anima_rt_run_sdpa": ([_P] * 4 + [ct.c_int] * 4 + [ct.c_float, ct.c_bool], ct.c_bool),
     "anima_rt_run_rmsnorm": ([_P, _P, _P, ct.c_int, ct.c_int, ct.c_float], ct.c_bool),
     "anima_rt_run_rope": ([_P, _P, _P, ct.c_int, ct.c_int, ct.c_int], ct.c_bool),
+    "anima_rt_run_gelu": ([_P, _P, ct.c_int], ct.c_bool),
+    "anima_rt_run_silu": ([_P, _P, ct.c_int], ct.c_bool),
+    "anima_rt_run_layernorm": ([_P, _P, ct.c_int, ct.c_int, ct.c_float], ct.c_bool),
+    "anima_rt_run_softmax": ([_P, _P, ct.c_int, ct.c_int], ct.c_bool),
+    "anima_rt_run_gemm_fp32": ([_P, _P, _P, ct.c_int, ct.c_int, ct.c_int], ct.c_bool),
+    "anima_rt_run_gemm_bf16": ([_P, _P, _P, ct.c_int, ct.c_int, ct.c_int], ct.c_bool),
     "anima_rt_run_attention": ([_P] * 8 + [ct.c_int] * 5 + [ct.c_float, ct.c_float, ct.c_uint],
                                ct.c_bool),
     "anima_rt_last_error": ([], ct.c_char_p),

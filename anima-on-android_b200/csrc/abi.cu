@@ -8,6 +8,7 @@
 //    kernels on the library's stream, copies the result back and synchronises.
 //    Calls are serialised by one mutex (one workspace); like the reference they are
 //    safe to call from several threads.
+#include <initializer_list>
 #include <mutex>
 #include <string>
 
@@ -31,13 +32,21 @@ int gate_residual_ln_modulate_launch(float* x, const float* gate, long long gate
                                      int out_dtype, long long rows, int rows_per_b, int D,
                                      float eps, int sm_count, cudaStream_t st);
 int gelu16_launch(const void* x, void* y, int dtype, long long n, int sm_count, cudaStream_t st);
-int attn_fwd_launch_noalloc(const AnimaAttnArgs* a, int* status, int sm_count, cudaStream_t st,
-                            const char** why);
+int attn_fwd_launch_noalloc(const AnimaAttnArgs* a, int* status, int sm_count, void* scratch,
+                            cudaStream_t st, const char** why);
+cudaError_t noalloc_scratch_address(void** ptr);
 int prologue_launch(const AnimaPrologueArgs* a, int sm_count, cudaStream_t st);
 int rmsnorm_launch(const float* x, const float* w, float* y, long long m, int d, float eps,
                    int sm_count, cudaStream_t st);
 int rope_launch(const float* t, const float* f, float* out, int N, int S, int D, int sm_count,
                 cudaStream_t st);
+int act_launch(int which, const float* x, float* y, long long n, int sm_count, cudaStream_t st);
+int layernorm_launch(const float* x, float* y, long long m, int d, float eps, int sm_count,
+                     cudaStream_t st);
+int softmax_launch(const float* x, float* y, long long outer, int dim, int sm_count,
+                   cudaStream_t st);
+int gemm_nt_launch(const float* A, const void* Bm, bool b_bf16, float* C, int M, int N, int K,
+                   cudaStream_t st);
 }  // namespace anima
 
 using namespace anima;
@@ -50,11 +59,17 @@ void set_error(const std::string& s) { g_last_error = s; }
 
 constexpr int kMaxDevices = 64;
 
+// The status word: first error a kernel recorded on this device (0 = clean).  It is a
+// static device variable, so no entry of the library allocates device memory for it;
+// each device that loads the library has its own copy, zero at load.
+__device__ int g_status_word;
+
 struct DeviceState {
   bool ready = false;
   int sm_count = 0;
   int cc = 0;
-  int* status = nullptr;  // one int of device memory: first error a kernel recorded
+  int* status = nullptr;          // device address of g_status_word on this device
+  void* noalloc_scratch = nullptr;  // device address of the no-allocation scratch array
 };
 DeviceState g_dev[kMaxDevices];
 std::mutex g_dev_mu;
@@ -87,11 +102,13 @@ DeviceState* current_device(int* rc) {
                 std::to_string(major * 10 + minor));
       return nullptr;
     }
+    // The symbol's address on this device (the device is current); a host-side
+    // `&g_status_word` would be a host stand-in, not a device address.
     int* st = nullptr;
-    if (cudaMalloc(&st, sizeof(int)) != cudaSuccess || cudaMemset(st, 0, sizeof(int)) != cudaSuccess) {
+    if (cudaGetSymbolAddress(reinterpret_cast<void**>(&st), g_status_word) != cudaSuccess || !st) {
       cudaGetLastError();
-      *rc = ANIMA_ERR_NOMEM;
-      set_error("cannot allocate the device status word");
+      *rc = ANIMA_ERR_CUDA;
+      set_error("cudaGetSymbolAddress of the device status word failed");
       return nullptr;
     }
     d.sm_count = sms;
@@ -100,6 +117,21 @@ DeviceState* current_device(int* rc) {
     d.ready = true;
   }
   return &d;
+}
+
+// Device address of the no-allocation scratch on the current device (looked up once per
+// device, under the same lock as the rest of the device state); nullptr on failure.
+void* noalloc_scratch(DeviceState* d) {
+  std::lock_guard<std::mutex> lk(g_dev_mu);
+  if (!d->noalloc_scratch) {
+    void* ptr = nullptr;
+    if (noalloc_scratch_address(&ptr) != cudaSuccess || !ptr) {
+      cudaGetLastError();
+      return nullptr;
+    }
+    d->noalloc_scratch = ptr;
+  }
+  return d->noalloc_scratch;
 }
 
 const char* code_name(int rc) {
@@ -202,6 +234,62 @@ bool rt_finish(const char* what) {
   return true;
 }
 
+// One host buffer of a compatibility call (nullptr host: an absent optional input).
+struct RtBuf {
+  const void* host;
+  size_t bytes;
+};
+
+// Body of the single-kernel host entries: copies each input into the library workspace,
+// runs `launch(device inputs, device output, sm_count, stream)` and copies `out_bytes` of
+// its output back to `out`, all on the library stream, then checks the status word.  On a
+// failure after the first enqueue the stream is drained before false is returned, so no
+// copy still touches the caller's arrays.
+template <class F>
+bool rt_call(const char* who, std::initializer_list<RtBuf> ins, void* out, size_t out_bytes,
+             F launch) {
+  constexpr int kMaxIns = 4;
+  if (ins.size() > (size_t)kMaxIns) return rt_fail(std::string(who) + ": too many inputs");
+  std::lock_guard<std::recursive_mutex> lk(g_rt_mu);
+  size_t offs[kMaxIns] = {}, off = 0;
+  int n = 0;
+  for (const RtBuf& b : ins) {
+    offs[n++] = off;
+    off = align_up(off + b.bytes);
+  }
+  const size_t o_out = off;
+  if (!rt_prepare(align_up(o_out + out_bytes))) return false;
+  char* ws = static_cast<char*>(g_rt.ws);
+  cudaStream_t st = g_rt.stream;
+  auto bail = [&]() {
+    cudaStreamSynchronize(st);
+    cudaGetLastError();
+    return false;
+  };
+  const void* dev_in[kMaxIns] = {};
+  n = 0;
+  for (const RtBuf& b : ins) {
+    if (b.host) {
+      dev_in[n] = ws + offs[n];
+      if (b.bytes &&
+          !rt_check(cudaMemcpyAsync(ws + offs[n], b.host, b.bytes, cudaMemcpyHostToDevice, st), who))
+        return bail();
+    }
+    ++n;
+  }
+  int rc = ANIMA_OK;
+  DeviceState* dev = current_device(&rc);
+  if (!dev) return bail();
+  rc = launch(dev_in, ws + o_out, dev->sm_count, st);
+  if (rc != ANIMA_OK) {
+    rt_fail(std::string(who) + ": " + code_name(rc));
+    return bail();
+  }
+  if (!rt_check(cudaMemcpyAsync(out, ws + o_out, out_bytes, cudaMemcpyDeviceToHost, st), who))
+    return bail();
+  return rt_finish(who);
+}
+
 // Shared body of anima_rt_run_sdpa_flash / anima_rt_run_sdpa / anima_rt_run_attention.
 bool rt_attention(const float* q, const float* k, const float* v, const float* q_w,
                   const float* k_w, const float* freqs, const int* kv_valid, float* out,
@@ -249,22 +337,31 @@ bool rt_attention(const float* q, const float* k, const float* v, const float* q
   if (!rt_prepare(off)) return false;
   char* ws = static_cast<char*>(g_rt.ws);
   cudaStream_t st = g_rt.stream, sin = g_rt.in, sout = g_rt.out;
+  // On a failure after the first enqueue, copies of earlier chunks may still read q/k/v
+  // or write `out`: every stream finishes before the caller sees false and reuses them.
+  auto bail = [&]() {
+    cudaStreamSynchronize(sin);
+    cudaStreamSynchronize(st);
+    cudaStreamSynchronize(sout);
+    cudaGetLastError();
+    return false;
+  };
   // The split schedule's arrival counters (first 4 KiB of its workspace) must start at
   // zero; this workspace is shared with other data, so clear them on every call.
-  if (ws_split && !rt_check(cudaMemsetAsync(ws + o_split, 0, 4096, st), who)) return false;
+  if (ws_split && !rt_check(cudaMemsetAsync(ws + o_split, 0, 4096, st), who)) return bail();
   float *dq = (float*)(ws + o_q), *dk = (float*)(ws + o_k), *dv = (float*)(ws + o_v);
   float* dout = (float*)(ws + o_out);
   float* dw = (float*)(ws + o_w);
   if (q_w && !rt_check(cudaMemcpyAsync(dw, q_w, D * 4, cudaMemcpyHostToDevice, sin), who))
-    return false;
+    return bail();
   if (k_w && !rt_check(cudaMemcpyAsync(dw + D, k_w, D * 4, cudaMemcpyHostToDevice, sin), who))
-    return false;
+    return bail();
   if (freqs && !rt_check(cudaMemcpyAsync(ws + o_f, freqs, (size_t)S_q * D * 2 * 4,
                                          cudaMemcpyHostToDevice, sin), who))
-    return false;
+    return bail();
   if (kv_valid && !rt_check(cudaMemcpyAsync(ws + o_valid, kv_valid, (size_t)B * 4,
                                             cudaMemcpyHostToDevice, sin), who))
-    return false;
+    return bail();
   const size_t row = (size_t)H * D * 4, crow = (size_t)G * D * 4;  // bytes: pitch, chunk row
   for (int c = 0; c < nchunks; ++c) {
     const int b0 = (c / ng) * Bc, h0 = (c % ng) * G, bn = min(Bc, B - b0);
@@ -278,7 +375,7 @@ bool rt_attention(const float* q, const float* k, const float* v, const float* q
                                     cudaMemcpyHostToDevice, sin), who) ||
         !rt_check(cudaEventRecord(g_rt.ev_in[c], sin), who) ||
         !rt_check(cudaStreamWaitEvent(st, g_rt.ev_in[c], 0), who))
-      return false;
+      return bail();
     // ---- prologue + attention on this chunk's heads (its own head-major operand block)
     uint16_t* qb = (uint16_t*)(ws + o_qb) + c * cq;
     uint16_t* kb = (uint16_t*)(ws + o_kb) + c * ck;
@@ -310,7 +407,10 @@ bool rt_attention(const float* q, const float* k, const float* v, const float* q
     pa.v_out = vb;
     pa.op_dtype = ANIMA_DTYPE_BF16;
     int rc = anima_attn_prologue(&pa, st);
-    if (rc != ANIMA_OK) return rt_fail(std::string(who) + ": prologue: " + code_name(rc));
+    if (rc != ANIMA_OK) {
+      rt_fail(std::string(who) + ": prologue: " + code_name(rc));
+      return bail();
+    }
     AnimaAttnArgs aa = {};
     aa.q = qb;
     aa.k = kb;
@@ -332,15 +432,18 @@ bool rt_attention(const float* q, const float* k, const float* v, const float* q
     aa.workspace = ws_split ? ws + o_split : nullptr;
     aa.workspace_bytes = ws_split;
     rc = anima_attn_fwd(&aa, st);
-    if (rc != ANIMA_OK) return rt_fail(std::string(who) + ": attention: " + code_name(rc));
+    if (rc != ANIMA_OK) {
+      rt_fail(std::string(who) + ": attention: " + code_name(rc));
+      return bail();
+    }
     // ---- copy out
     if (!rt_check(cudaEventRecord(g_rt.ev_done[c], st), who) ||
         !rt_check(cudaStreamWaitEvent(sout, g_rt.ev_done[c], 0), who) ||
         !rt_check(cudaMemcpy2DAsync(out + qo, row, dout + qo, row, crow, (size_t)bn * S_q,
                                     cudaMemcpyDeviceToHost, sout), who))
-      return false;
+      return bail();
   }
-  if (!rt_check(cudaStreamSynchronize(sout), who)) return false;
+  if (!rt_check(cudaStreamSynchronize(sout), who)) return bail();
   return rt_finish(who);
 }
 
@@ -391,8 +494,19 @@ int anima_attn_fwd_noalloc(const AnimaAttnArgs* a, void* stream) {
   int rc = ANIMA_OK;
   DeviceState* d = current_device(&rc);
   if (!d) return rc;
+  if (a->flags & ANIMA_FLAG_PAIR) {  // the CTA-pair kernel uses no scratch
+    rc = attn_fwd_pair_launch(a, d->status, static_cast<cudaStream_t>(stream));
+    if (rc != ANIMA_OK) set_error(std::string("anima_attn_fwd_noalloc: ") + code_name(rc));
+    return rc;
+  }
+  void* scratch = noalloc_scratch(d);
+  if (!scratch) {
+    set_error("anima_attn_fwd_noalloc: cudaGetSymbolAddress of the no-allocation scratch failed");
+    return ANIMA_ERR_CUDA;
+  }
   const char* why = nullptr;
-  rc = attn_fwd_launch_noalloc(a, d->status, d->sm_count, static_cast<cudaStream_t>(stream), &why);
+  rc = attn_fwd_launch_noalloc(a, d->status, d->sm_count, scratch,
+                               static_cast<cudaStream_t>(stream), &why);
   if (rc != ANIMA_OK)
     set_error(std::string("anima_attn_fwd_noalloc: ") + (why ? why : code_name(rc)));
   return rc;
@@ -555,46 +669,85 @@ bool anima_rt_run_rmsnorm(const float* x, const float* w, float* out, int m, int
   if (!g_rt.inited) return rt_fail("anima_rt_run_rmsnorm: anima_rt_init has not been called");
   if (!x || !out || m < 0 || d <= 0) return rt_fail("anima_rt_run_rmsnorm: bad arguments");
   if (m == 0) return true;
-  std::lock_guard<std::recursive_mutex> lk(g_rt_mu);
   const size_t n = (size_t)m * d;
-  const size_t o_x = 0, o_y = align_up(n * 4), o_w = o_y + align_up(n * 4);
-  if (!rt_prepare(o_w + align_up((size_t)d * 4))) return false;
-  char* ws = static_cast<char*>(g_rt.ws);
-  cudaStream_t st = g_rt.stream;
-  const char* who = "anima_rt_run_rmsnorm";
-  if (!rt_check(cudaMemcpyAsync(ws + o_x, x, n * 4, cudaMemcpyHostToDevice, st), who)) return false;
-  if (w && !rt_check(cudaMemcpyAsync(ws + o_w, w, (size_t)d * 4, cudaMemcpyHostToDevice, st), who))
-    return false;
-  int rc = ANIMA_OK;
-  DeviceState* dev = current_device(&rc);
-  rc = rmsnorm_launch((const float*)(ws + o_x), w ? (const float*)(ws + o_w) : nullptr,
-                      (float*)(ws + o_y), m, d, eps, dev->sm_count, st);
-  if (rc != ANIMA_OK) return rt_fail(std::string(who) + ": " + code_name(rc));
-  if (!rt_check(cudaMemcpyAsync(out, ws + o_y, n * 4, cudaMemcpyDeviceToHost, st), who)) return false;
-  return rt_finish(who);
+  return rt_call("anima_rt_run_rmsnorm", {{x, n * 4}, {w, (size_t)d * 4}}, out, n * 4,
+                 [&](const void* const* in, void* y, int sms, cudaStream_t st) {
+                   return rmsnorm_launch((const float*)in[0], (const float*)in[1], (float*)y, m,
+                                         d, eps, sms, st);
+                 });
 }
 
 bool anima_rt_run_rope(const float* t, const float* freqs, float* out, int N, int S, int D) {
-  const char* who = "anima_rt_run_rope";
   if (!t || !freqs || !out || N < 0 || S < 0 || D <= 0 || (D & 1))
-    return rt_fail(std::string(who) + ": bad arguments");
+    return rt_fail("anima_rt_run_rope: bad arguments");
   if (N == 0 || S == 0) return true;
-  std::lock_guard<std::recursive_mutex> lk(g_rt_mu);
   const size_t n = (size_t)N * S * D, nf = (size_t)S * D * 2;
-  const size_t o_t = 0, o_o = align_up(n * 4), o_f = o_o + align_up(n * 4);
-  if (!rt_prepare(o_f + align_up(nf * 4))) return false;
-  char* ws = static_cast<char*>(g_rt.ws);
-  cudaStream_t st = g_rt.stream;
-  if (!rt_check(cudaMemcpyAsync(ws + o_t, t, n * 4, cudaMemcpyHostToDevice, st), who) ||
-      !rt_check(cudaMemcpyAsync(ws + o_f, freqs, nf * 4, cudaMemcpyHostToDevice, st), who))
-    return false;
-  int rc = ANIMA_OK;
-  DeviceState* dev = current_device(&rc);
-  rc = rope_launch((const float*)(ws + o_t), (const float*)(ws + o_f), (float*)(ws + o_o), N, S,
-                   D, dev->sm_count, st);
-  if (rc != ANIMA_OK) return rt_fail(std::string(who) + ": " + code_name(rc));
-  if (!rt_check(cudaMemcpyAsync(out, ws + o_o, n * 4, cudaMemcpyDeviceToHost, st), who)) return false;
-  return rt_finish(who);
+  return rt_call("anima_rt_run_rope", {{t, n * 4}, {freqs, nf * 4}}, out, n * 4,
+                 [&](const void* const* in, void* y, int sms, cudaStream_t st) {
+                   return rope_launch((const float*)in[0], (const float*)in[1], (float*)y, N, S,
+                                      D, sms, st);
+                 });
+}
+
+// The reference's activation, normalisation and softmax entries fail before
+// anima_rt_init (anima_rt.cpp:24-57); its GEMM entries (gemm_backend.cpp:140-171) do not
+// need it.  Same here.
+static bool rt_act(int which, const float* x, float* out, int n, const char* who) {
+  if (!g_rt.inited) return rt_fail(std::string(who) + ": anima_rt_init has not been called");
+  if (!x || !out || n < 0) return rt_fail(std::string(who) + ": bad arguments");
+  if (n == 0) return true;
+  return rt_call(who, {{x, (size_t)n * 4}}, out, (size_t)n * 4,
+                 [&](const void* const* in, void* y, int sms, cudaStream_t st) {
+                   return act_launch(which, (const float*)in[0], (float*)y, n, sms, st);
+                 });
+}
+
+bool anima_rt_run_gelu(const float* x, float* out, int n) {
+  return rt_act(0, x, out, n, "anima_rt_run_gelu");
+}
+
+bool anima_rt_run_silu(const float* x, float* out, int n) {
+  return rt_act(1, x, out, n, "anima_rt_run_silu");
+}
+
+bool anima_rt_run_layernorm(const float* x, float* out, int m, int d, float eps) {
+  if (!g_rt.inited) return rt_fail("anima_rt_run_layernorm: anima_rt_init has not been called");
+  if (!x || !out || m < 0 || d <= 0) return rt_fail("anima_rt_run_layernorm: bad arguments");
+  if (m == 0) return true;
+  const size_t n = (size_t)m * d;
+  return rt_call("anima_rt_run_layernorm", {{x, n * 4}}, out, n * 4,
+                 [&](const void* const* in, void* y, int sms, cudaStream_t st) {
+                   return layernorm_launch((const float*)in[0], (float*)y, m, d, eps, sms, st);
+                 });
+}
+
+bool anima_rt_run_softmax(const float* x, float* out, int outer, int dim) {
+  if (!g_rt.inited) return rt_fail("anima_rt_run_softmax: anima_rt_init has not been called");
+  if (!x || !out || outer < 0 || dim <= 0) return rt_fail("anima_rt_run_softmax: bad arguments");
+  if (outer == 0) return true;
+  const size_t n = (size_t)outer * dim;
+  return rt_call("anima_rt_run_softmax", {{x, n * 4}}, out, n * 4,
+                 [&](const void* const* in, void* y, int sms, cudaStream_t st) {
+                   return softmax_launch((const float*)in[0], (float*)y, outer, dim, sms, st);
+                 });
+}
+
+static bool rt_gemm(const float* A, const void* Bm, bool bf16, float* C, int M, int N, int K,
+                    const char* who) {
+  if (!A || !Bm || !C || M < 0 || N < 0 || K < 0) return rt_fail(std::string(who) + ": bad arguments");
+  if (M == 0 || N == 0) return true;
+  return rt_call(who, {{A, (size_t)M * K * 4}, {Bm, (size_t)N * K * (bf16 ? 2 : 4)}}, C,
+                 (size_t)M * N * 4, [&](const void* const* in, void* y, int, cudaStream_t st) {
+                   return gemm_nt_launch((const float*)in[0], in[1], bf16, (float*)y, M, N, K, st);
+                 });
+}
+
+bool anima_rt_run_gemm_fp32(const float* A, const float* B, float* C, int M, int N, int K) {
+  return rt_gemm(A, B, false, C, M, N, K, "anima_rt_run_gemm_fp32");
+}
+
+bool anima_rt_run_gemm_bf16(const float* A, const uint16_t* W, float* C, int M, int N, int K) {
+  return rt_gemm(A, W, true, C, M, N, K, "anima_rt_run_gemm_bf16");
 }
 
 const char* anima_rt_last_error(void) { return g_last_error.c_str(); }

@@ -583,8 +583,8 @@ size_t attn_workspace_bytes(int B, int H, int S_q, int S_kv, unsigned flags, int
 }
 
 int attn_schedule_mode(int B, int H, int S_q, int S_kv, unsigned flags, int sm_count) {
-  static_assert(kSchedUnit == ANIMA_SCHED_UNIT && kSchedWhole == ANIMA_SCHED_WHOLE &&
-                    kSchedCut == ANIMA_SCHED_CUT,
+  static_assert((int)kSchedUnit == (int)ANIMA_SCHED_UNIT && (int)kSchedWhole == (int)ANIMA_SCHED_WHOLE &&
+                    (int)kSchedCut == (int)ANIMA_SCHED_CUT,
                 "schedule codes of the header");
   return plan_split(B * H, S_q, S_kv, flags, sm_count).mode;
 }
@@ -650,42 +650,28 @@ int attn_fwd_launch(const AnimaAttnArgs* a, int* status, int sm_count, cudaStrea
   }
 }
 
+// Device address of g_noalloc_scratch on the current device.  Host code must use this
+// address: the array's name in host code is a host-side stand-in.
+cudaError_t noalloc_scratch_address(void** ptr) { return cudaGetSymbolAddress(ptr, g_noalloc_scratch); }
+
 // Same launch as attn_fwd_launch, with the split schedule's scratch taken from
-// g_noalloc_scratch instead of the caller's workspace.  Host code only ever passes
-// the array's device address, looked up once per device with that device current.
-int attn_fwd_launch_noalloc(const AnimaAttnArgs* a, int* status, int sm_count, cudaStream_t st,
-                            const char** why) {
-  static void* scratch_ptr[64] = {};
-  int dev = -1;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) {
-    cudaGetLastError();
-    *why = "no usable CUDA device";
-    return ANIMA_ERR_CUDA;
-  }
-  if (!scratch_ptr[dev]) {
-    void* ptr = nullptr;
-    const cudaError_t e = cudaGetSymbolAddress(&ptr, g_noalloc_scratch);
-    if (e != cudaSuccess || !ptr) {
-      cudaGetLastError();
-      *why = "cudaGetSymbolAddress of the no-allocation scratch failed";
-      return ANIMA_ERR_CUDA;
-    }
-    scratch_ptr[dev] = ptr;
-  }
+// g_noalloc_scratch (its device address `scratch`, from noalloc_scratch_address) instead of
+// the caller's workspace.
+int attn_fwd_launch_noalloc(const AnimaAttnArgs* a, int* status, int sm_count, void* scratch,
+                            cudaStream_t st, const char** why) {
   const SplitPlan sp = plan_split(a->B * a->H, a->S_q, a->S_kv, a->flags, sm_count);
   if (sp.bytes > attn::kNoAllocScratchBytes) {
     *why = "this call's split schedule needs more scratch than the no-allocation entry's "
            "static array holds (it is sized for GPUs with up to 160 SMs)";
     return ANIMA_ERR_SHAPE;
   }
-  if (sp.bytes > 0 &&
-      cudaMemsetAsync(scratch_ptr[dev], 0, attn::kSemBytes, st) != cudaSuccess) {
+  if (sp.bytes > 0 && cudaMemsetAsync(scratch, 0, attn::kSemBytes, st) != cudaSuccess) {
     cudaGetLastError();
     *why = "clearing the no-allocation scratch counters failed";
     return ANIMA_ERR_CUDA;
   }
   AnimaAttnArgs b = *a;
-  b.workspace = scratch_ptr[dev];
+  b.workspace = scratch;
   b.workspace_bytes = attn::kNoAllocScratchBytes;
   return attn_fwd_launch(&b, status, sm_count, st);
 }

@@ -147,7 +147,9 @@ int anima_attn_fwd(const AnimaAttnArgs* args, void* stream);
  * on `stream` before its kernel; all calls on a device share the array, so calls that
  * overlap on the GPU (different streams, no ordering) race and must not be issued.
  * A call whose schedule would need more scratch than the array holds returns
- * ANIMA_ERR_SHAPE (see anima_rt_last_error). */
+ * ANIMA_ERR_SHAPE (see anima_rt_last_error).  ANIMA_FLAG_PAIR calls run the CTA-pair
+ * kernel, as in anima_attn_fwd; it uses no scratch.  No entry of this header allocates
+ * device memory: the status word below is a static device variable too. */
 int anima_attn_fwd_noalloc(const AnimaAttnArgs* args, void* stream);
 
 /* Workspace bytes anima_attn_fwd can use for this shape on the current device

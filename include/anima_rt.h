@@ -17,6 +17,7 @@
 #define ANIMA_RT_H_
 
 #include <stdbool.h>
+#include <stdint.h>
 
 #ifdef __cplusplus
 extern "C" {
@@ -59,6 +60,35 @@ bool anima_rt_run_rmsnorm(const float* x, const float* w, float* out, int m, int
  * ([cos, -sin, sin, cos] per pair), pairs (p, D/2 + p).  Bit-identical to the
  * reference (no fused multiply-add). */
 bool anima_rt_run_rope(const float* t, const float* freqs, float* out, int N, int S, int D);
+
+/* The rest of the symbols the reference's binding sets argtypes on
+ * (anima_rt/scripts/anima_rt_ops.py:12-27), so that binding loads this library.  They
+ * run on the device like the entries above (copy in, one kernel, copy back) and keep the
+ * reference's semantics; none of them is on the attention path.
+ *
+ * Replace anima_rt_run_gelu / anima_rt_run_silu (anima_rt/src/anima_rt.cpp:24-32;
+ * cpu/gelu_kernel.h:14-17, cpu/silu_kernel.h): out[i] = x*0.5*(1+erf(x/sqrt(2))) and
+ * x/(1+exp(-x)) over n fp32 values.  false before anima_rt_init, as in the reference. */
+bool anima_rt_run_gelu(const float* x, float* out, int n);
+bool anima_rt_run_silu(const float* x, float* out, int n);
+
+/* Replaces anima_rt_run_layernorm (anima_rt/src/anima_rt.cpp:36-43,
+ * cpu/layernorm_kernel.h): y = (x - mean) / sqrt(var + eps) per row of x [m, d], no
+ * affine (the reference passes null gamma/beta).  false before anima_rt_init. */
+bool anima_rt_run_layernorm(const float* x, float* out, int m, int d, float eps);
+
+/* Replaces anima_rt_run_softmax (anima_rt/src/anima_rt.cpp:52-57, cpu/softmax_kernel.h):
+ * y = exp(x - max) / sum(exp(x - max)) per row of x [outer, dim].  false before
+ * anima_rt_init. */
+bool anima_rt_run_softmax(const float* x, float* out, int outer, int dim);
+
+/* Replace anima_rt_run_gemm_fp32 / anima_rt_run_gemm_bf16
+ * (anima_rt/src/gemm_backend.cpp:140-171): C[M,N] = A[M,K] * B[N,K]^T with fp32 A and C;
+ * B fp32, or bf16 bit patterns (uint16) widened exactly to fp32.  fp32 arithmetic; the
+ * summation order differs from the reference's sequential loop.  Like the reference they
+ * do not require anima_rt_init. */
+bool anima_rt_run_gemm_fp32(const float* A, const float* B, float* C, int M, int N, int K);
+bool anima_rt_run_gemm_bf16(const float* A, const uint16_t* W, float* C, int M, int N, int K);
 
 /* Extension (no single reference counterpart): the whole per-block attention sequence
  * of NumpyAttention.forward (anima_rt/scripts/numpy_dit.py:285-294) in one call --

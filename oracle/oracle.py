@@ -31,7 +31,20 @@ import numpy as np
 HERE = os.path.dirname(os.path.abspath(__file__))
 PORT_SO = os.path.join(HERE, "liboracle.so")
 REF_SO = os.path.join(HERE, "_ref", "libanima_rt_ref.so")
-REF_TREE = os.environ.get("ANIMA_REFERENCE_TREE", "/root/reference")
+
+
+def reference_tree():
+    """The reference checkout: $ANIMA_REFERENCE_TREE, else a sibling checkout named
+    ``reference`` next to this repository; None when neither holds anima_rt/."""
+    cands = [os.environ.get("ANIMA_REFERENCE_TREE"),
+             os.path.join(os.path.dirname(os.path.dirname(HERE)), "reference")]
+    for c in cands:
+        if c and os.path.isdir(os.path.join(c, "anima_rt")):
+            return c
+    return None
+
+
+REF_TREE = reference_tree()
 
 _P = ct.c_void_p
 
@@ -39,7 +52,7 @@ _P = ct.c_void_p
 def build(ref: bool = True) -> None:
     """Compile liboracle.so and, when the reference tree exists, the reference lib."""
     subprocess.run(["make", "-s", "-C", HERE, "all"], check=True)
-    if ref and os.path.isdir(os.path.join(REF_TREE, "anima_rt")):
+    if ref and REF_TREE is not None:
         subprocess.run(["make", "-s", "-C", HERE, "ref", f"REF={REF_TREE}"], check=True)
 
 

@@ -1,7 +1,7 @@
 """Generate the golden fixtures in this directory from the reference itself.
 
-Run in a container that has the reference tree (default /root/reference, override with
-ANIMA_REFERENCE_TREE):
+Run where the reference checkout is available ($ANIMA_REFERENCE_TREE, or a sibling
+checkout named ``reference`` next to this repository):
 
     python tests/golden/make_golden.py
 
@@ -35,10 +35,13 @@ import numpy as np
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 REPO = os.path.dirname(os.path.dirname(HERE))
-REF = os.environ.get("ANIMA_REFERENCE_TREE", "/root/reference")
 sys.path.insert(0, REPO)
 
 from oracle import oracle as O  # noqa: E402
+
+REF = O.reference_tree()
+if REF is None:
+    raise SystemExit("no reference checkout: set ANIMA_REFERENCE_TREE")
 
 
 def _ref_python():

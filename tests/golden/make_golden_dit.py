@@ -22,9 +22,13 @@ import numpy as np
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 REPO = os.path.dirname(os.path.dirname(HERE))
-REF = os.environ.get("ANIMA_REFERENCE_TREE", "/root/reference")
 sys.path.insert(0, os.path.join(REPO, "anima-on-android_b200"))
 sys.path.insert(0, REPO)
+from oracle.oracle import reference_tree  # noqa: E402
+
+REF = reference_tree()
+if REF is None:
+    raise SystemExit("no reference checkout: set ANIMA_REFERENCE_TREE")
 
 CASES = {"small": dict(blocks=2, side=32), "full": dict(blocks=28, side=128)}
 WEIGHT_SEED, INPUT_SEED = 1234, 4321

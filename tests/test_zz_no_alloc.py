@@ -13,6 +13,7 @@ run every other test; it also passes on its own in a fresh process.
 """
 import ctypes as ct
 import math
+import os
 
 import numpy as np
 import pytest
@@ -39,13 +40,16 @@ def _args(L, q, k, v, out, B, H, Sq, Skv, workspace=None, flags=0):
     return a
 
 
-# With ANIMA_FLAG_SPLIT, (4096, 4096) and (1300, 700) run the split schedule (they use the
-# scratch); (512, 384) fits in one wave and uses none.
-@pytest.mark.parametrize("Sq,Skv", [(4096, 4096), (1300, 700), (512, 384)])
-def test_noalloc_entry_matches_workspace_entry_twice(Sq, Skv):
+# With ANIMA_FLAG_SPLIT, (4096, 4096) and (1300, 700) run the cut schedule (they use the
+# scratch); (512, 384) fits in one wave and runs one CTA per unit, using none.
+@pytest.mark.parametrize("Sq,Skv,sched", [(4096, 4096, "cut"), (1300, 700, "cut"),
+                                          (512, 384, "unit")])
+def test_noalloc_entry_matches_workspace_entry_twice(Sq, Skv, sched):
     from anima_attn import _lib as L
     torch.cuda.set_device(0)
     B, H = 2, 16
+    want = {"cut": L.SCHED_CUT, "unit": L.SCHED_UNIT}[sched]
+    assert L.lib.anima_attn_schedule(B, H, Sq, Skv, L.FLAG_SPLIT, 0) == want
     g = torch.Generator(device="cuda").manual_seed(Sq + Skv)
     q = torch.randn(B * H, Sq, 128, device="cuda", generator=g).to(torch.bfloat16)
     k = torch.randn(B * H, Skv, 128, device="cuda", generator=g).to(torch.bfloat16)
@@ -72,3 +76,106 @@ def test_noalloc_entry_matches_workspace_entry_twice(Sq, Skv):
         o = out.cpu().numpy()
         assert np.isfinite(o).all()
         assert rel_l2(o, r) <= ATTN_REL_L2 and max_abs(o, r) <= ATTN_MAX_ABS
+
+
+# A fresh process that loads the library, sets up its device state through a
+# device-pointer entry, and then measures the device's free memory around two calls of
+# the no-allocation entry on the cut schedule.  CUDA_MODULE_LOADING=EAGER loads every
+# kernel module of the library (and so reserves the static scratch) when the library's
+# runtime first initialises, i.e. before the first measurement; from then on any device
+# allocation by the entry -- its own cudaMalloc, or a local-memory reservation grown by a
+# kernel launch -- would lower the free memory.  No torch in that process: its buffers
+# come from the CUDA runtime directly, allocated before the first measurement.
+_FRESH = r"""
+import ctypes as ct, json, math, os, sys
+import numpy as np
+sys.path[:0] = [os.environ["PKG_ROOT"]]
+from anima_attn import _lib as L
+rt = ct.CDLL(os.environ["CUDART"])
+rt.cudaMemGetInfo.argtypes = [ct.POINTER(ct.c_size_t)] * 2
+rt.cudaMalloc.argtypes = [ct.POINTER(ct.c_void_p), ct.c_size_t]
+rt.cudaMemcpy.argtypes = [ct.c_void_p, ct.c_void_p, ct.c_size_t, ct.c_int]
+rt.cudaMemset.argtypes = [ct.c_void_p, ct.c_int, ct.c_size_t]
+assert rt.cudaSetDevice(0) == 0
+B, H, S, D = 2, 16, 4096, 128
+def dmalloc(n):
+    p = ct.c_void_p()
+    assert rt.cudaMalloc(ct.byref(p), n) == 0
+    return p.value
+rng = np.random.default_rng(5)
+ops = []
+for _ in range(3):
+    a = rng.standard_normal((B * H, S, D), dtype=np.float32)
+    bits = (a.view(np.uint32) >> 16).astype(np.uint16)  # bf16 by truncation
+    p = dmalloc(bits.nbytes)
+    assert rt.cudaMemcpy(p, bits.ctypes.data, bits.nbytes, 1) == 0
+    ops.append(p)
+nout = B * S * H * D * 4
+outs = [dmalloc(nout) for _ in range(3)]
+need = int(L.lib.anima_attn_workspace_size(B, H, S, S, L.FLAG_SPLIT))
+ws = dmalloc(need)
+assert rt.cudaMemset(ws, 0, need) == 0
+def args(out, workspace):
+    a = L.AttnArgs()
+    a.q, a.k, a.v = ops
+    a.op_dtype = L.DTYPE_BF16
+    a.out, a.out_dtype = out, L.DTYPE_F32
+    a.out_stride[:] = [S * H * D, D, H * D]
+    a.B, a.H, a.S_q, a.S_kv, a.D = B, H, S, S, D
+    a.scale, a.flags = 1 / math.sqrt(D), L.FLAG_SPLIT
+    a.kv_valid_len = None
+    a.workspace, a.workspace_bytes = workspace, (need if workspace else 0)
+    return a
+sm, cc = ct.c_int(), ct.c_int()
+assert L.lib.anima_attn_device_info(ct.byref(sm), ct.byref(cc)) == 0
+assert L.lib.anima_attn_schedule(B, H, S, S, L.FLAG_SPLIT, 0) == L.SCHED_CUT
+def free():
+    assert rt.cudaDeviceSynchronize() == 0
+    f, t = ct.c_size_t(), ct.c_size_t()
+    assert rt.cudaMemGetInfo(ct.byref(f), ct.byref(t)) == 0
+    return f.value
+f0 = free()
+for out in outs[:2]:
+    assert L.lib.anima_attn_fwd_noalloc(ct.byref(args(out, None)), None) == 0, L.last_error()
+f1 = free()
+assert L.lib.anima_attn_fwd(ct.byref(args(outs[2], ws)), None) == 0
+assert L.lib.anima_attn_status(None, 1) == 0
+res = []
+for out in outs:
+    h = np.empty(nout // 4, np.float32)
+    assert rt.cudaMemcpy(h.ctypes.data, out, nout, 2) == 0
+    res.append(h)
+print(json.dumps({"free_before": f0, "free_after": f1,
+                  "max_diff": [float(np.abs(r - res[2]).max()) for r in res[:2]],
+                  "finite": bool(all(np.isfinite(r).all() for r in res))}))
+"""
+
+
+def _cudart():
+    import glob
+    cands = glob.glob("/usr/local/cuda/lib64/libcudart.so.12*")
+    try:
+        import nvidia.cuda_runtime as cr
+        cands += glob.glob(os.path.join(os.path.dirname(cr.__file__), "lib", "libcudart.so.12*"))
+    except ImportError:
+        pass
+    if not cands:
+        pytest.skip("no libcudart.so.12 found")
+    return sorted(cands)[0]
+
+
+def test_noalloc_entry_allocates_nothing_in_a_fresh_process():
+    import json
+    import subprocess
+    import sys
+    from conftest import PKG_ROOT
+    env = dict(os.environ, CUDA_MODULE_LOADING="EAGER", PKG_ROOT=PKG_ROOT, CUDART=_cudart(),
+               CUDA_VISIBLE_DEVICES=os.environ.get("CUDA_VISIBLE_DEVICES", "0"))
+    r = subprocess.run([sys.executable, "-c", _FRESH], env=env, capture_output=True, text=True,
+                       timeout=300)
+    assert r.returncode == 0, r.stderr[-2000:]
+    res = json.loads(r.stdout.strip().splitlines()[-1])
+    assert res["finite"]
+    # same kernel, same schedule, scratch in a different place: identical results
+    assert res["max_diff"] == [0.0, 0.0], res
+    assert res["free_after"] == res["free_before"], res
