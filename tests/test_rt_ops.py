@@ -133,7 +133,8 @@ def test_layernorm_softmax_match_torch(rt, m, d):
     if ref_lib is not None:
         r2 = np.zeros((m, d), np.float32)
         assert ref_lib.anima_rt_run_softmax(x.ctypes.data, r2.ctypes.data, m, d)
-        assert max_abs(out, r2) <= 1e-6
+        # the reference sums a row sequentially in fp32: its own error grows with d
+        assert rel_l2(out, r2) <= 1e-5 and max_abs(out, r2) <= 5e-6
 
 
 @pytest.mark.gpu
