@@ -136,16 +136,41 @@ def timestep_sinusoid(t: torch.Tensor, channels: int) -> torch.Tensor:
     return torch.cat([torch.cos(emb), torch.sin(emb)], dim=-1)[:, None, :]
 
 
+# CUDA-event regions of one profiled step (profile_step): None outside it.
+_REGIONS: Optional[list] = None
+
+
+class _region:
+    """Brackets the work of one category (gemm, attention, fused, collective) on the current
+    stream with CUDA events while a step is being profiled; a no-op otherwise."""
+    __slots__ = ("cat", "e0")
+
+    def __init__(self, cat: str):
+        self.cat = cat
+
+    def __enter__(self):
+        if _REGIONS is not None:
+            self.e0 = torch.cuda.Event(enable_timing=True)
+            self.e0.record()
+
+    def __exit__(self, *exc):
+        if _REGIONS is not None:
+            e1 = torch.cuda.Event(enable_timing=True)
+            e1.record()
+            _REGIONS.append((self.cat, self.e0, e1))
+
+
 def _linear(x: torch.Tensor, w: torch.Tensor, out_dtype=torch.float32) -> torch.Tensor:
     """x [..., K] @ w[N, K]^T: operands in w's 16-bit type, fp32 accumulation, output in
     ``out_dtype`` (fp32, or w's type)."""
     shp = x.shape
     x2 = x.reshape(-1, shp[-1])
     if x.is_cuda:
-        if out_dtype == w.dtype:
-            y = torch.mm(x2.to(w.dtype), w.t())
-        else:
-            y = torch.mm(x2.to(w.dtype), w.t(), out_dtype=out_dtype)
+        with _region("gemm"):
+            if out_dtype == w.dtype:
+                y = torch.mm(x2.to(w.dtype), w.t())
+            else:
+                y = torch.mm(x2.to(w.dtype), w.t(), out_dtype=out_dtype)
     else:  # CPU tests of the sharding logic: same operand rounding, fp32 math
         y = (x2.to(w.dtype).float() @ w.float().t()).to(out_dtype)
     return y.reshape(*shp[:-1], w.shape[0])
@@ -225,7 +250,8 @@ class AnimaDiT:
         """LayerNorm(x) * (1 + scale) + shift as the next GEMM's 16-bit operand."""
         if x.is_cuda:
             from .ops import ln_modulate
-            return ln_modulate(x, scale, shift, self.cfg.eps, out_dtype=self.cfg.gemm_dtype)
+            with _region("fused"):
+                return ln_modulate(x, scale, shift, self.cfg.eps, out_dtype=self.cfg.gemm_dtype)
         h = F.layer_norm(x, (x.shape[-1],), eps=self.cfg.eps) * (1 + scale) + shift
         return h.to(self.cfg.gemm_dtype)
 
@@ -239,8 +265,9 @@ class AnimaDiT:
         gate, y = pending
         if x.is_cuda:
             from .ops import gate_residual_ln_modulate_
-            return x, gate_residual_ln_modulate_(x, gate, y, scale, shift, self.cfg.eps,
-                                                 out_dtype=self.cfg.gemm_dtype)
+            with _region("fused"):
+                return x, gate_residual_ln_modulate_(x, gate, y, scale, shift, self.cfg.eps,
+                                                     out_dtype=self.cfg.gemm_dtype)
         x = x + gate * y
         return x, self._ln_mod(x, scale, shift)
 
@@ -250,7 +277,8 @@ class AnimaDiT:
         CUDA; fp32 arithmetic either way."""
         if h.is_cuda and h.numel() % 8 == 0 and h.is_contiguous():
             from .ops import gelu_
-            return gelu_(h)
+            with _region("fused"):
+                return gelu_(h)
         return F.gelu(h.float()).to(h.dtype)
 
     def _mods(self, p, emb, lora):
@@ -301,14 +329,17 @@ class AnimaDiT:
     def _by_rank_linear(self, h, w):
         """h [n, K] @ w[r]^T for every rank r -> [N, n, M] (the all-to-all send buffer)."""
         if h.is_cuda:
-            return torch.matmul(h.to(w.dtype), w.transpose(1, 2))
+            with _region("gemm"):
+                return torch.matmul(h.to(w.dtype), w.transpose(1, 2))
         return (h.to(w.dtype).float() @ w.float().transpose(1, 2)).to(w.dtype)
 
     def _a2a(self, t: torch.Tensor) -> torch.Tensor:
         """all_to_all_single over dim 0 (destination rank in, source rank out)."""
         import torch.distributed as dist
         out = torch.empty_like(t)
-        dist.all_to_all_single(out, t.contiguous(), group=self.group)
+        t = t.contiguous()
+        with _region("collective"):
+            dist.all_to_all_single(out, t, group=self.group)
         return out
 
     def _attention_rows(self, p, h_loc, B, L, ctx, freqs):
@@ -325,8 +356,9 @@ class AnimaDiT:
             Skv = ctx.shape[1]
             kv = _linear(ctx, self.w[p + ".kv"], dt).view(B, Skv, 2, hl, hd)
             k, v = kv[:, :, 0], kv[:, :, 1]
-        o = self.attn_fn(q, k, v, self.w[p + ".q_norm.weight"], self.w[p + ".k_norm.weight"],
-                         freqs if ctx is None else None, eps=cfg.eps, out_dtype=dt, op_dtype=dt)
+        with _region("attention"):
+            o = self.attn_fn(q, k, v, self.w[p + ".q_norm.weight"], self.w[p + ".k_norm.weight"],
+                             freqs if ctx is None else None, eps=cfg.eps, out_dtype=dt, op_dtype=dt)
         # [B, L, hl, hd] = [N, n, hl*hd] by destination rank -> [N (source heads), n, hl*hd]
         o = self._a2a(o.reshape(N, n, hl * hd))
         o = o.permute(1, 0, 2).reshape(n, N * hl * hd)  # my rows, heads in order
@@ -355,7 +387,9 @@ class AnimaDiT:
         # gathered along dim 0 ([world * B, S, H/N, hd]); viewed as [world, B, ...]
         full = torch.empty((self.world * B,) + tuple(o_local.shape[1:]), dtype=o_local.dtype,
                            device=o_local.device)
-        dist.all_gather_into_tensor(full, o_local.contiguous(), group=self.group)
+        o_local = o_local.contiguous()
+        with _region("collective"):
+            dist.all_gather_into_tensor(full, o_local, group=self.group)
         full = full.view((self.world,) + tuple(o_local.shape))
         out = None
         for r in range(self.world):
@@ -376,9 +410,10 @@ class AnimaDiT:
             q = _linear(x, self.w[p + ".q_proj.weight"], dt).view(B, S, hl, hd)
             kv = _linear(src, self.w[p + ".kv"], dt).view(B, Skv, 2, hl, hd)
             k, v = kv[:, :, 0], kv[:, :, 1]
-        o = self.attn_fn(q, k, v, self.w[p + ".q_norm.weight"], self.w[p + ".k_norm.weight"],
-                         freqs if ctx is None else None, eps=cfg.eps, out_dtype=cfg.gemm_dtype,
-                         op_dtype=cfg.gemm_dtype)
+        with _region("attention"):
+            o = self.attn_fn(q, k, v, self.w[p + ".q_norm.weight"], self.w[p + ".k_norm.weight"],
+                             freqs if ctx is None else None, eps=cfg.eps, out_dtype=cfg.gemm_dtype,
+                             op_dtype=cfg.gemm_dtype)
         return self._gather_oproj(o, self.w[p + ".output_proj.weight"])
 
     def _block(self, b: int, x, pending, emb, lora, ctx, freqs):
@@ -431,7 +466,9 @@ class AnimaDiT:
             part = _linear(h, w["final_layer.linear.weight"])  # [n, p*p*t*C]
             import torch.distributed as dist
             out = torch.empty((R, part.shape[1]), dtype=part.dtype, device=part.device)
-            dist.all_gather_into_tensor(out, part.contiguous(), group=self.group)
+            part = part.contiguous()
+            with _region("collective"):
+                dist.all_gather_into_tensor(out, part, group=self.group)
             out = out.view(B, L, -1)
         else:
             h = _linear(xp, w["x_embedder.proj.1.weight"])  # [B, L, hidden]
@@ -492,3 +529,36 @@ class StepGraph:
         self.graph.replay()
         return self.out
 
+
+
+def profile_step(model: "AnimaDiT", x, sigma: float, sigma_next: float, ctx_cond, ctx_uncond,
+                 cfg_scale: float) -> dict:
+    """One eager ``euler_cfg_step`` with CUDA events around every GEMM, attention call (fused
+    prologue + attention kernels), fused LayerNorm/residual/GELU pass and collective.
+    Returns the step's device time and each category's total in ms and as a share of it;
+    "other" is the rest (torch elementwise ops, launch gaps, waits).  A collective's time
+    includes its wait for the slowest rank.  Event pairs add a little overhead, so these are
+    shares of an eager step, not of the graph-replayed one."""
+    global _REGIONS
+    torch.cuda.synchronize()
+    _REGIONS = []
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    try:
+        e0.record()
+        model.euler_cfg_step(x, sigma, sigma_next, ctx_cond, ctx_uncond, cfg_scale)
+        e1.record()
+        torch.cuda.synchronize()
+        regions, _REGIONS = _REGIONS, None
+    finally:
+        _REGIONS = None
+    total = e0.elapsed_time(e1)
+    cats: Dict[str, float] = {}
+    counts: Dict[str, int] = {}
+    for cat, a, b in regions:
+        cats[cat] = cats.get(cat, 0.0) + a.elapsed_time(b)
+        counts[cat] = counts.get(cat, 0) + 1
+    cats["other"] = max(0.0, total - sum(cats.values()))
+    return {"step_ms": round(total, 3),
+            "ms": {k: round(v, 3) for k, v in cats.items()},
+            "share": {k: round(v / total, 4) for k, v in cats.items()},
+            "calls": counts}

@@ -175,19 +175,19 @@ __global__ void __launch_bounds__(kThreads, 1)
       // of the MN-major V tile at row 16 * kk (2 KiB per step).
       const uint64_t dk0 = sdesc_sw128(smem_u32(sm.kv[0]), 16, 1024);      // K, slot 0
       const uint64_t dv0 = sdesc_sw128(smem_u32(sm.kv[0]), kPanel, 1024);  // V, slot 0
-      uint64_t dq[kNT][8];  // Q tile i, step kk: fixed for the whole kernel
-#pragma unroll
-      for (int i = 0; i < kNT; ++i)
-#pragma unroll
-        for (int kk = 0; kk < 8; ++kk)
-          dq[i][kk] = sdesc_sw128(smem_u32(sm.q[i]) + (kk >> 2) * kPanel + (kk & 3) * 32, 16, 1024);
+      const uint64_t dq0 = sdesc_sw128(smem_u32(sm.q[0]), 16, 1024);  // Q tile 0, step 0
 
+      // The Q descriptors are recomputed per call (one add each) rather than held: a table
+      // of all 16 held 32 registers of this thread's budget and made it spill.
       auto issue_qk = [&](int i, int slot) {
         const uint64_t kb = desc_plus(dk0, (uint32_t)slot * kTile);
-        uint64_t b[8];
+        uint64_t b[8], aq[8];
 #pragma unroll
-        for (int kk = 0; kk < 8; ++kk) b[kk] = desc_plus(kb, (kk >> 2) * kPanel + (kk & 3) * 32);
-        umma_ss_x8(tmem + i * 128, dq[i], b, idesc_qk, 0u);
+        for (int kk = 0; kk < 8; ++kk) {
+          b[kk] = desc_plus(kb, (kk >> 2) * kPanel + (kk & 3) * 32);
+          aq[kk] = desc_plus(dq0, (uint32_t)i * kTile + (kk >> 2) * kPanel + (kk & 3) * 32);
+        }
+        umma_ss_x8(tmem + i * 128, aq, b, idesc_qk, 0u);
       };
       auto issue_pv = [&](int i, int slot, bool acc) {
         const uint64_t vb = desc_plus(dv0, (uint32_t)slot * kTile);
@@ -355,19 +355,29 @@ __global__ void __launch_bounds__(kThreads, 1)
           const uint64_t scale2 = f2pack(sl2, sl2), base2 = f2pack(nb, nb);
 #pragma unroll
           for (int k = 0; k < 4; ++k) sum2[k] = 0ull;
+          // The polynomial share is fixed per pair at compile time, and the test of `full`
+          // sits outside the unrolled loop: a runtime test per pair makes the compiler branch
+          // or evaluate both exponentials, which saves no MUFU work.
+          auto pass = [&](auto pc) {
+            constexpr bool kPoly = decltype(pc)::value;
 #pragma unroll
-          for (int pr = 0; pr < 64; ++pr) {
-            float x0, x1;
-            f2unpack(fma2(f2pack(SV(2 * pr), SV(2 * pr + 1)), scale2, base2), x0, x1);
-            if (full && (pr & 7) < kPolyPer8) {
-              exp2_poly_pair(x0, x1);
-            } else {
-              x0 = ex2_approx(x0);
-              x1 = ex2_approx(x1);
+            for (int pr = 0; pr < 64; ++pr) {
+              float x0, x1;
+              f2unpack(fma2(f2pack(SV(2 * pr), SV(2 * pr + 1)), scale2, base2), x0, x1);
+              if (kPoly && (pr & 7) < kPolyPer8) {
+                exp2_poly_pair(x0, x1);
+              } else {
+                x0 = ex2_approx(x0);
+                x1 = ex2_approx(x1);
+              }
+              sum2[pr & 3] = add2(sum2[pr & 3], f2pack(x0, x1));
+              pk[pr >> 5][pr & 31] = pack2<kOp>(x0, x1);
             }
-            sum2[pr & 3] = add2(sum2[pr & 3], f2pack(x0, x1));
-            pk[pr >> 5][pr & 31] = pack2<kOp>(x0, x1);
-          }
+          };
+          if (kPolyPer8 > 0 && full)
+            pass(std::true_type{});
+          else
+            pass(std::false_type{});
         };
         auto row_sum = [&]() {
           float sa, sb;

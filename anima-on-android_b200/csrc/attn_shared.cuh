@@ -3,6 +3,8 @@
 // parameters, the segment walk of the three schedules (one CTA per unit, persistent whole
 // units, and the cut last round), and the staged output epilogue.
 #pragma once
+#include <type_traits>
+
 #include "common.cuh"
 
 namespace anima {

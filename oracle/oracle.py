@@ -252,3 +252,19 @@ def prologue(q, k, v, q_w, k_w, freqs=None, eps=1e-6, kind="port"):
         kn = rope(kn, freqs, kind)
     tr = lambda t: np.ascontiguousarray(_f32(t).transpose(0, 2, 1, 3))
     return tr(qn), tr(kn), tr(v)
+
+
+def numpy_rope(t, freqs):
+    """The reference's live-path RoPE, numpy broadcasting on [B, S, H, D] fp32
+    (anima_rt/scripts/numpy_dit.py:33-37, the numpy twin of predict2.apply_rotary_pos_emb):
+    with freqs [S, D/2, 2, 2] = [[cos, -sin], [sin, cos]] per pair p and x = (t[p], t[p+D/2]),
+    out[p] = cos x0 - sin x1, out[p+D/2] = sin x0 + cos x1, computed as the reference does
+    (elementwise products of broadcast arrays, fp32), so its cost is the reference's cost.
+    Used as the timed CPU baseline of the prologue and as a checker."""
+    t = np.asarray(t, dtype=np.float32)
+    B, S, H, D = t.shape
+    half = D // 2
+    f = np.asarray(freqs, dtype=np.float32).reshape(S, 1, half, 2, 2)
+    x = np.moveaxis(t.reshape(B, S, H, 2, half), -2, -1)[..., None, :]  # [B,S,H,half,1,2]
+    y = f[..., 0] * x[..., 0] + f[..., 1] * x[..., 1]                   # [B,S,H,half,2]
+    return np.moveaxis(y, -1, -2).reshape(B, S, H, D)

@@ -39,6 +39,9 @@ def test_rope_matches_reference_fixture():
     assert np.array_equal(O.rope(g["t"], g["freqs"]), g["out_anima_rt"])
     # predict2.apply_rotary_pos_emb (torch) agrees to fp32 rounding
     assert max_abs(g["out_anima_rt"], g["out_predict2"]) < 1e-5
+    # the numpy restatement of numpy_dit._numpy_rope (the CPU prologue baseline)
+    assert np.array_equal(O.numpy_rope(g["t"], g["freqs"]), g["out_anima_rt"])
+    assert max_abs(O.numpy_rope(g["t"], g["freqs"]), g["out_predict2"]) < 1e-5
 
 
 def test_rope_table_matches_video_rope_3d():
