@@ -11,8 +11,8 @@ Import from the repository root with the distribution folder on sys.path:
 """
 from . import _lib
 from ._lib import AnimaError, last_error
-from .ops import attention, attention_core, device_info, prologue, sdpa, status, version
+from .ops import apply_rope, attention, attention_core, device_info, prologue, sdpa, status, version
 from .rope import rope_freqs_3d
 
-__all__ = ["AnimaError", "attention", "attention_core", "device_info", "last_error",
+__all__ = ["AnimaError", "apply_rope", "attention", "attention_core", "device_info", "last_error",
            "prologue", "rope_freqs_3d", "sdpa", "status", "version", "_lib"]

@@ -70,6 +70,8 @@ SIGNATURES = {
     "anima_attn_schedule": ([ct.c_int] * 4 + [ct.c_uint, ct.c_int], ct.c_int),
     "anima_attn_status": ([_P, ct.c_int], ct.c_int),
     "anima_attn_selftest_timeout": ([ct.c_uint, _P], ct.c_int),
+    "anima_attn_rope": ([_P, ct.POINTER(ct.c_int64), _P, _P, ct.POINTER(ct.c_int64), ct.c_int,
+                         ct.c_int, ct.c_int, ct.c_int, _P], ct.c_int),
     "anima_dit_ln_modulate": ([_P, _P, _P, ct.c_int64, _P, ct.c_int, ct.c_int64, ct.c_int, ct.c_int,
                                ct.c_float, _P], ct.c_int),
     "anima_dit_gate_residual": ([_P, _P, ct.c_int64, _P, ct.c_int64, ct.c_int, ct.c_int, _P], ct.c_int),

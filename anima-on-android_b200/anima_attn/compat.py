@@ -157,21 +157,67 @@ class AnimaRTRMSNorm(nn.RMSNorm):
         return res.reshape(*batch, D) if batch else res.squeeze(0)
 
 
-def patch_predict2(p2) -> None:
+class Predict2Backend:
+    """The three operations patch_predict2 installs.  The default is this library on the
+    GPU; CPU tests pass stand-ins with the same signatures to check the patch's plumbing
+    against the reference model (the GPU kernels are tested on the GPU on their own).
+      sdpa(q, k, v)                      [B, H, S, D] -> [B, H, S_q, D], q's dtype
+      rope(t, freqs)                     t [B, S, H, D], freqs [S, D/2, 2, 2] -> t's shape
+      attention(q, k, v, q_norm_w, k_norm_w, rope_freqs, eps=..., out_dtype=...)
+                                         ops.attention's signature"""
+
+    def __init__(self, sdpa=None, rope=None, attention=None):
+        self.sdpa = sdpa or ops.sdpa
+        self.rope = rope or _rope_any_device
+        self.attention = attention or ops.attention
+
+
+def _rope_any_device(t, freqs):
+    """apply_rotary_pos_emb on CUDA tensors through anima_attn_rope; on host tensors through
+    the reference-facing host ABI (anima_rt_run_rope)."""
+    if t.is_cuda:
+        return ops.apply_rope(t, freqs)
+    S, D = t.shape[1], t.shape[-1]
+    f = np.ascontiguousarray(freqs.detach().float().reshape(S, D // 2, 2, 2).numpy())
+    out = anima_rt_rope(t.detach().float().numpy(), f)
+    return torch.from_numpy(out).to(dtype=t.dtype).reshape(t.shape)
+
+
+def _freqs_per_token(rope_emb, S, D):
+    """predict2 hands the blocks the 3D RoPE table as [1, S, 1, D/2, 2, 2] (a broadcast
+    shape, no batch; src/predict2.py:885).  Returns it as [S, D/2, 2, 2]; a table of another
+    size (for instance with a real batch dimension) is rejected rather than misread."""
+    if rope_emb.numel() != S * D * 2:
+        raise ValueError(f"rope_emb of shape {tuple(rope_emb.shape)} does not hold one "
+                         f"[{D // 2}, 2, 2] entry per token of a {S}-token sequence")
+    return rope_emb.reshape(S, D // 2, 2, 2)
+
+
+def patch_predict2(p2, backend: "Predict2Backend" = None, fused: bool = True) -> dict:
     """Route a loaded ``predict2`` module's attention through the B200 library.
 
+    The reference's own patch points (anima_rt/scripts/phone_pipeline_anima_rt.py:224-252):
     * ``_scaled_dot_product_attention(q, k, v, heads, skip_reshape)`` (predict2.py:25-29)
-      -> ops.sdpa;
-    * ``Attention.forward`` (predict2.py:201-214) -> projections with the module's own
-      Linear layers, then ONE fused call (q/k RMSNorm with the module's weights, RoPE
-      when self-attention, SDPA), then ``output_proj``.
-    """
+      -> backend.sdpa, reshaped as the reference does;
+    * ``apply_rotary_pos_emb(t, freqs)`` (predict2.py:31-38) -> backend.rope;
+    and, going further than the reference, ``Attention.forward`` (predict2.py:201-214): the
+    module's own projections, then ONE fused call (q/k RMSNorm with the module's weights,
+    RoPE for self-attention, SDPA), then ``output_proj``.  fused=False patches only the
+    reference's two points.  Returns the replaced originals (restore them with
+    unpatch_predict2)."""
+    be = backend or Predict2Backend()
+    orig = {"_scaled_dot_product_attention": p2._scaled_dot_product_attention,
+            "apply_rotary_pos_emb": p2.apply_rotary_pos_emb,
+            "Attention.forward": p2.Attention.forward}
 
     def _sdpa(q, k, v, heads, skip_reshape=False, transformer_options=None):
-        out = ops.sdpa(q, k, v)
+        out = be.sdpa(q, k, v)
         if skip_reshape:
             return out.transpose(1, 2).reshape(q.shape[0], -1, heads * q.shape[-1])
         return out.reshape(q.shape[0], q.shape[2], heads * q.shape[-1])
+
+    def _rope(t, freqs):
+        return be.rope(t, _freqs_per_token(freqs, t.shape[1], t.shape[-1]))
 
     def _forward(self, x, context=None, rope_emb=None, transformer_options={}):
         ctx = x if context is None else context
@@ -183,12 +229,22 @@ def patch_predict2(p2) -> None:
         v = self.v_proj(ctx).view(B, Skv, H, D)
         freqs = None
         if self.is_selfattn and rope_emb is not None:
-            freqs = rope_emb.reshape(Sq, D // 2, 2, 2)
-        o = ops.attention(q, k, v, self.q_norm.weight, self.k_norm.weight, freqs,
-                          eps=self.q_norm.eps if self.q_norm.eps is not None else 1e-6,
-                          out_dtype=torch.float32 if x.dtype == torch.float32 else torch.bfloat16)
+            freqs = _freqs_per_token(rope_emb, Sq, D)
+        eps = self.q_norm.eps if getattr(self.q_norm, "eps", None) is not None else 1e-6
+        o = be.attention(q, k, v, self.q_norm.weight, self.k_norm.weight, freqs, eps=eps,
+                         out_dtype=torch.float32 if x.dtype == torch.float32 else torch.bfloat16)
         o = o.reshape(B, Sq, H * D).to(x.dtype)
         return self.output_dropout(self.output_proj(o))
 
     p2._scaled_dot_product_attention = _sdpa
-    p2.Attention.forward = _forward
+    p2.apply_rotary_pos_emb = _rope
+    if fused:
+        p2.Attention.forward = _forward
+    return orig
+
+
+def unpatch_predict2(p2, orig: dict) -> None:
+    """Undo patch_predict2 with the originals it returned."""
+    p2._scaled_dot_product_attention = orig["_scaled_dot_product_attention"]
+    p2.apply_rotary_pos_emb = orig["apply_rotary_pos_emb"]
+    p2.Attention.forward = orig["Attention.forward"]

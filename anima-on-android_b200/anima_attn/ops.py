@@ -228,6 +228,35 @@ def sdpa(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, scale: Optional[floa
     return o if o.dtype == q.dtype else o.to(q.dtype)
 
 
+def apply_rope(t: torch.Tensor, freqs: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """predict2.apply_rotary_pos_emb (src/predict2.py:31-38) on the GPU.
+
+    t [B, S, H, D] (any strides, D contiguous) or [N, S, D]; freqs holding [S, D/2, 2, 2]
+    values (predict2's [1, S, 1, D/2, 2, 2] broadcast shape is accepted).  Computes in fp32
+    and returns t's dtype, like the reference."""
+    _check_cuda(t, freqs)
+    if t.dim() == 3:
+        tv = t.unsqueeze(2)
+    elif t.dim() == 4:
+        tv = t
+    else:
+        raise ValueError("t must be [B, S, H, D] or [N, S, D]")
+    O, S, Hn, D = tv.shape
+    fr = freqs.detach().to(device=t.device, dtype=torch.float32).reshape(-1).contiguous()
+    if fr.numel() != S * D * 2:
+        raise ValueError(f"freqs must hold [S={S}, {D // 2}, 2, 2] values, got {freqs.shape}")
+    src = tv if tv.dtype == torch.float32 else tv.float()
+    if src.stride(3) != 1:
+        src = src.contiguous()
+    res = torch.empty((O, S, Hn, D), device=t.device, dtype=torch.float32) if out is None else out
+    ts = (ct.c_int64 * 3)(src.stride(0), src.stride(1), src.stride(2))
+    os_ = (ct.c_int64 * 3)(res.stride(0), res.stride(1), res.stride(2))
+    L.check(L.lib.anima_attn_rope(_ptr(src), ts, _ptr(fr), _ptr(res), os_, O, S, Hn, D,
+                                  ct.c_void_p(_stream())), "anima_attn_rope")
+    res = res.view(t.shape) if t.dim() == 3 else res
+    return res if res.dtype == t.dtype else res.to(t.dtype)
+
+
 def ln_modulate(x: torch.Tensor, scale: torch.Tensor, shift: torch.Tensor, eps: float = 1e-6,
                 out_dtype=torch.float16) -> torch.Tensor:
     """LayerNorm(x) * (1 + scale) + shift -> out_dtype, one pass (DiT block, predict2.py:512).

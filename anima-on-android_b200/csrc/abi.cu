@@ -40,6 +40,9 @@ int rmsnorm_launch(const float* x, const float* w, float* y, long long m, int d,
                    int sm_count, cudaStream_t st);
 int rope_launch(const float* t, const float* f, float* out, int N, int S, int D, int sm_count,
                 cudaStream_t st);
+int rope_strided_launch(const float* t, const long long* ts, const float* f, float* out,
+                        const long long* os, int O, int S, int Hn, int D, int sm_count,
+                        cudaStream_t st);
 int act_launch(int which, const float* x, float* y, long long n, int sm_count, cudaStream_t st);
 int layernorm_launch(const float* x, float* y, long long m, int d, float eps, int sm_count,
                      cudaStream_t st);
@@ -547,6 +550,23 @@ int anima_attn_status(void* stream, int reset) {
   }
   if (reset && code) cudaMemset(d->status, 0, sizeof(int));
   return code;
+}
+
+int anima_attn_rope(const float* t, const int64_t t_stride[3], const float* freqs, float* out,
+                    const int64_t out_stride[3], int O, int S, int Hn, int D, void* stream) {
+  if (!t || !t_stride || !freqs || !out || !out_stride || O < 0 || S < 0 || Hn < 0 || D <= 0 ||
+      (D & 1))
+    return ANIMA_ERR_ARG;
+  for (int i = 0; i < 3; ++i)
+    if (t_stride[i] < 0 || out_stride[i] < 0) return ANIMA_ERR_ARG;
+  if ((long long)O * S * Hn == 0) return ANIMA_OK;
+  int rc = ANIMA_OK;
+  DeviceState* d = current_device(&rc);
+  if (!d) return rc;
+  const long long ts[3] = {t_stride[0], t_stride[1], t_stride[2]};
+  const long long os[3] = {out_stride[0], out_stride[1], out_stride[2]};
+  return rope_strided_launch(t, ts, freqs, out, os, O, S, Hn, D, d->sm_count,
+                             static_cast<cudaStream_t>(stream));
 }
 
 static bool al16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }

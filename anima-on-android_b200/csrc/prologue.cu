@@ -247,6 +247,33 @@ __global__ void __launch_bounds__(256)
   }
 }
 
+// RoPE on a strided fp32 view [O, S, Hn, D] (D contiguous) into another: t at element
+// offset o*ts[0] + s*ts[1] + h*ts[2], out likewise with os_[].  Same arithmetic as
+// rope_kernel.  Covers the reference's [N, S, D] (O = N, Hn = 1) and predict2's
+// [B, S, H, D] (apply_rotary_pos_emb) without a transpose copy.
+__global__ void __launch_bounds__(256)
+    rope_strided_kernel(const float* t, long long ts0, long long ts1, long long ts2,
+                        const float* f, float* out, long long os0, long long os1, long long os2,
+                        int O, int S, int Hn, int D) {
+  const int half = D / 2;
+  const long long total = (long long)O * S * Hn * half;
+  for (long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x; idx < total;
+       idx += (long long)gridDim.x * blockDim.x) {
+    const int pr = (int)(idx % half);
+    long long r = idx / half;
+    const int h = (int)(r % Hn);
+    r /= Hn;
+    const int s = (int)(r % S);
+    const long long o = r / S;
+    const float* x = t + o * ts0 + s * ts1 + h * ts2;
+    float* y = out + o * os0 + s * os1 + h * os2;
+    const float* fr = f + (long long)s * D * 2 + 4 * pr;
+    const float a = x[pr], c = x[half + pr];
+    y[pr] = __fadd_rn(__fmul_rn(fr[0], a), __fmul_rn(fr[1], c));
+    y[half + pr] = __fadd_rn(__fmul_rn(fr[2], a), __fmul_rn(fr[3], c));
+  }
+}
+
 // ---------------------------------------------------------------- launchers
 static int grid_for(long long warps_needed, int threads, int sm_count) {
   long long blocks = (warps_needed * 32 + threads - 1) / threads;
@@ -336,4 +363,18 @@ int rope_launch(const float* t, const float* f, float* out, int N, int S, int D,
   return cudaGetLastError() == cudaSuccess ? ANIMA_OK : ANIMA_ERR_CUDA;
 }
 
+}  // namespace anima
+
+namespace anima {
+int rope_strided_launch(const float* t, const long long* ts, const float* f, float* out,
+                        const long long* os, int O, int S, int Hn, int D, int sm_count,
+                        cudaStream_t st) {
+  const long long total = (long long)O * S * Hn * (D / 2);
+  if (total == 0) return ANIMA_OK;
+  long long blocks = (total + 255) / 256;
+  if (blocks > (long long)sm_count * 8) blocks = (long long)sm_count * 8;
+  rope_strided_kernel<<<(int)blocks, 256, 0, st>>>(t, ts[0], ts[1], ts[2], f, out, os[0], os[1],
+                                                    os[2], O, S, Hn, D);
+  return cudaGetLastError() == cudaSuccess ? ANIMA_OK : ANIMA_ERR_CUDA;
+}
 }  // namespace anima

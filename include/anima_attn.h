@@ -171,6 +171,16 @@ int anima_attn_schedule(int B, int H, int S_q, int S_kv, unsigned flags, int sm_
  * recorded.  Synchronises `stream`; clears the word when reset != 0. */
 int anima_attn_status(void* stream, int reset);
 
+/* RoPE on device memory, for callers that apply it outside the fused prologue (replaces
+ * predict2.apply_rotary_pos_emb, src/predict2.py:31-38, and the device side of
+ * anima_rt_run_rope, anima_rt/include/cpu/rope_kernel.h:30-62, with the same arithmetic).
+ * t and out are fp32 views [O, S, Hn, D] with element strides {o, s, h} and D contiguous
+ * ([N, S, D]: O = N, Hn = 1; [B, S, H, D]: O = B, Hn = H); freqs [S, D/2, 2, 2] fp32
+ * ([cos, -sin, sin, cos] per pair), pairs (p, D/2 + p).  out may equal t.  Asynchronous on
+ * `stream`. */
+int anima_attn_rope(const float* t, const int64_t t_stride[3], const float* freqs, float* out,
+                    const int64_t out_stride[3], int O, int S, int Hn, int D, void* stream);
+
 /* DiT block helpers around the attention (fused HBM passes; no single reference
  * counterpart, they replace chains of elementwise ops of src/predict2.py:469-583).
  * anima_dit_ln_modulate: y = LayerNorm(x) * (1 + scale[b]) + shift[b] over rows of D = 2048

@@ -10,7 +10,9 @@ import torch.nn.functional as F
 def rope(t, freqs):
     # predict2.apply_rotary_pos_emb on t [B, S, H, D] with freqs [S, D/2, 2, 2]
     f = freqs[None, :, None]
-    t_ = t.reshape(*t.shape[:-1], 2, -1).movedim(-2, -1).unsqueeze(-2).float()
+    t_ = t.reshape(*t.shape[:-1], 2, -1).movedim(-2, -1).unsqueeze(-2)
+    t_ = t_ if t_.dtype == torch.float64 else t_.float()
+    f = f.to(t_.dtype)
     out = f[..., 0] * t_[..., 0] + f[..., 1] * t_[..., 1]
     return out.movedim(-1, -2).reshape(*t.shape)
 

@@ -367,10 +367,11 @@ def test_config3_masked_cross_attention(aa, O):
     _ok(out.cpu().numpy().transpose(0, 2, 1, 3), ref)
 
 
-@pytest.mark.parametrize("L", [4096, 16384])
+@pytest.mark.parametrize("L", [4096, 9216, 16384])
 def test_long_sequence_rows_and_properties(aa, O, L):
-    """Config 5 sizes: sampled query rows against all keys (rows are independent, so
-    the sliced oracle is exact), plus size-independent properties of the full output."""
+    """Config 5 sizes (64x64, 96x96 and 128x128 latent grids): sampled query rows of every
+    (batch, head) against all keys (rows are independent, so the sliced oracle is exact),
+    plus size-independent properties of the full output."""
     side = int(np.sqrt(L))
     rng = np.random.default_rng(L)
     B, H = 2, 16
@@ -383,10 +384,14 @@ def test_long_sequence_rows_and_properties(aa, O, L):
     torch.cuda.synchronize()
     got = out.cpu().numpy()  # [B, L, H, D]
     rq, rk, rv = O.prologue(q, k, v, qw, kw, fr)  # [B, H, L, D]
-    rows = np.sort(rng.choice(L, size=96, replace=False))
-    for (b, h) in [(0, 0), (1, 15), (1, 7)]:
-        ref = O.sdpa(rq[b, h][rows][None], rk[b, h][None], rv[b, h][None])[0]
-        _ok(got[b, rows, h], ref)
+    # 24 rows of each of the 32 (b, h), a fresh sample per head, first and last rows included
+    rows = np.stack([np.sort(np.concatenate([[0, L - 1], rng.choice(np.arange(1, L - 1), 22,
+                                                                     replace=False)]))
+                     for _ in range(B * H)])
+    qs = np.stack([rq[bh // H, bh % H][rows[bh]] for bh in range(B * H)])  # [BH, 24, D]
+    ref = O.sdpa(qs, rk.reshape(B * H, L, 128), rv.reshape(B * H, L, 128), threads=16)
+    sel = np.stack([got[bh // H, rows[bh], bh % H] for bh in range(B * H)])
+    _ok(sel, ref)
     # rows of softmax sum to one: V = 1 gives an all-ones output
     ones = torch.ones_like(dv)
     o1 = aa.attention(dq, dk, ones, _dev(qw), _dev(kw), _dev(fr))
@@ -437,3 +442,79 @@ def test_cta_pair_kernel(aa, O, B, H, Sq, Skv, causal, valid):
     ref = (O.sdpa(q, k, v, causal=causal) if valid is None
            else O.sdpa_varlen(q, k, v, np.array(valid, np.int32)))
     _ok(out.cpu().numpy(), ref)
+
+
+# ------------------------------------------------------------------ RoPE entry, predict2 patch
+def test_apply_rope_device_entry_bit_exact(aa, O):
+    """anima_attn_rope (predict2.apply_rotary_pos_emb on the device) against the restated
+    reference RoPE: bit-exact on [B, S, H, D], on a strided head view and on [N, S, D]."""
+    rng = np.random.default_rng(3)
+    t = rng.standard_normal((2, 64, 6, 128), dtype=np.float32)
+    fr = O.rope_freqs_3d(1, 8, 8)
+    got = aa.apply_rope(_dev(t), _dev(fr))
+    assert np.array_equal(got.cpu().numpy(), O.rope(t, fr))
+    view = _dev(t)[:, :, ::2]  # heads 0, 2, 4: element strides (S*6*D, 6*D, 2*D)
+    got = aa.apply_rope(view, _dev(fr))
+    assert np.array_equal(got.cpu().numpy(), O.rope(np.ascontiguousarray(t[:, :, ::2]), fr))
+    t3 = rng.standard_normal((5, 64, 128), dtype=np.float32)
+    assert np.array_equal(aa.apply_rope(_dev(t3), _dev(fr)).cpu().numpy(), O.rope(t3, fr))
+    tb = _dev(t).to(torch.bfloat16)  # computed in fp32, returned in t's dtype
+    got = aa.apply_rope(tb, _dev(fr))
+    assert got.dtype == torch.bfloat16
+    ref = O.rope(tb.float().cpu().numpy(), fr)
+    assert np.abs(got.float().cpu().numpy() - ref).max() <= 2 ** -7 * np.abs(ref).max()
+
+
+def test_patched_predict2_attention_forward_on_gpu(aa):
+    """The fused Attention.forward that patch_predict2 installs, with the library's GPU
+    backend, on a module with predict2.Attention's attribute surface (the reference module
+    itself is tested on CPU with stand-ins in tests/test_predict2_patch.py), for self- and
+    cross-attention, against the same math in fp64 on the CPU."""
+    import types
+    import torch.nn as nn
+    import torch.nn.functional as F
+    from anima_attn import compat
+    from dit_cpu_attention import rope as cpu_rope
+
+    class Attention(nn.Module):  # predict2.Attention's fields (src/predict2.py:91-160)
+        def __init__(self, dim, ctx_dim, heads, selfattn):
+            super().__init__()
+            self.n_heads, self.head_dim, self.is_selfattn = heads, 128, selfattn
+            inner = heads * 128
+            self.q_proj = nn.Linear(dim, inner, bias=False)
+            self.k_proj = nn.Linear(ctx_dim, inner, bias=False)
+            self.v_proj = nn.Linear(ctx_dim, inner, bias=False)
+            self.q_norm, self.k_norm = nn.RMSNorm(128, eps=1e-6), nn.RMSNorm(128, eps=1e-6)
+            self.output_proj = nn.Linear(inner, dim, bias=False)
+            self.output_dropout = nn.Identity()
+
+        def forward(self, *a, **kw):
+            raise AssertionError("not patched")
+
+    fake = types.SimpleNamespace(_scaled_dot_product_attention=None, apply_rotary_pos_emb=None,
+                                 Attention=Attention)
+    compat.patch_predict2(fake)
+    torch.manual_seed(0)
+    B, S, dim, H = 2, 144, 512, 4
+    fr = torch.from_numpy(aa.rope_freqs_3d(1, 12, 12).cpu().numpy())
+    for selfattn, Skv, cdim in ((True, S, dim), (False, 77, 256)):
+        m = Attention(dim, cdim, H, selfattn)
+        with torch.no_grad():
+            for nrm in (m.q_norm, m.k_norm):
+                nrm.weight.copy_(1 + 0.1 * torch.randn(128))
+        x, ctx = torch.randn(B, S, dim), torch.randn(B, Skv, cdim)
+        rope_emb = fr.reshape(1, S, 1, 64, 2, 2)  # predict2's broadcast shape
+        with torch.no_grad():
+            got = m.cuda()(x.cuda(), None if selfattn else ctx.cuda(), rope_emb=rope_emb.cuda())
+            md = m.double().cpu()
+            src = x.double() if selfattn else ctx.double()
+            q = md.q_proj(x.double()).view(B, S, H, 128)
+            k = md.k_proj(src).view(B, -1, H, 128)
+            v = md.v_proj(src).view(B, -1, H, 128)
+            q = F.rms_norm(q, (128,), md.q_norm.weight, 1e-6)
+            k = F.rms_norm(k, (128,), md.k_norm.weight, 1e-6)
+            if selfattn:
+                q, k = cpu_rope(q, fr.double()).double(), cpu_rope(k, fr.double()).double()
+            o = F.scaled_dot_product_attention(q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2))
+            ref = md.output_proj(o.transpose(1, 2).reshape(B, S, H * 128))
+        _ok(got.double().cpu().numpy(), ref.numpy())
