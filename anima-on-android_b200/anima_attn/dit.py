@@ -351,14 +351,10 @@ class AnimaDiT:
             qkv = self._a2a(self._by_rank_linear(h_loc, self.w[p + ".qkv"]))  # [N, n, 3*hl*hd]
             qkv = qkv.view(B, L, 3, hl, hd)  # rows in global order: source rank r = rows r
             q, k, v = qkv[:, :, 0], qkv[:, :, 1], qkv[:, :, 2]
+            o = self._cross_or_self(p, q, None, freqs, (k, v))
         else:
             q = self._a2a(self._by_rank_linear(h_loc, self.w[p + ".q_by_rank"])).view(B, L, hl, hd)
-            Skv = ctx.shape[1]
-            kv = _linear(ctx, self.w[p + ".kv"], dt).view(B, Skv, 2, hl, hd)
-            k, v = kv[:, :, 0], kv[:, :, 1]
-        with _region("attention"):
-            o = self.attn_fn(q, k, v, self.w[p + ".q_norm.weight"], self.w[p + ".k_norm.weight"],
-                             freqs if ctx is None else None, eps=cfg.eps, out_dtype=dt, op_dtype=dt)
+            o = self._cross_or_self(p, q, ctx, None, None)
         # [B, L, hl, hd] = [N, n, hl*hd] by destination rank -> [N (source heads), n, hl*hd]
         o = self._a2a(o.reshape(N, n, hl * hd))
         o = o.permute(1, 0, 2).reshape(n, N * hl * hd)  # my rows, heads in order
@@ -372,7 +368,7 @@ class AnimaDiT:
         x, h = self._add_ln_rows(x, pending, sc_sa, sh_sa, segs)
         y = self._attention_rows(p + "self_attn", h, B, L, None, freqs)
         x, h = self._add_ln_rows(x, (g_sa, y), sc_ca, sh_ca, segs)
-        y = self._attention_rows(p + "cross_attn", h, B, L, ctx, None)
+        y = self._attention_rows(p + "cross_attn", h, B, L, self._ctx_for(p, ctx), None)
         x, h = self._add_ln_rows(x, (g_ca, y), sc_m, sh_m, segs)
         return x, (g_m, self._mlp(p, h))
 
@@ -397,24 +393,69 @@ class AnimaDiT:
             out = part if out is None else out + part
         return out
 
-    def _attention(self, p: str, x: torch.Tensor, ctx: Optional[torch.Tensor], freqs):
+    def _attention(self, p: str, x: torch.Tensor, ctx, freqs):
+        """ctx: None (self-attention), the context tensor, or this block's entry of a
+        context_cache (cross-attention K/V prepared for the whole sampling run)."""
         cfg = self.cfg
         B, S = x.shape[:2]
-        src = x if ctx is None else ctx
-        Skv = src.shape[1]
         hl, hd, dt = self.h_local, cfg.head_dim, cfg.gemm_dtype
         if ctx is None:
             qkv = _linear(x, self.w[p + ".qkv"], dt).view(B, S, 3, hl, hd)
             q, k, v = qkv[:, :, 0], qkv[:, :, 1], qkv[:, :, 2]
         else:
             q = _linear(x, self.w[p + ".q_proj.weight"], dt).view(B, S, hl, hd)
-            kv = _linear(src, self.w[p + ".kv"], dt).view(B, Skv, 2, hl, hd)
-            k, v = kv[:, :, 0], kv[:, :, 1]
-        with _region("attention"):
-            o = self.attn_fn(q, k, v, self.w[p + ".q_norm.weight"], self.w[p + ".k_norm.weight"],
-                             freqs if ctx is None else None, eps=cfg.eps, out_dtype=cfg.gemm_dtype,
-                             op_dtype=cfg.gemm_dtype)
+        o = self._cross_or_self(p, q, None if ctx is None else ctx, freqs,
+                                (k, v) if ctx is None else None)
         return self._gather_oproj(o, self.w[p + ".output_proj.weight"])
+
+    def _cross_or_self(self, p, q, ctx, freqs, kv):
+        """The attention call of one block: self-attention on (k, v) = kv, or
+        cross-attention on ctx (a context tensor, or a cached entry)."""
+        cfg = self.cfg
+        dt = cfg.gemm_dtype
+        qw, kw = self.w[p + ".q_norm.weight"], self.w[p + ".k_norm.weight"]
+        if ctx is None:
+            k, v = kv
+            with _region("attention"):
+                return self.attn_fn(q, k, v, qw, kw, freqs, eps=cfg.eps, out_dtype=dt, op_dtype=dt)
+        entry = ctx if isinstance(ctx, dict) else self._context_entry(p, ctx)
+        if "kh" in entry:  # operands already in the attention core's layout (GPU)
+            from .ops import attention_cached_kv
+            with _region("attention"):
+                return attention_cached_kv(q, entry["kh"], entry["vh"], qw, eps=cfg.eps,
+                                           out_dtype=dt)
+        with _region("attention"):
+            return self.attn_fn(q, entry["k"], entry["v"], qw, kw, None, eps=cfg.eps,
+                                out_dtype=dt, op_dtype=dt)
+
+    def _context_entry(self, p, ctx, keep_operands=False):
+        """Cross-attention K/V of block prefix p for context ctx [B, N, ctx_dim]: the
+        projection of this rank's heads, and with keep_operands (GPU, library attention)
+        also their k-norm + head-major 16-bit operands, which then replace the K/V side of
+        the prologue in every step."""
+        cfg = self.cfg
+        B, Skv = ctx.shape[:2]
+        kv = _linear(ctx, self.w[p + ".kv"], cfg.gemm_dtype).view(B, Skv, 2, self.h_local,
+                                                                 cfg.head_dim)
+        entry = {"k": kv[:, :, 0], "v": kv[:, :, 1]}
+        if keep_operands:
+            from .ops import prologue
+            _, kh, vh = prologue(None, entry["k"], entry["v"], None, self.w[p + ".k_norm.weight"],
+                                 None, cfg.eps, False, True, cfg.gemm_dtype)
+            entry = {"kh": kh, "vh": vh}
+        return entry
+
+    def context_cache(self, ctx_cond: torch.Tensor, ctx_uncond: torch.Tensor) -> Dict[str, dict]:
+        """Cross-attention K/V of every block for the CFG pair's contexts (stacked [uncond,
+        cond], the order euler_cfg_step uses).  The text context is the same in every step of
+        a sampling run (anima_rt/scripts/sampling.py:127), while the reference projects and
+        normalises its K/V in every step and block (numpy_dit.py:276-286); with the cache a
+        step runs only the query side of each cross-attention."""
+        from .ops import attention as _lib_attention
+        ctx = torch.cat([ctx_uncond, ctx_cond], dim=0).float()
+        keep = ctx.is_cuda and self.attn_fn is _lib_attention
+        return {f"blocks.{b}.cross_attn": self._context_entry(f"blocks.{b}.cross_attn", ctx, keep)
+                for b in range(self.cfg.blocks)}
 
     def _block(self, b: int, x, pending, emb, lora, ctx, freqs):
         """One block on the whole residual stream [B, L, D]; pending as in _block_rows."""
@@ -423,13 +464,19 @@ class AnimaDiT:
         x, h = self._add_ln(x, pending, sc_sa, sh_sa)
         y = self._attention(p + "self_attn", h, None, freqs)
         x, h = self._add_ln(x, (g_sa, y), sc_ca, sh_ca)
-        y = self._attention(p + "cross_attn", h, ctx, None)
+        y = self._attention(p + "cross_attn", h, self._ctx_for(p, ctx), None)
         x, h = self._add_ln(x, (g_ca, y), sc_m, sh_m)
         return x, (g_m, self._mlp(p, h))
 
+    @staticmethod
+    def _ctx_for(p, ctx):
+        """This block's context: the tensor itself, or its entry of a context_cache."""
+        return ctx[p + "cross_attn"] if isinstance(ctx, dict) else ctx
+
     # ------------------------------------------------------------------ forward
-    def forward(self, x: torch.Tensor, timesteps: torch.Tensor, context: torch.Tensor):
-        """x [B, C, T, H, W] latent, timesteps [B], context [B, N, ctx_dim] -> v, x's shape."""
+    def forward(self, x: torch.Tensor, timesteps: torch.Tensor, context):
+        """x [B, C, T, H, W] latent, timesteps [B], context [B, N, ctx_dim] (or the
+        context_cache of that context) -> v, x's shape."""
         cfg, w = self.cfg, self.w
         B, C, T, Hh, Ww = x.shape
         ps, pt = cfg.patch, cfg.patch_t
@@ -446,7 +493,7 @@ class AnimaDiT:
         lora = _linear(F.silu(_linear(sample, w["t_embedder.1.linear_1.weight"])),
                        w["t_embedder.1.linear_2.weight"])
         emb = F.rms_norm(sample, (cfg.hidden,), w["t_embedding_norm.weight"], cfg.eps)
-        ctx = context.float()
+        ctx = context if isinstance(context, dict) else context.float()
         fm = _linear(_linear(F.silu(emb), w["final_layer.adaln_modulation.1.weight"]),
                      w["final_layer.adaln_modulation.2.weight"])
         shift, scale = (fm + lora[:, :, :2 * cfg.hidden]).chunk(2, dim=-1)
@@ -482,14 +529,19 @@ class AnimaDiT:
         out = out.permute(0, 7, 1, 6, 2, 4, 3, 5).reshape(B, cfg.out_channels, T, Hh, Ww)
         return out
 
-    def euler_cfg_step(self, x: torch.Tensor, sigma: float, sigma_next: float,
-                       ctx_cond: torch.Tensor, ctx_uncond: torch.Tensor, cfg_scale: float):
+    def euler_cfg_step(self, x: torch.Tensor, sigma, sigma_next, ctx_cond: torch.Tensor,
+                       ctx_uncond: torch.Tensor, cfg_scale: float, ctx_cache: dict = None):
         """One EulerSampler step (sampling.py:121-138): CFG pair [uncond, cond] in one
         batch, v = v_u + cfg (v_c - v_u), x' = x + v (sigma_next - sigma).
-        x [1, C, H, W] -> [1, C, H, W]."""
+        x [1, C, H, W] -> [1, C, H, W].  sigma / sigma_next are numbers or one-element
+        device tensors (a captured step then serves every step of a schedule);
+        ctx_cache: context_cache(ctx_cond, ctx_uncond), used instead of the contexts."""
         xb = x[:, :, None].expand(2, -1, -1, -1, -1).contiguous()
-        ctx = torch.cat([ctx_uncond, ctx_cond], dim=0)
-        t = torch.full((2,), sigma, dtype=torch.float32, device=x.device)
+        ctx = ctx_cache if ctx_cache is not None else torch.cat([ctx_uncond, ctx_cond], dim=0)
+        if torch.is_tensor(sigma):
+            t = sigma.reshape(1).float().expand(2)
+        else:
+            t = torch.full((2,), sigma, dtype=torch.float32, device=x.device)
         v = self.forward(xb, t, ctx)
         v_cfg = v[0:1] + cfg_scale * (v[1:2] - v[0:1])
         return x + v_cfg[:, :, 0] * (sigma_next - sigma)

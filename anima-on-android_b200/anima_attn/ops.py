@@ -56,22 +56,31 @@ def prologue(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
     contiguous) -> (q, k, v) [B*H, S, D] in ``op_dtype``.  ``norm_q``/``norm_k`` apply
     RMSNorm (weights may be None = 1); ``rope_freqs`` [S, D/2, 2, 2] fp32 rotates q and k.
     Replaces numpy_dit.py:285-291 / predict2.py:182-193.
+    q = None, or k = v = None, runs one side only and returns None for the other (a side
+    whose operands are kept across calls, e.g. the K/V of a constant text context).
     """
+    ref = q if q is not None else k
+    if ref is None or (k is None) != (v is None):
+        raise ValueError("pass q, or k and v, or all three")
     _check_cuda(q, k, v)
-    B, Sq, H, D = q.shape
-    Skv = k.shape[1]
-    if k.shape != (B, Skv, H, D) or v.shape != k.shape:
+    B, _, H, D = ref.shape
+    Sq = 0 if q is None else q.shape[1]
+    Skv = 0 if k is None else k.shape[1]
+    present = [t for t in (q, k, v) if t is not None]
+    if q is not None and q.shape != (B, Sq, H, D):
+        raise ValueError("q must be [B, S_q, H, D]")
+    if k is not None and (k.shape != (B, Skv, H, D) or v.shape != k.shape):
         raise ValueError("k and v must be [B, S_kv, H, D] matching q")
-    if q.dtype not in _TORCH_DT or k.dtype != q.dtype or v.dtype != q.dtype:
+    if ref.dtype not in _TORCH_DT or any(t.dtype != ref.dtype for t in present):
         raise ValueError("q, k, v must share one of float32/bfloat16/float16")
-    for t in (q, k, v):
+    for t in present:
         if t.stride(3) != 1:
             raise ValueError("the head dimension must be contiguous")
-    dev = q.device
+    dev = ref.device
     if out is None:
-        qo = torch.empty((B * H, Sq, D), device=dev, dtype=op_dtype)
-        ko = torch.empty((B * H, Skv, D), device=dev, dtype=op_dtype)
-        vo = torch.empty((B * H, Skv, D), device=dev, dtype=op_dtype)
+        qo = None if q is None else torch.empty((B * H, Sq, D), device=dev, dtype=op_dtype)
+        ko = None if k is None else torch.empty((B * H, Skv, D), device=dev, dtype=op_dtype)
+        vo = None if v is None else torch.empty((B * H, Skv, D), device=dev, dtype=op_dtype)
     else:
         qo, ko, vo = out
     qw, kw = _as_weight(q_norm_w, dev), _as_weight(k_norm_w, dev)
@@ -84,9 +93,9 @@ def prologue(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
         flags |= L.FLAG_ROPE
     a = L.PrologueArgs()
     a.q, a.k, a.v = _ptr(q), _ptr(k), _ptr(v)
-    a.in_dtype = _TORCH_DT[q.dtype]
+    a.in_dtype = _TORCH_DT[ref.dtype]
     for name, t in (("q_stride", q), ("k_stride", k), ("v_stride", v)):
-        getattr(a, name)[:] = [t.stride(0), t.stride(1), t.stride(2)]
+        getattr(a, name)[:] = [0, 0, 0] if t is None else [t.stride(0), t.stride(1), t.stride(2)]
     a.B, a.H, a.S_q, a.S_kv, a.D = B, H, Sq, Skv, D
     a.q_norm_w, a.k_norm_w = _ptr(qw), _ptr(kw)
     a.eps = float(eps)
@@ -206,6 +215,20 @@ def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
     qh, kh, vh = prologue(q, k, v, q_norm_w, k_norm_w, rope_freqs, eps, norm_q, norm_k,
                           op_dtype, out=workspace)
     return attention_core(qh, kh, vh, B, H, scale, kv_valid_len, causal, out=out,
+                          out_layout="bshd", out_dtype=out_dtype)
+
+
+def attention_cached_kv(q: torch.Tensor, kh: torch.Tensor, vh: torch.Tensor,
+                        q_norm_w: Optional[torch.Tensor] = None, norm_q: bool = True,
+                        kv_valid_len: Optional[torch.Tensor] = None, scale: Optional[float] = None,
+                        eps: float = 1e-6, out_dtype=torch.float32,
+                        out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """Cross-attention whose K/V operands were prepared earlier: q [B, S_q, H, D] pre-norm
+    projection -> [B, S_q, H, D].  kh/vh [B*H, S_kv, D] 16-bit head-major, as prologue(None,
+    k, v) returns them.  Runs the q side of the prologue and the attention core only."""
+    B, Sq, H, D = q.shape
+    qh, _, _ = prologue(q, None, None, q_norm_w, None, None, eps, norm_q, False, kh.dtype)
+    return attention_core(qh, kh, vh, B, H, scale, kv_valid_len, False, out=out,
                           out_layout="bshd", out_dtype=out_dtype)
 
 

@@ -292,19 +292,28 @@ static int prologue_t(const PrologueParams& prm, int sm_count, cudaStream_t st) 
 
 int prologue_launch(const AnimaPrologueArgs* a, int sm_count, cudaStream_t st) {
   if (a->D != 128) return ANIMA_ERR_SHAPE;
-  if (a->B <= 0 || a->H <= 0 || a->S_q <= 0 || a->S_kv <= 0) return ANIMA_ERR_SHAPE;
-  if (!a->q || !a->k || !a->v || !a->q_out || !a->k_out || !a->v_out) return ANIMA_ERR_ARG;
+  // S_q == 0 or S_kv == 0 skips that side; its pointers may then be null.
+  if (a->B <= 0 || a->H <= 0 || a->S_q < 0 || a->S_kv < 0 || (a->S_q == 0 && a->S_kv == 0))
+    return ANIMA_ERR_SHAPE;
+  const bool has[3] = {a->S_q > 0, a->S_kv > 0, a->S_kv > 0};
+  if ((has[0] && (!a->q || !a->q_out)) || (has[1] && (!a->k || !a->v || !a->k_out || !a->v_out)))
+    return ANIMA_ERR_ARG;
   if ((a->flags & ANIMA_FLAG_ROPE) && (!a->rope_freqs || a->S_q != a->S_kv))
     return ANIMA_ERR_ARG;
   const int esz = a->in_dtype == ANIMA_DTYPE_F32 ? 4 : 2;
   const int64_t* st3[3] = {a->q_stride, a->k_stride, a->v_stride};
   const void* in3[3] = {a->q, a->k, a->v};
+  void* out3[3] = {a->q_out, a->k_out, a->v_out};
   PrologueParams prm;
   for (int t = 0; t < 3; ++t) {
+    prm.in[t] = nullptr;
+    prm.sb[t] = prm.ss[t] = prm.sh[t] = 0;
+    if (!has[t]) continue;
     const int vec = 16 / esz;  // elements per 16-byte load
     for (int d = 0; d < 3; ++d)
       if (st3[t][d] < 0 || (st3[t][d] % vec) != 0) return ANIMA_ERR_ARG;
     if ((reinterpret_cast<uintptr_t>(in3[t]) & 15u) != 0) return ANIMA_ERR_ARG;
+    if ((reinterpret_cast<uintptr_t>(out3[t]) & 15u) != 0) return ANIMA_ERR_ARG;
     prm.in[t] = in3[t];
     prm.sb[t] = st3[t][0];
     prm.ss[t] = st3[t][1];
@@ -312,9 +321,6 @@ int prologue_launch(const AnimaPrologueArgs* a, int sm_count, cudaStream_t st) {
   }
   if ((reinterpret_cast<uintptr_t>(a->rope_freqs) & 15u) != 0) return ANIMA_ERR_ARG;
   if ((reinterpret_cast<uintptr_t>(a->q_norm_w) & 15u) || (reinterpret_cast<uintptr_t>(a->k_norm_w) & 15u))
-    return ANIMA_ERR_ARG;
-  if ((reinterpret_cast<uintptr_t>(a->q_out) | reinterpret_cast<uintptr_t>(a->k_out) |
-       reinterpret_cast<uintptr_t>(a->v_out)) & 15u)
     return ANIMA_ERR_ARG;
   prm.out[0] = a->q_out;
   prm.out[1] = a->k_out;

@@ -589,7 +589,32 @@ def dit_flops(blocks=28, L=4096, B=2, ctx=512, hidden=2048, mlp=8192, ctx_dim=10
     return blocks * per
 
 
-def dit_step_ms(args, rank, world, local_rank, dist, shard, profile=True):
+def sampler_run(model, x, cc, cu, args, dist, dev, steps):
+    """A whole sampling run (EulerSampler.sample over the z_image schedule) with the
+    cross-attention K/V of every block prepared once per run: the precompute, and the
+    steps replayed from one captured graph, each timed with CUDA events (max over ranks)."""
+    import torch
+    from anima_attn.sampling import EulerCFGSampler, z_image_sigmas
+
+    e = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
+    s = EulerCFGSampler(model, cc, cu, 5.0, x.shape, graph=bool(args.graph))
+    sig = z_image_sigmas(steps)
+    s.sample(x, sig)  # warm
+    _barrier(dist)
+    e[0].record()
+    s.refresh_context(cc, cu)  # the per-run precompute: K/V of every block's cross-attention
+    e[1].record()
+    s.sample(x, sig)
+    e[2].record()
+    torch.cuda.synchronize()
+    pre, run = _max_over_ranks([e[0].elapsed_time(e[1]), e[1].elapsed_time(e[2])], dist, dev)
+    del s
+    return {"steps": steps, "schedule": "z_image (shift 3)", "context_precompute_ms": round(pre, 3),
+            "ms_per_step": round(run / steps, 3), "run_ms": round(pre + run, 3),
+            "cuda_graph": bool(args.graph)}
+
+
+def dit_step_ms(args, rank, world, local_rank, dist, shard, profile=True, sampler_steps=0):
     """One Euler+CFG step of the Anima DiT (config 4): latent 16x128x128 (4096 tokens), 28
     blocks, hidden 2048, 16 heads, CFG pair batched (B=2), sigma 0.5 -> 0, cfg 5; attention
     split by head over the ranks in the given layout.  Returns device ms per step (graph
@@ -662,6 +687,9 @@ def dit_step_ms(args, rank, world, local_rank, dist, shard, profile=True):
             host_step()
         e2e_ms = (time.perf_counter() - t0) / n_e2e * 1e3
         del graph, run_step  # a graph holding NCCL calls goes before the process group
+        sampler = None
+        if sampler_steps:
+            sampler = sampler_run(model, x, cc, cu, args, dist, dev, sampler_steps)
     ms, e2e_ms = _max_over_ranks([ms, e2e_ms], dist, dev)
     Lt = (side // 2) ** 2
     fl = dit_flops(args.blocks, Lt)
@@ -670,7 +698,7 @@ def dit_step_ms(args, rank, world, local_rank, dist, shard, profile=True):
            "e2e_bytes": {"h2d_per_step": (hx.numel() + hcc.numel() + hcu.numel()) * 4,
                          "d2h_per_step": hout.numel() * 4},
            "clocks": clocks.summary(t_begin, t_end), "breakdown_eager": breakdown,
-           "layout": shard if world > 1 else "one GPU"}
+           "layout": shard if world > 1 else "one GPU", "sampler": sampler}
     del model
     torch.cuda.empty_cache()
     return res
@@ -688,8 +716,9 @@ def run_dit_section(args, rank, world, local_rank, dist):
            "data": ("synthetic (seeded latent and context, N(0,0.02) bf16-valued weights)"
                     if not args.weights else
                     f"synthetic latent and context; weights from {os.path.basename(args.weights)}")}
-    for sh in shards:
-        out[sh] = dit_step_ms(args, rank, world, local_rank, dist, sh)
+    for i, sh in enumerate(shards):
+        out[sh] = dit_step_ms(args, rank, world, local_rank, dist, sh,
+                              sampler_steps=args.sampler_steps if i == 0 else 0)
     out["ms"] = out["heads"]["ms"]
     return out
 
@@ -729,6 +758,8 @@ def main():
     ap.add_argument("--blocks", type=int, default=28, help="DiT blocks")
     ap.add_argument("--latent", type=int, default=128, help="DiT latent side")
     ap.add_argument("--dit-steps", type=int, default=10, help="timed DiT steps")
+    ap.add_argument("--sampler-steps", type=int, default=10,
+                    help="DiT: steps of the timed sampling run (0: none)")
     ap.add_argument("--graph", type=int, choices=[0, 1], default=1,
                     help="DiT: replay the step as one captured CUDA graph (1) or issue it op by "
                          "op from Python (0)")

@@ -69,6 +69,9 @@ enum { ANIMA_DTYPE_F32 = 0, ANIMA_DTYPE_BF16 = 1, ANIMA_DTYPE_F16 = 2 };
  * rope_freqs: fp32 [S_q, D/2, 2, 2] table (VideoRopePosition3DEmb layout); with
  * ANIMA_FLAG_ROPE it rotates q and k (requires S_q == S_kv).
  * q_norm_w / k_norm_w: fp32 [D]; NULL means weight 1.
+ * S_q = 0 or S_kv = 0 skips that side (its input and output pointers may be NULL), for
+ * callers that keep one side's operands across calls, such as the cross-attention K/V of
+ * a text context that stays the same over a sampling run.
  */
 typedef struct AnimaPrologueArgs {
   const void* q;
