@@ -723,6 +723,70 @@ def run_dit_section(args, rank, world, local_rank, dist):
     return out
 
 
+# ---------------------------------------------------------------- schedules
+def run_schedules(args):
+    """The attention kernel's three schedules on given shapes (B=2, H=16, bf16 operands, fp32
+    output): ANIMA_FLAG_UNIT (one CTA per 256-row unit), ANIMA_FLAG_WHOLE (persistent grid,
+    whole units), ANIMA_FLAG_SPLIT (persistent grid, last round cut into key-tile slices) and
+    the library's own choice, interleaved over --rounds rounds so clock drift hits all alike;
+    median TFLOP/s of each.  The schedules' outputs are checked against each other first.
+    --kv64 times the 64-key-tile kernel instead of the default."""
+    import torch
+    from anima_attn import _lib as L
+
+    torch.cuda.set_device(0)
+    kf = L.FLAG_KV64 if args.kv64 else 0
+    flags = {"unit": L.FLAG_UNIT, "whole": L.FLAG_WHOLE, "split": L.FLAG_SPLIT, "auto": 0}
+    st = ct.c_void_p(torch.cuda.current_stream().cuda_stream)
+    out_all = {}
+    for shape in args.shapes.split(","):
+        Sq, Skv = (int(x) for x in shape.split(":"))
+        q = torch.randn(B * H, Sq, D, device="cuda", dtype=torch.bfloat16)
+        k, v = (torch.randn(B * H, Skv, D, device="cuda", dtype=torch.bfloat16) for _ in range(2))
+        out = torch.empty(B, Sq, H, D, device="cuda")
+        ws = torch.zeros(max(1, int(L.lib.anima_attn_workspace_size(B, H, Sq, Skv, L.FLAG_SPLIT | kf))),
+                         dtype=torch.uint8, device="cuda")
+
+        def attn_args(f):
+            a = L.AttnArgs()
+            a.q, a.k, a.v = q.data_ptr(), k.data_ptr(), v.data_ptr()
+            a.op_dtype, a.out, a.out_dtype = L.DTYPE_BF16, out.data_ptr(), L.DTYPE_F32
+            a.out_stride[:] = [out.stride(0), out.stride(2), out.stride(1)]
+            a.B, a.H, a.S_q, a.S_kv, a.D = B, H, Sq, Skv, D
+            a.scale, a.flags = 1 / math.sqrt(D), flags[f] | kf
+            a.kv_valid_len = None
+            a.workspace, a.workspace_bytes = ws.data_ptr(), ws.numel()
+            return a
+
+        fl = attn_flops(B, H, Sq, Skv)
+        n = max(5, int(2e12 / fl))
+        res = {f: [] for f in flags}
+        ref = None
+        for r in range(args.rounds):
+            for f in flags:
+                a = attn_args(f)
+                for _ in range(2):
+                    L.check(L.lib.anima_attn_fwd(ct.byref(a), st), "anima_attn_fwd")
+                torch.cuda.synchronize()
+                if r == 0:
+                    if ref is None:
+                        ref = out.clone()
+                    elif (out - ref).abs().max().item() > 2e-2:
+                        raise SystemExit(f"schedule {f} disagrees at {Sq}x{Skv}")
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record()
+                for _ in range(n):
+                    L.lib.anima_attn_fwd(ct.byref(a), st)
+                e1.record()
+                torch.cuda.synchronize()
+                res[f].append(fl / (e0.elapsed_time(e1) / n * 1e-3) / 1e12)
+        sched = {0: "unit", 1: "whole", 2: "cut"}.get(L.lib.anima_attn_schedule(B, H, Sq, Skv, kf, 0))
+        out_all[shape] = {**{f: round(statistics.median(t), 1) for f, t in res.items()},
+                          "auto_runs": sched}
+    return {"workload": "attention schedules, B=2 H=16 bf16 -> fp32, TFLOP/s (median of rounds)",
+            "kernel": "64-key tiles" if args.kv64 else "128-key tiles", "shapes": out_all}
+
+
 # ---------------------------------------------------------------- main
 def reference_line(args, world):
     r = cpu_reference(args.L, args.steps, args.warmup)
@@ -753,8 +817,12 @@ def main():
                     help="N GPUs: heads = the 16 heads split over the ranks (strong scaling); "
                          "replicas = the whole workload on every rank (weak scaling)")
     ap.add_argument("--seed", type=int, default=0)
-    ap.add_argument("--workload", choices=["attn", "dit"], default="attn",
-                    help="attn: the headline line with every section; dit: only the DiT step")
+    ap.add_argument("--workload", choices=["attn", "dit", "schedules"], default="attn",
+                    help="attn: the headline line with every section; dit: only the DiT step; "
+                         "schedules: the attention kernel's schedules on --shapes")
+    ap.add_argument("--shapes", default="4096:4096", help="schedules: SQ:SKV[,SQ:SKV...]")
+    ap.add_argument("--rounds", type=int, default=3, help="schedules: interleaved rounds")
+    ap.add_argument("--kv64", action="store_true", help="schedules: the 64-key-tile kernel")
     ap.add_argument("--blocks", type=int, default=28, help="DiT blocks")
     ap.add_argument("--latent", type=int, default=128, help="DiT latent side")
     ap.add_argument("--dit-steps", type=int, default=10, help="timed DiT steps")
@@ -783,6 +851,10 @@ def main():
             print(json.dumps(reference_line(args, world)))
         return
 
+    if args.workload == "schedules":
+        if rank == 0:
+            print(json.dumps(run_schedules(args)))
+        return
     if args.shard == "heads" and H % world:
         raise SystemExit("heads must divide over ranks")
     # CPU figures first, before any GPU work in this process (rank 0, one GPU only)
