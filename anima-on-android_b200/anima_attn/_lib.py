@@ -44,6 +44,14 @@ class AttnArgs(ct.Structure):
                 ("workspace", _P), ("workspace_bytes", ct.c_uint64)]
 
 
+class QkvProjArgs(ct.Structure):
+    _fields_ = [("x", _P), ("w", _P), ("dtype", ct.c_int), ("B", ct.c_int), ("L", ct.c_int),
+                ("H", ct.c_int), ("K", ct.c_int), ("n_tensors", ct.c_int),
+                ("first_tensor", ct.c_int), ("q_norm_w", _P), ("k_norm_w", _P),
+                ("eps", ct.c_float), ("rope_freqs", _P), ("flags", ct.c_uint), ("q_out", _P),
+                ("k_out", _P), ("v_out", _P)]
+
+
 # Every symbol the headers declare, with its ctypes signature.
 SIGNATURES = {
     # include/anima_rt.h -- argtypes as the reference binds them (anima_rt_ops.py:11-34)
@@ -70,6 +78,7 @@ SIGNATURES = {
     "anima_attn_schedule": ([ct.c_int] * 4 + [ct.c_uint, ct.c_int], ct.c_int),
     "anima_attn_status": ([_P, ct.c_int], ct.c_int),
     "anima_attn_selftest_timeout": ([ct.c_uint, _P], ct.c_int),
+    "anima_qkv_projection": ([ct.POINTER(QkvProjArgs), _P], ct.c_int),
     "anima_attn_rope": ([_P, ct.POINTER(ct.c_int64), _P, _P, ct.POINTER(ct.c_int64), ct.c_int,
                          ct.c_int, ct.c_int, ct.c_int, _P], ct.c_int),
     "anima_dit_ln_modulate": ([_P, _P, _P, ct.c_int64, _P, ct.c_int, ct.c_int64, ct.c_int, ct.c_int,

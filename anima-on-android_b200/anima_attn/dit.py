@@ -189,11 +189,15 @@ class AnimaDiT:
     docstring; both split the attention by head.
     ``attn_fn`` replaces the attention op (signature of anima_attn.attention); tests on
     CPU pass a reference implementation, the product uses the B200 kernels.
+    ``fused_qkv``: with the library attention on CUDA, outside the tokens layout, the q/k/v
+    projections run as anima_qkv_projection (the GEMM with q/k RMSNorm, RoPE and the
+    head-major 16-bit store in its epilogue) followed by the attention core, instead of a
+    cuBLAS GEMM whose output the attention prologue reads back.
     """
 
     def __init__(self, cfg: DiTConfig, weights: Dict[str, torch.Tensor], rank: int = 0,
                  world: int = 1, group=None, attn_fn: Optional[AttnFn] = None,
-                 shard: str = "tokens"):
+                 shard: str = "tokens", fused_qkv: bool = True):
         if cfg.heads % world:
             raise ValueError("heads must divide evenly over ranks")
         if shard not in ("tokens", "heads"):
@@ -231,10 +235,13 @@ class AnimaDiT:
                 self.w[ca + "q_proj.weight"] = self.w[ca + "q_proj.weight"][lo:hi].contiguous()
             ck, cv = (self.w.pop(ca + f"{c}_proj.weight") for c in "kv")
             self.w[ca + "kv"] = torch.cat([ck[lo:hi], cv[lo:hi]]).contiguous()
+        from .ops import attention as _lib_attention
         if attn_fn is None:
-            from .ops import attention as attn_fn
+            attn_fn = _lib_attention
         self.attn_fn = attn_fn
+        self.fused_qkv = bool(fused_qkv) and attn_fn is _lib_attention
         self._freqs_cache = {}
+        self._w32 = {}
 
     # ------------------------------------------------------------------ pieces
     def _rope(self, T, Hp, Wp, device):
@@ -393,12 +400,42 @@ class AnimaDiT:
             out = part if out is None else out + part
         return out
 
+    def _fused(self, x: torch.Tensor) -> bool:
+        """Whether x [B, S, K] can feed anima_qkv_projection (token count a multiple of 32)."""
+        return self.fused_qkv and x.is_cuda and x.shape[1] % 32 == 0
+
+    def _norm32(self, name: str) -> torch.Tensor:
+        """An RMSNorm weight as the fp32 vector the fused kernels read (made once)."""
+        t = self._w32.get(name)
+        if t is None:
+            t = self._w32[name] = self.w[name].float().contiguous()
+        return t
+
     def _attention(self, p: str, x: torch.Tensor, ctx, freqs):
         """ctx: None (self-attention), the context tensor, or this block's entry of a
         context_cache (cross-attention K/V prepared for the whole sampling run)."""
         cfg = self.cfg
         B, S = x.shape[:2]
         hl, hd, dt = self.h_local, cfg.head_dim, cfg.gemm_dtype
+        entry = None
+        if ctx is not None and self._fused(x):
+            entry = ctx if isinstance(ctx, dict) else self._context_entry(p, ctx, True)
+        if self._fused(x) and (ctx is None or "kh" in entry):
+            from .ops import attention_core, qkv_projection
+            x16 = x.to(dt).contiguous()
+            qw = self._norm32(p + ".q_norm.weight")
+            with _region("qkv_fused"):
+                if ctx is None:
+                    qh, kh, vh = qkv_projection(x16, self.w[p + ".qkv"], hl, 3, 0, qw,
+                                                self._norm32(p + ".k_norm.weight"), freqs,
+                                                cfg.eps)
+                else:
+                    qh, _, _ = qkv_projection(x16, self.w[p + ".q_proj.weight"], hl, 1, 0, qw,
+                                              None, None, cfg.eps, True, False)
+                    kh, vh = entry["kh"], entry["vh"]
+            with _region("attention"):
+                o = attention_core(qh, kh, vh, B, hl, out_dtype=dt)
+            return self._gather_oproj(o, self.w[p + ".output_proj.weight"])
         if ctx is None:
             qkv = _linear(x, self.w[p + ".qkv"], dt).view(B, S, 3, hl, hd)
             q, k, v = qkv[:, :, 0], qkv[:, :, 1], qkv[:, :, 2]
@@ -435,6 +472,14 @@ class AnimaDiT:
         the prologue in every step."""
         cfg = self.cfg
         B, Skv = ctx.shape[:2]
+        if keep_operands and self._fused(ctx):
+            from .ops import qkv_projection
+            with _region("qkv_fused"):
+                _, kh, vh = qkv_projection(ctx.to(cfg.gemm_dtype).contiguous(), self.w[p + ".kv"],
+                                           self.h_local, 2, 1, None,
+                                           self._norm32(p + ".k_norm.weight"), None, cfg.eps,
+                                           False, True)
+            return {"kh": kh, "vh": vh}
         kv = _linear(ctx, self.w[p + ".kv"], cfg.gemm_dtype).view(B, Skv, 2, self.h_local,
                                                                  cfg.head_dim)
         entry = {"k": kv[:, :, 0], "v": kv[:, :, 1]}

@@ -22,6 +22,8 @@ import torch
 
 from . import _lib as L
 
+L_ = L
+
 _TORCH_DT = {torch.float32: L.DTYPE_F32, torch.bfloat16: L.DTYPE_BF16, torch.float16: L.DTYPE_F16}
 
 
@@ -249,6 +251,48 @@ def sdpa(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, scale: Optional[floa
     o = attention_core(qh, kh, vh, B, H, scale, None, is_causal, out_layout="bhsd",
                        out_dtype=out_dtype)
     return o if o.dtype == q.dtype else o.to(q.dtype)
+
+
+def qkv_projection(x: torch.Tensor, w: torch.Tensor, H: int, n_tensors: int = 3,
+                   first_tensor: int = 0, q_norm_w: Optional[torch.Tensor] = None,
+                   k_norm_w: Optional[torch.Tensor] = None,
+                   rope_freqs: Optional[torch.Tensor] = None, eps: float = 1e-6,
+                   norm_q: bool = True, norm_k: bool = True):
+    """Projection GEMM with the attention prologue in its epilogue (anima_qkv_projection).
+
+    x [B, L, K] 16-bit contiguous, w [n_tensors*H*128, K] in x's dtype (rows: tensor, head,
+    128; tensors q, k, v from ``first_tensor``).  Returns the attention core's operands
+    (q, k, v) [B*H, L, 128] in x's dtype, None for tensors not computed: q/k RMSNorm over the
+    fp32 accumulator, RoPE on q and k when ``rope_freqs`` [L, 64, 2, 2] is given."""
+    _check_cuda(x, w)
+    B, L, K = x.shape
+    if x.dtype not in (torch.float16, torch.bfloat16) or w.dtype != x.dtype:
+        raise ValueError("x and w must share float16 or bfloat16")
+    if w.shape != (n_tensors * H * 128, K) or not (x.is_contiguous() and w.is_contiguous()):
+        raise ValueError("w must be [n_tensors*H*128, K]; x and w contiguous")
+    outs = [None, None, None]
+    for c in range(first_tensor, first_tensor + n_tensors):
+        outs[c] = torch.empty((B * H, L, 128), device=x.device, dtype=x.dtype)
+    qw, kw = _as_weight(q_norm_w, x.device), _as_weight(k_norm_w, x.device)
+    fr = None
+    flags = (L_.FLAG_QNORM if norm_q else 0) | (L_.FLAG_KNORM if norm_k else 0)
+    if rope_freqs is not None:
+        fr = rope_freqs.detach().to(device=x.device, dtype=torch.float32).reshape(-1).contiguous()
+        if fr.numel() != L * 256:
+            raise ValueError("rope_freqs must hold [L, 64, 2, 2] values")
+        flags |= L_.FLAG_ROPE
+    a = L_.QkvProjArgs()
+    a.x, a.w = _ptr(x), _ptr(w)
+    a.dtype = _TORCH_DT[x.dtype]
+    a.B, a.L, a.H, a.K = B, L, H, K
+    a.n_tensors, a.first_tensor = n_tensors, first_tensor
+    a.q_norm_w, a.k_norm_w = _ptr(qw), _ptr(kw)
+    a.eps = float(eps)
+    a.rope_freqs = _ptr(fr)
+    a.flags = flags
+    a.q_out, a.k_out, a.v_out = (_ptr(t) for t in outs)
+    L_.check(L_.lib.anima_qkv_projection(ct.byref(a), ct.c_void_p(_stream())), "anima_qkv_projection")
+    return tuple(outs)
 
 
 def apply_rope(t: torch.Tensor, freqs: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:

@@ -18,7 +18,7 @@ REPO = os.path.dirname(HERE)
 CSRC = os.path.join(HERE, "csrc")
 OUT = os.path.join(HERE, "anima_attn", "libanima_attn.so")
 SOURCES = ["attn_fwd.cu", "attn_fwd64.cu", "attn_fwd2.cu", "prologue.cu", "dit_ops.cu", "selftest.cu",
-           "rt_ops.cu", "abi.cu"]
+           "rt_ops.cu", "qkv_gemm.cu", "abi.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 

@@ -44,6 +44,7 @@ int rope_strided_launch(const float* t, const long long* ts, const float* f, flo
                         const long long* os, int O, int S, int Hn, int D, int sm_count,
                         cudaStream_t st);
 int act_launch(int which, const float* x, float* y, long long n, int sm_count, cudaStream_t st);
+int qkv_projection_launch(const AnimaQkvProjArgs* a, int* status, int sm_count, cudaStream_t st);
 int layernorm_launch(const float* x, float* y, long long m, int d, float eps, int sm_count,
                      cudaStream_t st);
 int softmax_launch(const float* x, float* y, long long outer, int dim, int sm_count,
@@ -550,6 +551,16 @@ int anima_attn_status(void* stream, int reset) {
   }
   if (reset && code) cudaMemset(d->status, 0, sizeof(int));
   return code;
+}
+
+int anima_qkv_projection(const AnimaQkvProjArgs* a, void* stream) {
+  if (!a) return ANIMA_ERR_ARG;
+  int rc = ANIMA_OK;
+  DeviceState* d = current_device(&rc);
+  if (!d) return rc;
+  rc = qkv_projection_launch(a, d->status, d->sm_count, static_cast<cudaStream_t>(stream));
+  if (rc != ANIMA_OK) set_error(std::string("anima_qkv_projection: ") + code_name(rc));
+  return rc;
 }
 
 int anima_attn_rope(const float* t, const int64_t t_stride[3], const float* freqs, float* out,

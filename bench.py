@@ -614,11 +614,14 @@ def sampler_run(model, x, cc, cu, args, dist, dev, steps):
             "cuda_graph": bool(args.graph)}
 
 
-def dit_step_ms(args, rank, world, local_rank, dist, shard, profile=True, sampler_steps=0):
+def dit_step_ms(args, rank, world, local_rank, dist, shard, profile=True, sampler_steps=0,
+                fused_qkv=True):
     """One Euler+CFG step of the Anima DiT (config 4): latent 16x128x128 (4096 tokens), 28
     blocks, hidden 2048, 16 heads, CFG pair batched (B=2), sigma 0.5 -> 0, cfg 5; attention
-    split by head over the ranks in the given layout.  Returns device ms per step (graph
-    replay, max over ranks), e2e ms through host tensors, clocks and the eager breakdown."""
+    split by head over the ranks in the given layout.  fused_qkv: q/k/v projections through
+    anima_qkv_projection (else cuBLAS GEMMs + the attention prologue).  Returns device ms
+    per step (graph replay, max over ranks), e2e ms through host tensors, clocks and the
+    eager breakdown."""
     import torch
     from anima_attn.dit import AnimaDiT, DiTConfig, StepGraph, make_weights, profile_step
 
@@ -633,7 +636,8 @@ def dit_step_ms(args, rank, world, local_rank, dist, shard, profile=True, sample
         weights = load_dit_weights(args.weights, cfg, device=dev)
     else:
         weights = make_weights(cfg, seed=1234, device=dev, rng_device=dev)
-    model = AnimaDiT(cfg, weights, rank=rank, world=world, group=group, shard=shard)
+    model = AnimaDiT(cfg, weights, rank=rank, world=world, group=group, shard=shard,
+                     fused_qkv=fused_qkv)
     del weights
     side = args.latent
     g = torch.Generator(device=dev).manual_seed(4321)
@@ -698,7 +702,9 @@ def dit_step_ms(args, rank, world, local_rank, dist, shard, profile=True, sample
            "e2e_bytes": {"h2d_per_step": (hx.numel() + hcc.numel() + hcu.numel()) * 4,
                          "d2h_per_step": hout.numel() * 4},
            "clocks": clocks.summary(t_begin, t_end), "breakdown_eager": breakdown,
-           "layout": shard if world > 1 else "one GPU", "sampler": sampler}
+           "layout": shard if world > 1 else "one GPU", "sampler": sampler,
+           "qkv_projection": ("anima_qkv_projection (GEMM + norm/RoPE epilogue)" if model.fused_qkv
+                              else "cuBLAS GEMM + attention prologue")}
     del model
     torch.cuda.empty_cache()
     return res
@@ -719,6 +725,9 @@ def run_dit_section(args, rank, world, local_rank, dist):
     for i, sh in enumerate(shards):
         out[sh] = dit_step_ms(args, rank, world, local_rank, dist, sh,
                               sampler_steps=args.sampler_steps if i == 0 else 0)
+    if world == 1:  # the same step with the projections as cuBLAS GEMMs + the prologue
+        out["heads_cublas_qkv"] = dit_step_ms(args, rank, world, local_rank, dist, "heads",
+                                              fused_qkv=False)
     out["ms"] = out["heads"]["ms"]
     return out
 

@@ -174,6 +174,37 @@ int anima_attn_schedule(int B, int H, int S_q, int S_kv, unsigned flags, int sm_
  * recorded.  Synchronises `stream`; clears the word when reset != 0. */
 int anima_attn_status(void* stream, int reset);
 
+/*
+ * Q/K/V projection with the prologue in its epilogue (tcgen05 GEMM, sm_100a).  Replaces,
+ * in one kernel, the projection GEMMs and the norm / RoPE / transpose passes that follow
+ * them (anima_rt/scripts/numpy_dit.py:276-291; src/predict2.py:174-193):
+ *   C = x W^T (x [B*L, K], W [N, K], both row-major 16-bit, fp32 accumulation); the N
+ *   columns are n_tensors blocks of H heads x 128, tensors in the order q, k, v starting at
+ *   first_tensor.  Per 128-column head block of q and k, RMSNorm over the fp32 accumulator
+ *   (ANIMA_FLAG_QNORM / KNORM; weights [128] fp32, NULL = 1) and RoPE with rope_freqs
+ *   [L, 64, 2, 2] (ANIMA_FLAG_ROPE); v is stored as is.  Outputs: head-major
+ *   [B*H, L, 128] of dtype per tensor (the layout anima_attn_fwd reads), 16-byte aligned.
+ * L must be a multiple of 32 and K of 8.  Asynchronous on `stream`.
+ */
+typedef struct AnimaQkvProjArgs {
+  const void* x;
+  const void* w;
+  int dtype;              /* ANIMA_DTYPE_F16 or BF16: x, w and the outputs */
+  int B, L, H, K;
+  int n_tensors;          /* 1 .. 3 */
+  int first_tensor;       /* 0 = q, 1 = k, 2 = v */
+  const float* q_norm_w;
+  const float* k_norm_w;
+  float eps;
+  const float* rope_freqs;
+  unsigned flags;         /* ANIMA_FLAG_QNORM | ANIMA_FLAG_KNORM | ANIMA_FLAG_ROPE */
+  void* q_out;
+  void* k_out;
+  void* v_out;
+} AnimaQkvProjArgs;
+
+int anima_qkv_projection(const AnimaQkvProjArgs* args, void* stream);
+
 /* RoPE on device memory, for callers that apply it outside the fused prologue (replaces
  * predict2.apply_rotary_pos_emb, src/predict2.py:31-38, and the device side of
  * anima_rt_run_rope, anima_rt/include/cpu/rope_kernel.h:30-62, with the same arithmetic).

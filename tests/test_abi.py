@@ -59,7 +59,8 @@ int main(void) {{ printf("size %zu\\n", sizeof({struct})); {body} return 0; }}""
     return {k: int(v) for k, v in (line.split() for line in out.strip().splitlines())}
 
 
-@pytest.mark.parametrize("cls,cname", [(L.PrologueArgs, "AnimaPrologueArgs"), (L.AttnArgs, "AnimaAttnArgs")])
+@pytest.mark.parametrize("cls,cname", [(L.PrologueArgs, "AnimaPrologueArgs"), (L.AttnArgs, "AnimaAttnArgs"),
+                                       (L.QkvProjArgs, "AnimaQkvProjArgs")])
 def test_struct_layout_matches_header(cls, cname, tmp_path):
     fields = [f for f, _ in cls._fields_]
     c = _c_layout(cname, fields, tmp_path)

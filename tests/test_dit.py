@@ -85,7 +85,10 @@ def test_head_parallel_two_ranks_matches_reference_model_cpu(shard):
 
 @pytest.mark.gpu
 @pytest.mark.parametrize("which", ["small", "full"])
-def test_dit_step_on_gpu_matches_reference_model(which):
+@pytest.mark.parametrize("fused_qkv", [True, False])
+def test_dit_step_on_gpu_matches_reference_model(which, fused_qkv):
+    """fused_qkv: projections through anima_qkv_projection + the attention core (default),
+    or cuBLAS projections + the prologue + the core."""
     from anima_attn.dit import AnimaDiT, DiTConfig, make_weights
     path = os.path.join(GOLDEN, f"dit_{which}.npz")
     if not os.path.exists(path):
@@ -93,12 +96,13 @@ def test_dit_step_on_gpu_matches_reference_model(which):
     g, blocks, wseed, x, cc, cu = _load(which)
     cfg = DiTConfig(blocks=blocks)
     torch.cuda.set_device(0)
-    model = AnimaDiT(cfg, make_weights(cfg, seed=wseed, device="cuda"))
+    model = AnimaDiT(cfg, make_weights(cfg, seed=wseed, device="cuda"), fused_qkv=fused_qkv)
+    assert model.fused_qkv == fused_qkv
     with torch.no_grad():
         out = _step(model, g, x, cc, cu, "cuda").cpu().numpy()
     assert np.isfinite(out).all()
     r = rel_l2(out, g["x_next"])
-    print(f"DiT step {which}: latent rel-L2 {r:.3e}")
+    print(f"DiT step {which} fused_qkv={fused_qkv}: latent rel-L2 {r:.3e}")
     assert r <= LATENT_REL_L2
 
 
