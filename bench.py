@@ -1,7 +1,7 @@
 """Benchmark of the Anima DiT attention hot path on B200.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--L 4096] [--shard heads|replicas] [--workload attn|dit]
+                    [--L 4096] [--shard heads|replicas] [--workload attn|dit|schedules|qkv]
 
 One step = one fused attention call of one DiT block over one synthetic batch: per-head
 q/k RMSNorm + 3D RoPE + bf16 cast (prologue kernel) and the tcgen05 flash attention
@@ -32,6 +32,10 @@ Headline line (rank 0 prints one JSON line):
                 GPUs in the head-parallel layout (and, for N > 1, the token-split layout),
                 with CUDA-event shares of GEMMs, attention, fused passes and collectives in an
                 eager step.
+
+Other workloads (one JSON object each): schedules (the attention kernel's three schedules on
+given shapes) and qkv (anima_qkv_projection, the q/k/v projection GEMM with the prologue in its
+epilogue, against a cuBLAS GEMM followed by the prologue kernel, at the DiT's shapes).
 
 Multi-GPU (torchrun, one process per GPU): "heads" (default) splits the 16 heads over the
 ranks (strong scaling; N=1 is the full problem); "replicas" runs the whole workload on every
@@ -796,6 +800,80 @@ def run_schedules(args):
             "kernel": "64-key tiles" if args.kv64 else "128-key tiles", "shapes": out_all}
 
 
+# ---------------------------------------------------------------- qkv projection
+def run_qkv(args):
+    """anima_qkv_projection (the projection GEMM with q/k RMSNorm, RoPE and the head-major
+    16-bit store in its epilogue) against the path it replaces: a cuBLAS GEMM writing
+    [B, L, n, H, 128] followed by the attention prologue; and the cuBLAS GEMM alone, the
+    tensor-core anchor.  DiT shapes: B=2 (CFG pair), L=--L tokens, K=2048, fp16; --qkv-shapes
+    lists H:n (heads per GPU, tensors: 3 = q/k/v of self-attention, 1 = the cross-attention
+    query).  Median of --steps timed launches, each after a 256 MiB write that flushes L2."""
+    import torch
+    import anima_attn
+    from anima_attn import ops
+
+    torch.cuda.set_device(0)
+    dev, dt, Bq, K = "cuda", torch.float16, 2, 2048
+    L = args.L
+    side = int(math.isqrt(L))
+    if side * side != L:
+        raise SystemExit("qkv: --L must be a square token grid")
+    peak = load_peaks()["tflops"]
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    g = torch.Generator(device=dev).manual_seed(args.seed)
+    freqs = anima_attn.rope_freqs_3d(1, side, side, device=dev)
+
+    def timed(fn):
+        for _ in range(args.warmup):
+            fn()
+        ts = []
+        for _ in range(args.steps):
+            flush.zero_()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            fn()
+            e1.record()
+            torch.cuda.synchronize()
+            ts.append(e0.elapsed_time(e1))
+        return statistics.median(ts)
+
+    out = {}
+    for spec in args.qkv_shapes.split(","):
+        Hh, n = (int(v) for v in spec.split(":"))
+        x = torch.randn(Bq, L, K, device=dev, generator=g).to(dt)
+        w = (0.02 * torch.randn(n * Hh * 128, K, device=dev, generator=g)).to(dt)
+        qw = 1 + 0.1 * torch.randn(128, device=dev, generator=g)
+        kw = 1 + 0.1 * torch.randn(128, device=dev, generator=g)
+        rope = freqs if n == 3 else None
+
+        def fused():
+            return ops.qkv_projection(x, w, Hh, n, 0, qw, kw, rope, 1e-6, True, n == 3)
+
+        def unfused():
+            c = torch.mm(x.view(Bq * L, K), w.t()).view(Bq, L, n, Hh, 128)
+            if n == 3:
+                return ops.prologue(c[:, :, 0], c[:, :, 1], c[:, :, 2], qw, kw, rope, 1e-6,
+                                    True, True, dt)
+            return ops.prologue(c[:, :, 0], None, None, qw, None, None, 1e-6, True, False, dt)
+
+        a, b = fused(), unfused()
+        diff = max(float((u.float() - v.float()).abs().max()) for u, v in zip(a, b)
+                   if u is not None)
+        tf, tu = timed(fused), timed(unfused)
+        tg = timed(lambda: torch.mm(x.view(Bq * L, K), w.t()))
+        fl = 2.0 * Bq * L * K * n * Hh * 128
+        tflops = lambda ms: round(fl / (ms * 1e-3) / 1e12, 1)
+        out[spec] = {"fused_ms": round(tf, 4), "cublas_plus_prologue_ms": round(tu, 4),
+                     "cublas_gemm_ms": round(tg, 4), "fused_tflops": tflops(tf),
+                     "fused_frac_of_measured_peak": round(fl / (tf * 1e-3) / 1e12 / peak, 3),
+                     "cublas_gemm_tflops": tflops(tg), "speedup_vs_unfused": round(tu / tf, 3),
+                     "max_abs_diff_vs_unfused": round(diff, 4)}
+    if anima_attn.status() != 0:
+        raise SystemExit("device-side timeout recorded")
+    return {"workload": f"q/k/v projection + prologue, B={Bq} L={L} K={K} fp16 (DiT shapes)",
+            "peak_bf16_tflops_measured": peak, "shapes": out}
+
+
 # ---------------------------------------------------------------- main
 def reference_line(args, world):
     r = cpu_reference(args.L, args.steps, args.warmup)
@@ -826,9 +904,12 @@ def main():
                     help="N GPUs: heads = the 16 heads split over the ranks (strong scaling); "
                          "replicas = the whole workload on every rank (weak scaling)")
     ap.add_argument("--seed", type=int, default=0)
-    ap.add_argument("--workload", choices=["attn", "dit", "schedules"], default="attn",
+    ap.add_argument("--workload", choices=["attn", "dit", "schedules", "qkv"], default="attn",
                     help="attn: the headline line with every section; dit: only the DiT step; "
-                         "schedules: the attention kernel's schedules on --shapes")
+                         "schedules: the attention kernel's schedules on --shapes; qkv: the "
+                         "fused projection against cuBLAS + prologue on --qkv-shapes")
+    ap.add_argument("--qkv-shapes", default="16:3,4:3,2:3,16:1",
+                    help="qkv: H:n[,H:n...] (heads per GPU, tensors projected)")
     ap.add_argument("--shapes", default="4096:4096", help="schedules: SQ:SKV[,SQ:SKV...]")
     ap.add_argument("--rounds", type=int, default=3, help="schedules: interleaved rounds")
     ap.add_argument("--kv64", action="store_true", help="schedules: the 64-key-tile kernel")
@@ -863,6 +944,10 @@ def main():
     if args.workload == "schedules":
         if rank == 0:
             print(json.dumps(run_schedules(args)))
+        return
+    if args.workload == "qkv":
+        if rank == 0:
+            print(json.dumps(run_qkv(args)))
         return
     if args.shard == "heads" and H % world:
         raise SystemExit("heads must divide over ranks")
