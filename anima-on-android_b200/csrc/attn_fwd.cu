@@ -6,14 +6,16 @@
 //
 // Work unit = 256 query rows (two 128-row tiles) of one (batch, head) against its keys,
 // streamed in 128-key tiles.  Three schedules share one kernel (plan_split chooses):
-//   unit         one CTA per unit (masked / causal calls, at most one wave, and long
-//                units, where the hardware's dynamic hand-out of CTAs balances best);
+//   unit         one CTA per unit (masked / causal calls, calls of at most one wave that
+//                keep most SMs busy, and long units, where the hardware's dynamic hand-out
+//                of CTAs balances best);
 //   whole        a persistent grid of one CTA per SM.  Whole units are dealt round-robin
 //                (CTA c takes units c, c+G, ...), so the CTAs in flight share heads and
 //                their K/V stay in L2, and a CTA moves to its next unit without start-up;
 //   cut          whole-unit rounds as above, and the units of the last, partial round cut
 //                into equal slices of key tiles spread over all CTAs, so that round is not
-//                left half idle.  A CTA holding a slice writes an fp32 partial (O, running
+//                left half idle.  A call of one wave that would leave most SMs idle (a few
+//                heads per GPU) has no whole round: all its units are cut.  A CTA holding a slice writes an fp32 partial (O, running
 //                max, running sum); the last warpgroup to finish a cut unit, told by an
 //                arrival counter, merges the partials and writes the output.  No CTA waits
 //                on another.
@@ -38,6 +40,8 @@
 // Online softmax in the exp2 domain (scores scaled by scale*log2(e)) with a lazy
 // rescale: the max used for P moves only when the new row max exceeds it by more than
 // 8 (a factor 256), so the O correction is rare after the first tiles.
+#include <algorithm>
+
 #include "attn_shared.cuh"
 
 namespace anima {
@@ -549,8 +553,30 @@ static SplitPlan plan_split(int bh, int S_q, int S_kv, unsigned flags, int sm_co
     return sp;  // masked / causal units differ in length: the hardware balances them
   const long long units = (long long)bh * ((S_q + attn::kUnitRows - 1) / attn::kUnitRows);
   const long long n = (S_kv + attn::kBN - 1) / attn::kBN;
-  if (units <= sm_count || units > 0x7fffffffLL) return sp;  // one wave
+  if (units > 0x7fffffffLL) return sp;
   const long long rounds = units / sm_count, tail = units - rounds * sm_count;
+  // Cutting the last round saves the idle share of the unit grid's last wave, (sm - tail)/sm
+  // of one unit's time, and costs segment set-up, partial stores and merges, which do not
+  // grow with the unit's n key tiles.  The cut is the default when the idle share exceeds
+  // 0.15 + 5/n: with B=2, H=16, bf16 that picks the faster schedule at every shape measured
+  // (cut at L = 2560, 3072, 4096, 5120, 6144 and S_q x S_kv = 4096 x 2048; not at 2048,
+  // 8192, 16384, where the idle share is 0.27, 0.08 and 0.16, nor at 4096 x 512 / 1024).
+  const bool worth = (sm_count - tail) * n * 100 > (long long)sm_count * (15 * n + 500);
+  if (units <= sm_count) {
+    // One wave: one CTA per unit, unless most SMs would idle (a few heads per GPU, e.g.
+    // B=2 with 2 heads at L = 4096: 64 units on 148 SMs).  Then every unit is cut into
+    // key-tile slices over all SMs, as the last round of a longer call is.  Here every
+    // unit pays a merge, so the rule compares step counts: cut ~ max(kMinSliceTiles,
+    // units * n / sm) + 5 steps of merge against n for one CTA per unit, taken below 0.9 n.
+    // Measured (B=2, L=4096, TFLOP/s unit -> cut): 2 heads 507 -> 668, 1 head 242 -> 377;
+    // 4 heads 893 = 892 (stays unit); at 1024 tokens (n = 8) the cut lost 3-5 %.
+    const long long cut_steps_x_sm =
+        std::max((long long)attn::kMinSliceTiles * sm_count, units * n) + 5LL * sm_count;
+    const bool one_wave_worth = 10 * cut_steps_x_sm < 9 * n * sm_count;
+    if (units == sm_count || (flags & ANIMA_FLAG_WHOLE) || !allow_cut || !one_wave_worth)
+      return sp;
+    if (2LL * tail * (long long)sizeof(int) > attn::kSemBytes) return sp;
+  }
   // Persistent grid of whole units: a CTA moves from unit to unit without its start-up
   // (TMEM allocation, barrier set-up, the first Q and K loads from DRAM) and with the next
   // unit's K/V already streaming, ~1.5 key-tile steps less overhead per unit than one CTA
@@ -563,17 +589,10 @@ static SplitPlan plan_split(int bh, int S_q, int S_kv, unsigned flags, int sm_co
   whole.mode = kSchedWhole;
   whole.rounds = (int)((units + sm_count - 1) / sm_count);
   if (flags & ANIMA_FLAG_WHOLE) return whole;
-  const SplitPlan nocut = (n <= 32) ? whole : sp;
+  const SplitPlan nocut = (rounds == 0 || n > 32) ? sp : whole;
   if (!allow_cut || tail == 0 || tail * n > 0x7fffffffLL) return nocut;  // whole rounds
   if (2LL * tail * (long long)sizeof(int) > attn::kSemBytes) return nocut;
-  // Cutting the last round saves the idle share of the unit grid's last wave, (sm - tail)/sm
-  // of one unit's time, and costs segment set-up, partial stores and merges, which do not
-  // grow with the unit's n key tiles.  The cut is the default when the idle share exceeds
-  // 0.15 + 5/n: with B=2, H=16, bf16 that picks the faster schedule at every shape measured
-  // (cut at L = 2560, 3072, 4096, 5120, 6144 and S_q x S_kv = 4096 x 2048; not at 2048,
-  // 8192, 16384, where the idle share is 0.27, 0.08 and 0.16, nor at 4096 x 512 / 1024).
-  const bool worth = (sm_count - tail) * n * 100 > (long long)sm_count * (15 * n + 500);
-  if (!(flags & ANIMA_FLAG_SPLIT) && !worth) return nocut;
+  if (rounds > 0 && !(flags & ANIMA_FLAG_SPLIT) && !worth) return nocut;
   sp.mode = kSchedCut;
   sp.rounds = (int)rounds;
   sp.tail_units = (int)tail;

@@ -738,8 +738,8 @@ def run_dit_section(args, rank, world, local_rank, dist):
 
 # ---------------------------------------------------------------- schedules
 def run_schedules(args):
-    """The attention kernel's three schedules on given shapes (B=2, H=16, bf16 operands, fp32
-    output): ANIMA_FLAG_UNIT (one CTA per 256-row unit), ANIMA_FLAG_WHOLE (persistent grid,
+    """The attention kernel's three schedules on given shapes (B=2, H=--sched-heads, bf16
+    operands, fp32 output): ANIMA_FLAG_UNIT (one CTA per 256-row unit), ANIMA_FLAG_WHOLE (persistent grid,
     whole units), ANIMA_FLAG_SPLIT (persistent grid, last round cut into key-tile slices) and
     the library's own choice, interleaved over --rounds rounds so clock drift hits all alike;
     median TFLOP/s of each.  The schedules' outputs are checked against each other first.
@@ -748,6 +748,7 @@ def run_schedules(args):
     from anima_attn import _lib as L
 
     torch.cuda.set_device(0)
+    H = args.sched_heads  # heads per GPU (16 / N under the N-GPU head split)
     kf = L.FLAG_KV64 if args.kv64 else 0
     flags = {"unit": L.FLAG_UNIT, "whole": L.FLAG_WHOLE, "split": L.FLAG_SPLIT, "auto": 0}
     st = ct.c_void_p(torch.cuda.current_stream().cuda_stream)
@@ -796,7 +797,7 @@ def run_schedules(args):
         sched = {0: "unit", 1: "whole", 2: "cut"}.get(L.lib.anima_attn_schedule(B, H, Sq, Skv, kf, 0))
         out_all[shape] = {**{f: round(statistics.median(t), 1) for f, t in res.items()},
                           "auto_runs": sched}
-    return {"workload": "attention schedules, B=2 H=16 bf16 -> fp32, TFLOP/s (median of rounds)",
+    return {"workload": f"attention schedules, B=2 H={H} bf16 -> fp32, TFLOP/s (median of rounds)",
             "kernel": "64-key tiles" if args.kv64 else "128-key tiles", "shapes": out_all}
 
 
@@ -913,6 +914,8 @@ def main():
     ap.add_argument("--shapes", default="4096:4096", help="schedules: SQ:SKV[,SQ:SKV...]")
     ap.add_argument("--rounds", type=int, default=3, help="schedules: interleaved rounds")
     ap.add_argument("--kv64", action="store_true", help="schedules: the 64-key-tile kernel")
+    ap.add_argument("--sched-heads", type=int, default=16,
+                    help="schedules: heads per GPU (16 / N under the N-GPU head split)")
     ap.add_argument("--blocks", type=int, default=28, help="DiT blocks")
     ap.add_argument("--latent", type=int, default=128, help="DiT latent side")
     ap.add_argument("--dit-steps", type=int, default=10, help="timed DiT steps")

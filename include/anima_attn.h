@@ -49,7 +49,10 @@ enum { ANIMA_DTYPE_F32 = 0, ANIMA_DTYPE_BF16 = 1, ANIMA_DTYPE_F16 = 2 };
 #define ANIMA_FLAG_PAIR 0x20u  /* anima_attn_fwd: run on CTA pairs (2-SM MMA), one pair per
                                   512-row unit                             */
 /* Schedule overrides of anima_attn_fwd(_noalloc) for calls that span more than one wave of
- * 256-row units (the library's own choice is described at `workspace` below):            */
+ * 256-row units (the library's own choice is described at `workspace` below).  A call of
+ * one wave runs one CTA per unit, or, when most SMs would idle (e.g. B=2 with 2 heads at
+ * 4096 tokens: 64 units), the cut schedule over all SMs; ANIMA_FLAG_UNIT / WHOLE keep it at
+ * one CTA per unit:                                                                      */
 #define ANIMA_FLAG_SPLIT 0x40u /* persistent grid with the last round cut into key-tile slices
                                   (needs the workspace; anima_attn_workspace_size takes the
                                   same flag)                                               */

@@ -131,6 +131,17 @@ def test_schedule_choice(Sq, Skv, flags, want):
     assert L.lib.anima_attn_schedule(2, 16, Sq, Skv, flags, 148) == SCHED_CODE[want]
 
 
+@pytest.mark.parametrize("H,want", [(16, "cut"), (8, "whole"), (4, "unit"), (2, "cut"), (1, "cut")])
+def test_schedule_choice_by_heads_per_gpu(H, want):
+    """B=2, L=4096 split over 1/2/4/8 GPUs by head: 512, 256, 128, 64 units on 148 SMs.  One
+    wave that would leave most SMs idle (2 heads: 64 units; 1 head: 32) is cut over all SMs;
+    ANIMA_FLAG_UNIT and ANIMA_FLAG_WHOLE keep one CTA per unit there."""
+    assert L.lib.anima_attn_schedule(2, H, 4096, 4096, 0, 148) == SCHED_CODE[want]
+    if H <= 4:
+        assert L.lib.anima_attn_schedule(2, H, 4096, 4096, L.FLAG_UNIT, 148) == SCHED_CODE["unit"]
+        assert L.lib.anima_attn_schedule(2, H, 4096, 4096, L.FLAG_WHOLE, 148) == SCHED_CODE["unit"]
+
+
 def test_schedule_query_rejects_bad_shapes():
     assert L.lib.anima_attn_schedule(0, 16, 4096, 4096, 0, 148) < 0
     assert L.lib.anima_attn_schedule(2, 16, 4096, -1, 0, 148) < 0

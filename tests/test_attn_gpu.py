@@ -249,6 +249,39 @@ def test_schedules_match_each_other_and_oracle(aa, O, Sq, Skv):
     assert rel_l2(s_np, u_np) < ATTN_REL_L2
 
 
+@pytest.mark.parametrize("B,H,Sq,Skv,out", [(2, 2, 4096, 4096, "f32"), (1, 1, 1000, 3000, "f32"),
+                                             (2, 2, 2048, 2048, "bf16"), (2, 1, 2500, 1300, "f16")])
+def test_one_wave_cut_matches_unit_and_oracle(aa, O, B, H, Sq, Skv, out):
+    """Calls of one wave of 256-row units that would leave most of the 148 SMs idle (a few
+    heads per GPU, as the 8-GPU head split gives) run every unit cut into key-tile slices
+    over all SMs, merged in-kernel; ANIMA_FLAG_UNIT keeps one CTA per unit.  Both against
+    the oracle on sampled rows of every (b, h), and against each other.  Ragged shapes put a
+    partial query unit and a partial key tile into slices that span two units."""
+    from anima_attn import _lib as L
+    sm = torch.cuda.get_device_properties(0).multi_processor_count
+    assert L.lib.anima_attn_schedule(B, H, Sq, Skv, 0, sm) == L.SCHED_CUT
+    assert L.lib.anima_attn_schedule(B, H, Sq, Skv, L.FLAG_UNIT, sm) == L.SCHED_UNIT
+    rng = np.random.default_rng(Sq * 7 + Skv + H)
+    q = rng.standard_normal((B * H, Sq, 128), dtype=np.float32)
+    k = rng.standard_normal((B * H, Skv, 128), dtype=np.float32)
+    v = rng.standard_normal((B * H, Skv, 128), dtype=np.float32)
+    tdt = {"f32": torch.float32, "bf16": torch.bfloat16, "f16": torch.float16}[out]
+    qh, kh, vh = (_dev(t).to(torch.bfloat16) for t in (q, k, v))
+    for _ in range(2):  # the second call finds the arrival counters left at zero by the first
+        cut = aa.attention_core(qh, kh, vh, B, H, out_layout="bhsd", out_dtype=tdt)
+    unit = aa.attention_core(qh, kh, vh, B, H, out_layout="bhsd", out_dtype=tdt, schedule="unit")
+    torch.cuda.synchronize()
+    assert aa.status() == 0
+    c_np, u_np = cut.float().cpu().numpy(), unit.float().cpu().numpy()
+    rows = np.unique(np.concatenate([np.arange(0, 16), np.arange(Sq - 16, Sq),
+                                     rng.choice(Sq, size=min(Sq, 96), replace=False)]))
+    ref = O.sdpa(q[:, rows], k, v, threads=8).reshape(B, H, len(rows), 128)
+    rel = ATTN_REL_L2 if out == "f32" else 8e-3  # 16-bit output adds its rounding
+    _ok(c_np[:, :, rows], ref, rel=rel)
+    _ok(u_np[:, :, rows], ref, rel=rel)
+    assert rel_l2(c_np, u_np) < rel
+
+
 KV64_CASES = [  # (B, H, Sq, Skv, causal, masked, schedule, out_dtype)
     (1, 1, 1, 1, False, False, "auto", "f32"), (1, 2, 7, 9, False, False, "auto", "f32"),
     (1, 2, 127, 65, False, False, "auto", "f32"), (2, 3, 300, 1000, False, False, "auto", "bf16"),
