@@ -274,6 +274,137 @@ __global__ void __launch_bounds__(256)
   }
 }
 
+// prologue_tokens_kernel: prologue_kernel's arithmetic for calls with few heads (H at most
+// half of the HB rows a warp loads per batch: 4 for fp32, 8 for 16-bit input, i.e. the head
+// split over 4 or more GPUs).  prologue_kernel's item is one token, so with H = 2 a warp has
+// 2 of its 8 row slots (1 KiB) in flight and the pass is latency-bound (measured: 26.5 us
+// for 37.7 MB at H = 2, 1.4 TB/s).  Here an item is TG = HB / H consecutive tokens of one
+// tensor, so every batch fills its HB rows.  Each pass needs the RoPE row of its own token;
+// those rows are prefetched into L1 with the data loads and read when the pass is processed,
+// so they hold no registers while the loads are in flight.
+template <typename T>
+__device__ __forceinline__ T sel3(const T (&a)[3], int t) {  // no runtime index into params
+  return t == 0 ? a[0] : t == 1 ? a[1] : a[2];
+}
+
+__device__ __forceinline__ void prefetch_l1(const void* p) {
+  asm volatile("prefetch.global.L1 [%0];" ::"l"(p));
+}
+
+template <typename Tin, int kOp>
+__global__ void __launch_bounds__(256, sizeof(Tin) == 4 ? 3 : 2)
+    prologue_tokens_kernel(const PrologueParams p, int TG, long long items_q, long long items_k) {
+  constexpr int E = 16 / (int)sizeof(Tin);
+  constexpr int R = 64 / E;        // lanes per head row
+  constexpr int G = 32 / R;        // head rows per pass
+  constexpr int kPasses = 4;
+  const int lane = threadIdx.x & 31;
+  const int gl = lane % R;
+  const int grp = lane / R;
+  const long long warp0 = ((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const long long nwarps = ((long long)gridDim.x * blockDim.x) >> 5;
+  const long long total = items_q + 2 * items_k;
+
+  for (long long item = warp0; item < total; item += nwarps) {
+    int t;
+    long long it, tokens;
+    if (item < items_q) {
+      t = 0;
+      it = item;
+      tokens = p.tokens_q;
+    } else if (item < items_q + items_k) {
+      t = 1;
+      it = item - items_q;
+      tokens = p.tokens_k;
+    } else {
+      t = 2;
+      it = item - items_q - items_k;
+      tokens = p.tokens_k;
+    }
+    const int S = sel3(p.S, t);
+    const long long sb = sel3(p.sb, t), ss_ = sel3(p.ss, t), sh = sel3(p.sh, t);
+    const long long tok0 = it * TG;
+    const int b0 = (int)(tok0 / S);
+    const int s0 = (int)(tok0 - (long long)b0 * S);
+    const Tin* base = reinterpret_cast<const Tin*>(sel3(p.in, t)) + E * gl;
+    char* dst = reinterpret_cast<char*>(sel3(p.out, t));
+    const bool norm = (p.norm_mask >> t) & 1u;
+    const bool rope = (p.freqs != nullptr) && t < 2;
+
+    uint4 lo[kPasses], hi[kPasses];
+    int rb[kPasses], rs[kPasses], rh[kPasses];
+    bool ok[kPasses];
+#pragma unroll
+    for (int u = 0; u < kPasses; ++u) {
+      int tl = 0, h = G * u + grp;  // this lane group's row of the item: token tl, head h
+      while (h >= p.H) {
+        h -= p.H;
+        ++tl;
+      }
+      int si = s0 + tl, b = b0;
+      while (si >= S) {  // the item's tokens may run into the next sample
+        si -= S;
+        ++b;
+      }
+      rb[u] = b;
+      rs[u] = si;
+      rh[u] = h;
+      ok[u] = tl < TG && tok0 + tl < tokens;
+      if (ok[u]) {
+        const Tin* row = base + (long long)b * sb + (long long)si * ss_ + (long long)h * sh;
+        lo[u] = load16<Tin>(row);
+        hi[u] = load16<Tin>(row + 64);
+        if (rope) prefetch_l1(p.freqs + (long long)si * 256 + 4 * E * gl);
+      } else {  // no row here: defined values for the norm shuffle, nothing stored
+        lo[u] = hi[u] = make_uint4(0u, 0u, 0u, 0u);
+      }
+    }
+    float wl[E], wh[E];
+    {
+      const float* w = t == 0 ? p.w[0] : t == 1 ? p.w[1] : nullptr;
+#pragma unroll
+      for (int e = 0; e < E; e += 4) {
+        const float4 a = (norm && w) ? __ldg(reinterpret_cast<const float4*>(w + E * gl + e))
+                                     : make_float4(1.f, 1.f, 1.f, 1.f);
+        const float4 c = (norm && w) ? __ldg(reinterpret_cast<const float4*>(w + 64 + E * gl + e))
+                                     : make_float4(1.f, 1.f, 1.f, 1.f);
+        wl[e] = a.x; wl[e + 1] = a.y; wl[e + 2] = a.z; wl[e + 3] = a.w;
+        wh[e] = c.x; wh[e + 1] = c.y; wh[e + 2] = c.z; wh[e + 3] = c.w;
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < kPasses; ++u) {
+      float a[E], c[E];
+      widen<Tin>(lo[u], a);
+      widen<Tin>(hi[u], c);
+      if (norm) {
+        float ss = 0.f;
+#pragma unroll
+        for (int e = 0; e < E; ++e) ss += a[e] * a[e] + c[e] * c[e];
+#pragma unroll
+        for (int o = R / 2; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+        const float inv = 1.0f / sqrtf(ss / 128.0f + p.eps);
+        // x * inv * w with both products rounded (the reference's order)
+#pragma unroll
+        for (int e = 0; e < E; ++e) {
+          a[e] = __fmul_rn(__fmul_rn(a[e], inv), wl[e]);
+          c[e] = __fmul_rn(__fmul_rn(c[e], inv), wh[e]);
+        }
+      }
+      if (rope && ok[u]) {
+        const float4* fr = reinterpret_cast<const float4*>(p.freqs + (long long)rs[u] * 256) + E * gl;
+#pragma unroll
+        for (int e = 0; e < E; ++e) rot(a[e], c[e], __ldg(fr + e));
+      }
+      if (ok[u]) {
+        char* orow = dst + ((((long long)rb[u] * p.H + rh[u]) * S + rs[u]) * 128 + E * gl) * 2;
+        store_op<E, kOp>(orow, a);
+        store_op<E, kOp>(orow + 128, c);
+      }
+    }
+  }
+}
+
 // ---------------------------------------------------------------- launchers
 static int grid_for(long long warps_needed, int threads, int sm_count) {
   long long blocks = (warps_needed * 32 + threads - 1) / threads;
@@ -283,8 +414,19 @@ static int grid_for(long long warps_needed, int threads, int sm_count) {
   return (int)blocks;
 }
 
+// Few heads (H <= HB / 2): prologue_tokens_kernel with TG = HB / H tokens per item;
+// otherwise prologue_kernel, one token per item.
 template <typename Tin, int kOp>
 static int prologue_t(const PrologueParams& prm, int sm_count, cudaStream_t st) {
+  constexpr int HB = (32 / (64 / (16 / (int)sizeof(Tin)))) * 4;  // rows per batch: 8 or 16
+  if (2 * prm.H <= HB) {
+    const int TG = HB / prm.H;
+    const long long items_q = (prm.tokens_q + TG - 1) / TG;
+    const long long items_k = (prm.tokens_k + TG - 1) / TG;
+    prologue_tokens_kernel<Tin, kOp><<<grid_for(items_q + 2 * items_k, 256, sm_count), 256, 0, st>>>(
+        prm, TG, items_q, items_k);
+    return cudaGetLastError() == cudaSuccess ? ANIMA_OK : ANIMA_ERR_CUDA;
+  }
   const long long items = prm.tokens_q + 2 * prm.tokens_k;
   prologue_kernel<Tin, kOp><<<grid_for(items, 256, sm_count), 256, 0, st>>>(prm);
   return cudaGetLastError() == cudaSuccess ? ANIMA_OK : ANIMA_ERR_CUDA;

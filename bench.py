@@ -303,20 +303,40 @@ def _max_over_ranks(vals, dist, dev):
     return t.tolist()
 
 
-def _time_events(fn, steps, warmup, dist, dev):
-    """Device time per call of fn (CUDA events on the current stream), max over ranks."""
+_FLUSH = {}
+
+
+def _flush_l2(dev):
+    """Write 256 MiB (twice the 126 MB L2) so the next call starts with a cold L2."""
+    import torch
+    buf = _FLUSH.get(str(dev))
+    if buf is None:
+        buf = _FLUSH[str(dev)] = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    buf.zero_()
+
+
+L2_BYTES = 126e6  # B200 L2; calls whose inputs are smaller flush it between timed calls
+
+
+def _time_events(fn, steps, warmup, dist, dev, flush=True):
+    """Device time per call of fn: CUDA events around each call on the current stream; with
+    flush (inputs smaller than L2) a 256 MiB write before every call, outside the events;
+    mean over calls, max over ranks."""
     import torch
     stream = torch.cuda.current_stream()
     for _ in range(warmup):
         fn()
     _barrier(dist)
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record(stream)
-    for _ in range(steps):
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+           for _ in range(steps)]
+    for e0, e1 in evs:
+        if flush:
+            _flush_l2(dev)
+        e0.record(stream)
         fn()
-    e1.record(stream)
+        e1.record(stream)
     torch.cuda.synchronize()
-    ms = e0.elapsed_time(e1) / steps
+    ms = sum(e0.elapsed_time(e1) for e0, e1 in evs) / steps
     _barrier(dist)
     return _max_over_ranks([ms], dist, dev)[0]
 
@@ -349,6 +369,8 @@ def run_ours(args, rank, world, local_rank, dist):
         if evs is not None:
             evs[2].record(stream)
 
+    in_bytes = 3 * B * L_ * heads * D * 4
+    flush = in_bytes < L2_BYTES
     evs = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(args.steps)]
     clocks = ClockSampler(local_rank)
     with clocks:
@@ -357,13 +379,15 @@ def run_ours(args, rank, world, local_rank, dist):
         _barrier(dist)
         t_begin = time.perf_counter()
         for i in range(args.steps):
+            if flush:
+                _flush_l2(dev)  # outside the step's events: the step starts with a cold L2
             step(evs[i])
         torch.cuda.synchronize()
         t_end = time.perf_counter()
         _barrier(dist)
     if anima_attn.status() != 0:
         raise SystemExit("device status word reports a kernel timeout")
-    total_ms = evs[0][0].elapsed_time(evs[-1][2])
+    total_ms = sum(e[0].elapsed_time(e[2]) for e in evs)
     pro_ms = sum(e[0].elapsed_time(e[1]) for e in evs) / args.steps
     att_ms = sum(e[1].elapsed_time(e[2]) for e in evs) / args.steps
     total_ms, pro_ms, att_ms = _max_over_ranks([total_ms, pro_ms, att_ms], dist, dev)
@@ -431,7 +455,9 @@ def run_ours(args, rank, world, local_rank, dist):
                                f"attention), B={B} H={H} L={L_} D={D}, BASELINE config 5 @ L={L_}",
                    "global_batch": B * (world if args.shard == "replicas" else 1), "seq_len": L_,
                    "heads_per_gpu": heads, "parallelism": f"{args.shard}{world}",
-                   "l2": f"inputs {3 * B * L_ * heads * D * 4 / 2**20:.0f} MiB fp32 > 126 MB L2",
+                   "l2": (f"inputs {in_bytes / 2**20:.0f} MiB fp32 < 126 MB L2: L2 flushed "
+                          "(256 MiB write) before every timed step, outside its events" if flush
+                          else f"inputs {in_bytes / 2**20:.0f} MiB fp32 > 126 MB L2"),
                    "attn_ms": round(att_ms, 4), "prologue_ms": round(pro_ms, 4),
                    "schedule": args.schedule, "schedule_run": sched_run,
                    "prologue_gbs": round(pro_bytes / (pro_ms * 1e-3) / 1e9, 1),
@@ -547,7 +573,8 @@ def run_sweep(args, rank, world, local_rank, dist):
             anima_attn.attention_core(qh, kh, vh, B, heads, out=out)
 
         n = args.steps if Ls < 16384 else max(3, args.steps // 4)
-        ms = _time_events(step, n, args.warmup, dist, dev)
+        ms = _time_events(step, n, args.warmup, dist, dev,
+                          flush=3 * B * Ls * heads * D * 4 < L2_BYTES)
         fl = attn_flops(B, heads, Ls, Ls) * world
         res[str(Ls)] = {"ms": round(ms, 4), "tflops": round(fl / (ms * 1e-3) / 1e12, 1),
                         "pct_of_dense_bf16_peak": round(100 * fl / world / (ms * 1e-3) / 1e12 /
@@ -742,7 +769,7 @@ def run_schedules(args):
     operands, fp32 output): ANIMA_FLAG_UNIT (one CTA per 256-row unit), ANIMA_FLAG_WHOLE (persistent grid,
     whole units), ANIMA_FLAG_SPLIT (persistent grid, last round cut into key-tile slices) and
     the library's own choice, interleaved over --rounds rounds so clock drift hits all alike;
-    median TFLOP/s of each.  The schedules' outputs are checked against each other first.
+    median TFLOP/s of each, every launch timed by its own events after an L2 flush.  The schedules' outputs are checked against each other first.
     --kv64 times the 64-key-tile kernel instead of the default."""
     import torch
     from anima_attn import _lib as L
@@ -773,7 +800,7 @@ def run_schedules(args):
             return a
 
         fl = attn_flops(B, H, Sq, Skv)
-        n = max(5, int(2e12 / fl))
+        n = max(5, min(200, int(2e12 / fl)))
         res = {f: [] for f in flags}
         ref = None
         for r in range(args.rounds):
@@ -787,13 +814,16 @@ def run_schedules(args):
                         ref = out.clone()
                     elif (out - ref).abs().max().item() > 2e-2:
                         raise SystemExit(f"schedule {f} disagrees at {Sq}x{Skv}")
-                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-                e0.record()
-                for _ in range(n):
+                evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+                       for _ in range(n)]
+                for e0, e1 in evs:
+                    _flush_l2("cuda")  # cold L2 for every launch, outside its events
+                    e0.record()
                     L.lib.anima_attn_fwd(ct.byref(a), st)
-                e1.record()
+                    e1.record()
                 torch.cuda.synchronize()
-                res[f].append(fl / (e0.elapsed_time(e1) / n * 1e-3) / 1e12)
+                ms = sum(e0.elapsed_time(e1) for e0, e1 in evs) / n
+                res[f].append(fl / (ms * 1e-3) / 1e12)
         sched = {0: "unit", 1: "whole", 2: "cut"}.get(L.lib.anima_attn_schedule(B, H, Sq, Skv, kf, 0))
         out_all[shape] = {**{f: round(statistics.median(t), 1) for f, t in res.items()},
                           "auto_runs": sched}

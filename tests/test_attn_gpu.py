@@ -199,6 +199,44 @@ def test_prologue_16bit_strided_views(aa, O, in_dtype, H):
         assert np.all(np.abs(g - ref) <= np.abs(ref) * 2.0 ** -10 + 1e-6)
 
 
+@pytest.mark.parametrize("H,grid,in_dtype", [(1, (1, 32, 32), "f32"), (2, (1, 64, 64), "f32"),
+                                             (16, (1, 64, 64), "f32"), (40, (1, 16, 16), "f32"),
+                                             (3, (10, 10, 10), "bf16"), (48, (2, 8, 8), "f16"),
+                                             (64, (2, 8, 8), "f16")])
+def test_prologue_layouts_and_head_counts(aa, O, H, grid, in_dtype):
+    """The prologue over head counts that select each of its two kernels: few heads (fp32
+    H <= 4, 16-bit H <= 8: several tokens per warp item, the head split over 4-16 GPUs) and
+    one token per item otherwise.  Each runs on the usual [B, S, H, D] projection and on a
+    head-major [B, H, S, D] tensor viewed as [B, S, H, D] (head stride S*D): the same bits
+    from both layouts, and the oracle's operand-rounding bound.  S = 1000 with 3 heads (five
+    tokens per item) ends on a partial item and runs items across sample boundaries."""
+    rng = np.random.default_rng(H * 100 + grid[1])
+    B = 2
+    S = grid[0] * grid[1] * grid[2]
+    dt = {"f32": torch.float32, "bf16": torch.bfloat16, "f16": torch.float16}[in_dtype]
+    x = [torch.from_numpy(rng.standard_normal((B, S, H, 128), dtype=np.float32)).to(dt)
+         for _ in range(3)]
+    vals = [t.float().numpy() for t in x]  # the values the kernels read
+    qw = (1 + 0.1 * rng.standard_normal(128)).astype(np.float32)
+    kw = (1 + 0.1 * rng.standard_normal(128)).astype(np.float32)
+    fr = O.rope_freqs_3d(*grid)
+    dense = [t.cuda() for t in x]
+    head_major = [t.permute(0, 2, 1, 3).contiguous().cuda().permute(0, 2, 1, 3) for t in x]
+    if H > 1:  # one head: torch gives the size-1 head axis stride 128
+        assert head_major[0].stride(2) == S * 128 and dense[0].stride(2) == 128
+    a = aa.prologue(*dense, _dev(qw), _dev(kw), _dev(fr), op_dtype=torch.bfloat16)
+    b = aa.prologue(*head_major, _dev(qw), _dev(kw), _dev(fr), op_dtype=torch.bfloat16)
+    torch.cuda.synchronize()
+    assert aa.status() == 0
+    for u, w in zip(a, b):
+        assert torch.equal(u, w)
+    rq, rk, rv = O.prologue(*vals, qw, kw, fr)
+    for got, ref in zip(a, (rq, rk, rv)):
+        g = got.float().cpu().numpy().reshape(ref.shape)
+        # bf16 rounding of the fp32 oracle value: |err| <= 2^-8 |x| (+ tree-sum ulps)
+        assert np.all(np.abs(g - ref) <= np.abs(ref) * 2.0 ** -7 + 1e-6)
+
+
 def test_masked_cross_attention(aa, O):
     rng = np.random.default_rng(21)
     B, H, Sq, Skv = 6, 2, 200, 512
