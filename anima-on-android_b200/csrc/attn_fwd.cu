@@ -41,6 +41,7 @@
 // rescale: the max used for P moves only when the new row max exceeds it by more than
 // 8 (a factor 256), so the O correction is rare after the first tiles.
 #include <algorithm>
+#include <cstring>
 
 #include "attn_shared.cuh"
 
@@ -77,7 +78,8 @@ template <int kOp, int kOut>
 __global__ void __launch_bounds__(kThreads, 1)
     attn_fwd_kernel(const __grid_constant__ CUtensorMap tmap_q,
                     const __grid_constant__ CUtensorMap tmap_k,
-                    const __grid_constant__ CUtensorMap tmap_v, const Params p) {
+                    const __grid_constant__ CUtensorMap tmap_v,
+                    const __grid_constant__ CUtensorMap tmap_o, const Params p) {
   extern __shared__ uint8_t smem_raw[];
   const uint32_t pad = (1024u - (smem_u32(smem_raw) & 1023u)) & 1023u;
   Smem& sm = *reinterpret_cast<Smem*>(smem_raw + pad);
@@ -449,13 +451,15 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (!(ok = __all_sync(0xffffffffu, got))) break;
         tc_fence_after();
       }
-      segment_epilogue<kOut>(p, sg, n, i, row, lane, b, bh, grow, tO, m, l, sm.stage[warp]);
+      segment_epilogue<kOut>(p, sg, n, i, row, lane, b, bh, grow, tO, m, l, sm.stage[warp],
+                             p.tma_out ? &tmap_o : nullptr);
       if (n > 0) {
         tc_fence_before();
         mbar_arrive(&sm.o_empty[i]);
         ++a;
       }
     }
+    if (p.tma_out && lane == 0) bulk_wait_read_all();  // stores done reading shared memory
     tc_fence_before();
     __syncthreads();  // pairs with the control warpgroup's teardown barrier
   }
@@ -518,9 +522,37 @@ static int make_head_map(CUtensorMap* map, const void* base, int op_dtype, int b
   return r == CUDA_SUCCESS ? ANIMA_OK : ANIMA_ERR_CUDA;
 }
 
+// Output [B, S_q, H, 128] addressed by element strides (ob, oh, os) as a TMA tile map for
+// the epilogue's 32 x 32 blocks (box: 32 columns x 32 tokens of one head), axes ordered by
+// stride: (D, H, S, B) when heads are closer than tokens (token-major output), else
+// (D, S, H, B).  Swizzle 128 B (fp32) / 64 B (16-bit), the staging buffer's layout.
+// Returns false when the strides or alignment do not allow a map (then plain stores).
+static bool make_out_map(CUtensorMap* map, const AnimaAttnArgs* a, int* hs) {
+  EncodeTiledFn enc = get_encode_fn();
+  if (!enc) return false;
+  const int esz = a->out_dtype == ANIMA_DTYPE_F32 ? 4 : 2;
+  const long long ob = a->out_stride[0], oh = a->out_stride[1], os = a->out_stride[2];
+  if ((reinterpret_cast<uintptr_t>(a->out) & 15u) != 0 || ob <= 0 || oh <= 0 || os <= 0) return false;
+  if ((ob * esz) % 16 || (oh * esz) % 16 || (os * esz) % 16) return false;
+  const CUtensorMapDataType dt = a->out_dtype == ANIMA_DTYPE_F32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
+                                 : a->out_dtype == ANIMA_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                                                   : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  *hs = oh <= os ? 1 : 0;
+  cuuint64_t dims[4] = {128, (cuuint64_t)(*hs ? a->H : a->S_q), (cuuint64_t)(*hs ? a->S_q : a->H),
+                        (cuuint64_t)a->B};
+  cuuint64_t strides[3] = {(cuuint64_t)((*hs ? oh : os) * esz), (cuuint64_t)((*hs ? os : oh) * esz),
+                           (cuuint64_t)(ob * esz)};
+  cuuint32_t box[4] = {32, (cuuint32_t)(*hs ? 1 : 32), (cuuint32_t)(*hs ? 32 : 1), 1};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  const CUresult r = enc(map, dt, 4, a->out, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                         esz == 4 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B,
+                         CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
 template <int kOp, int kOut>
 static int launch_t(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv,
-                    const attn::Params& prm, int grid, cudaStream_t st) {
+                    const CUtensorMap& mo, const attn::Params& prm, int grid, cudaStream_t st) {
   auto kern = attn::attn_fwd_kernel<kOp, kOut>;
   static int attr_dev_mask = 0;  // devices on which the smem attribute was raised
   int dev = 0;
@@ -531,7 +563,7 @@ static int launch_t(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensor
       return ANIMA_ERR_CUDA;
     attr_dev_mask |= 1 << (dev & 31);
   }
-  kern<<<grid, attn::kThreads, attn::kSmemBytes, st>>>(mq, mk, mv, prm);
+  kern<<<grid, attn::kThreads, attn::kSmemBytes, st>>>(mq, mk, mv, mo, prm);
   return cudaGetLastError() == cudaSuccess ? ANIMA_OK : ANIMA_ERR_CUDA;
 }
 
@@ -664,18 +696,23 @@ int attn_fwd_launch(const AnimaAttnArgs* a, int* status, int sm_count, cudaStrea
   prm.sem = static_cast<int*>(a->workspace);
   prm.part = reinterpret_cast<float*>(static_cast<char*>(a->workspace) + attn::kSemBytes);
   const int grid = prm.split ? sm_count : (int)units;
+  prm.tma_out = 0;
+  prm.tma_hs = 0;
   if (kv64) return attn64_launch(mq, mk, mv, prm, grid, a->op_dtype, a->out_dtype, st);
+  CUtensorMap mo;
+  memset(&mo, 0, sizeof(mo));
+  prm.tma_out = make_out_map(&mo, a, &prm.tma_hs) ? 1 : 0;
   const bool bf = a->op_dtype == ANIMA_DTYPE_BF16;
   switch (a->out_dtype) {
     case ANIMA_DTYPE_F32:
-      return bf ? launch_t<ANIMA_DTYPE_BF16, ANIMA_DTYPE_F32>(mq, mk, mv, prm, grid, st)
-                : launch_t<ANIMA_DTYPE_F16, ANIMA_DTYPE_F32>(mq, mk, mv, prm, grid, st);
+      return bf ? launch_t<ANIMA_DTYPE_BF16, ANIMA_DTYPE_F32>(mq, mk, mv, mo, prm, grid, st)
+                : launch_t<ANIMA_DTYPE_F16, ANIMA_DTYPE_F32>(mq, mk, mv, mo, prm, grid, st);
     case ANIMA_DTYPE_BF16:
-      return bf ? launch_t<ANIMA_DTYPE_BF16, ANIMA_DTYPE_BF16>(mq, mk, mv, prm, grid, st)
-                : launch_t<ANIMA_DTYPE_F16, ANIMA_DTYPE_BF16>(mq, mk, mv, prm, grid, st);
+      return bf ? launch_t<ANIMA_DTYPE_BF16, ANIMA_DTYPE_BF16>(mq, mk, mv, mo, prm, grid, st)
+                : launch_t<ANIMA_DTYPE_F16, ANIMA_DTYPE_BF16>(mq, mk, mv, mo, prm, grid, st);
     default:
-      return bf ? launch_t<ANIMA_DTYPE_BF16, ANIMA_DTYPE_F16>(mq, mk, mv, prm, grid, st)
-                : launch_t<ANIMA_DTYPE_F16, ANIMA_DTYPE_F16>(mq, mk, mv, prm, grid, st);
+      return bf ? launch_t<ANIMA_DTYPE_BF16, ANIMA_DTYPE_F16>(mq, mk, mv, mo, prm, grid, st)
+                : launch_t<ANIMA_DTYPE_F16, ANIMA_DTYPE_F16>(mq, mk, mv, mo, prm, grid, st);
   }
 }
 

@@ -56,6 +56,8 @@ struct Params {
   int tail_ctas;       // CTAs sharing the last round (<= gridDim.x)
   int* sem;            // arrival counters [tail unit][tile], zero between calls
   float* part;         // partial slots [tail_ctas][2][kPartFloats]
+  int tma_out;         // 1: output blocks leave by TMA tensor stores (map passed separately)
+  int tma_hs;          // output map axes (D, H, S, B) (1) or (D, S, H, B) (0)
 };
 
 // Slice of the last round owned by CTA c: key-tile steps [slice_lo(c), slice_lo(c+1)).
@@ -186,23 +188,18 @@ __device__ __forceinline__ bool wg_any(int id, bool v) {
 // reads conflict on banks) and leaves as whole row segments: 4 rows x 128 B per fp32 store
 // instruction, 8 rows x 64 B for 16-bit, instead of 32 scattered 16-byte pieces.  Rows
 // >= nvalid are not written.
+// The warp's 32 x 32 block (lane = row, v = its 32 columns, times inv) into the staging
+// buffer: fp32 rows of 128 B with 16-byte chunks XOR-swizzled by (row & 7), 16-bit rows of
+// 64 B swizzled by ((row >> 1) & 3), so neither this write nor the transposed read conflicts
+// on banks.  These are the 128-byte and 64-byte swizzle layouts of a TMA tile.
 template <int kOut>
-__device__ __forceinline__ void store_block(char* out_w, long long row_bytes, int nvalid,
-                                            const float (&v)[32], int c, float inv,
-                                            float4* stage, int lane) {
+__device__ __forceinline__ void stage_block(const float (&v)[32], float inv, float4* stage,
+                                            int lane) {
   if (kOut == ANIMA_DTYPE_F32) {
 #pragma unroll
     for (int e = 0; e < 8; ++e)
       stage[lane * 8 + (e ^ (lane & 7))] =
           make_float4(v[4 * e] * inv, v[4 * e + 1] * inv, v[4 * e + 2] * inv, v[4 * e + 3] * inv);
-    __syncwarp();
-#pragma unroll
-    for (int k = 0; k < 8; ++k) {
-      const int r = 4 * k + (lane >> 3), q = lane & 7;
-      const float4 x = stage[r * 8 + (q ^ (r & 7))];
-      if (r < nvalid)
-        *reinterpret_cast<float4*>(out_w + r * row_bytes + (c * 32 + q * 4) * 4) = x;
-    }
   } else {
     uint4* st = reinterpret_cast<uint4*>(stage);
 #pragma unroll
@@ -212,7 +209,25 @@ __device__ __forceinline__ void store_block(char* out_w, long long row_bytes, in
           pack2<kOut>(v[8 * e + 2] * inv, v[8 * e + 3] * inv),
           pack2<kOut>(v[8 * e + 4] * inv, v[8 * e + 5] * inv),
           pack2<kOut>(v[8 * e + 6] * inv, v[8 * e + 7] * inv));
-    __syncwarp();
+  }
+}
+
+template <int kOut>
+__device__ __forceinline__ void store_block(char* out_w, long long row_bytes, int nvalid,
+                                            const float (&v)[32], int c, float inv,
+                                            float4* stage, int lane) {
+  stage_block<kOut>(v, inv, stage, lane);
+  __syncwarp();
+  if (kOut == ANIMA_DTYPE_F32) {
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const int r = 4 * k + (lane >> 3), q = lane & 7;
+      const float4 x = stage[r * 8 + (q ^ (r & 7))];
+      if (r < nvalid)
+        *reinterpret_cast<float4*>(out_w + r * row_bytes + (c * 32 + q * 4) * 4) = x;
+    }
+  } else {
+    const uint4* st = reinterpret_cast<const uint4*>(stage);
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
       const int r = 8 * k + (lane >> 2), q = lane & 3;
@@ -223,6 +238,25 @@ __device__ __forceinline__ void store_block(char* out_w, long long row_bytes, in
   __syncwarp();  // the buffer is free for the next block
 }
 
+// Output tile map of a call (om != nullptr): the staged block leaves as one TMA tensor store
+// issued by lane 0, which only waits, before the next block, for the bulk engine to have
+// read the buffer; rows past S_q are clipped by the map.  (x, y, z, w) are the block's map
+// coordinates: column 32c, then the head/token axes in the map's order, then the batch.
+template <int kOut>
+__device__ __forceinline__ void store_block_tma(const CUtensorMap* om, int x, int y, int z, int w,
+                                                const float (&v)[32], float inv, float4* stage,
+                                                int lane) {
+  if (lane == 0) bulk_wait_read_all();  // the previous block's store has read the buffer
+  __syncwarp();
+  stage_block<kOut>(v, inv, stage, lane);
+  fence_proxy_async_smem();  // these generic-proxy writes, before the async-proxy read
+  __syncwarp();
+  if (lane == 0) {
+    tma_store_4d(om, stage, x, y, z, w);
+    bulk_commit_group();
+  }
+}
+
 // Output of one segment of query tile i: O in tensor memory at tO (this warp's lane
 // quarter), m and l the row's running max and sum.  A whole unit is normalised and
 // stored; a slice of a cut unit is stored as an fp32 partial, or merged with the other
@@ -231,7 +265,8 @@ __device__ __forceinline__ void store_block(char* out_w, long long row_bytes, in
 template <int kOut>
 __device__ __forceinline__ void segment_epilogue(const Params& p, const Seg& sg, int n, int i,
                                                  int row, int lane, int b, int bh, int grow,
-                                                 uint32_t tO, float m, float l, float4* stage) {
+                                                 uint32_t tO, float m, float l, float4* stage,
+                                                 const CUtensorMap* om = nullptr) {
   // The warp's first output row, and how many of its 32 rows exist.
   constexpr int kEsize = kOut == ANIMA_DTYPE_F32 ? 4 : 2;
   const long long row_bytes = p.os * kEsize;
@@ -240,6 +275,16 @@ __device__ __forceinline__ void segment_epilogue(const Params& p, const Seg& sg,
                        (long long)(grow - lane) * p.os) *
                           kEsize;
   const int nvalid = p.S_q - (grow - lane);
+  // TMA coordinates of this warp's blocks: (32c, head or token, token or head, batch).
+  const int h_ = bh % p.H, s_ = grow - lane;
+  const int ty = p.tma_hs ? h_ : s_, tz = p.tma_hs ? s_ : h_;
+  auto put = [&](const float (&v)[32], int c, float inv) {
+    if (om != nullptr) {
+      if (nvalid > 0) store_block_tma<kOut>(om, c * 32, ty, tz, b, v, inv, stage, lane);
+    } else {
+      store_block<kOut>(out_w, row_bytes, nvalid, v, c, inv, stage, lane);
+    }
+  };
   if (sg.full) {
     const float inv = (l > 0.f) ? 1.f / l : 0.f;
 #pragma unroll 1
@@ -255,7 +300,7 @@ __device__ __forceinline__ void segment_epilogue(const Params& p, const Seg& sg,
 #pragma unroll
         for (int e = 0; e < 32; ++e) v[e] = 0.f;
       }
-      store_block<kOut>(out_w, row_bytes, nvalid, v, c, inv, stage, lane);
+      put(v, c, inv);
     }
   } else {
     // A slice of a cut unit.  The warpgroup that completes the unit tile's arrival
@@ -340,7 +385,7 @@ __device__ __forceinline__ void segment_epilogue(const Params& p, const Seg& sg,
             v[4 * e + 3] += wc * x[e].w;
           }
         }
-        store_block<kOut>(out_w, row_bytes, nvalid, v, c, 1.f, stage, lane);
+        put(v, c, 1.f);
       }
       if (row == 0) *cnt = 0;  // leave the counter zero for the next call
     }
