@@ -359,8 +359,45 @@ __device__ __forceinline__ void segment_epilogue(const Params& p, const Seg& sg,
       }
       const float inv = den > 0.f ? 1.f / den : 0.f;
       const float w_own = exp2f(m - M) * inv;
-      // Pass 2, 32 columns at a time: own O from tensor memory, every other slice's
-      // quad-major rows (one 512-byte run per warp load).
+      // Pass 2 in tensor memory: the own O scaled in place, then each other slice's partial
+      // added into it with all four 32-column chunks loaded at once (one L2 round trip per
+      // slice, 32 loads in flight, quad-major rows: one 512-byte run per warp load), then the
+      // merged rows stored.
+#pragma unroll 1
+      for (int c = 0; c < 4; ++c) {
+        uint32_t o[32];
+        tmem_ld32(tO + c * 32, o);
+        tmem_ld_wait();
+#pragma unroll
+        for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * w_own);
+        tmem_st32(tO + c * 32, o);
+      }
+      tmem_st_wait();
+#pragma unroll 1
+      for (int k = 0; k < nothers; ++k) {
+        const float* pc = part_of(other(k));
+        const float wc = exp2f(__ldcg(pc + kUnitRows * kD + r) - M) * inv;
+        const float4* src = reinterpret_cast<const float4*>(pc) + r;
+        float4 x[32];
+#pragma unroll
+        for (int j = 0; j < 32; ++j) x[j] = __ldcg(src + j * kUnitRows);
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          uint32_t o[32];
+          tmem_ld32(tO + c * 32, o);
+          tmem_ld_wait();
+#pragma unroll
+          for (int e = 0; e < 8; ++e) {
+            const float4 xe = x[c * 8 + e];
+            o[4 * e] = __float_as_uint(__uint_as_float(o[4 * e]) + wc * xe.x);
+            o[4 * e + 1] = __float_as_uint(__uint_as_float(o[4 * e + 1]) + wc * xe.y);
+            o[4 * e + 2] = __float_as_uint(__uint_as_float(o[4 * e + 2]) + wc * xe.z);
+            o[4 * e + 3] = __float_as_uint(__uint_as_float(o[4 * e + 3]) + wc * xe.w);
+          }
+          tmem_st32(tO + c * 32, o);
+        }
+        tmem_st_wait();
+      }
 #pragma unroll 1
       for (int c = 0; c < 4; ++c) {
         uint32_t o[32];
@@ -368,23 +405,7 @@ __device__ __forceinline__ void segment_epilogue(const Params& p, const Seg& sg,
         tmem_ld_wait();
         float v[32];
 #pragma unroll
-        for (int e = 0; e < 32; ++e) v[e] = __uint_as_float(o[e]) * w_own;
-#pragma unroll 2
-        for (int k = 0; k < nothers; ++k) {
-          const float* pc = part_of(other(k));
-          const float wc = exp2f(__ldcg(pc + kUnitRows * kD + r) - M) * inv;
-          const float4* src = reinterpret_cast<const float4*>(pc) + c * 8 * kUnitRows + r;
-          float4 x[8];
-#pragma unroll
-          for (int e = 0; e < 8; ++e) x[e] = __ldcg(src + e * kUnitRows);
-#pragma unroll
-          for (int e = 0; e < 8; ++e) {
-            v[4 * e] += wc * x[e].x;
-            v[4 * e + 1] += wc * x[e].y;
-            v[4 * e + 2] += wc * x[e].z;
-            v[4 * e + 3] += wc * x[e].w;
-          }
-        }
+        for (int e = 0; e < 32; ++e) v[e] = __uint_as_float(o[e]);
         put(v, c, 1.f);
       }
       if (row == 0) *cnt = 0;  // leave the counter zero for the next call
