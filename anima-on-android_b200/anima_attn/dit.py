@@ -13,8 +13,10 @@ The attention of every block (norm, RoPE, SDPA) runs in this library's kernels, 
 the HBM passes around it: each gated residual update fused with the LayerNorm + adaLN
 modulation + 16-bit cast that follows it (anima_dit_gate_residual_ln_modulate; the first
 LayerNorm of the step alone, anima_dit_ln_modulate) and the exact GELU of the MLP
-(anima_dit_gelu).  GEMMs run in PyTorch (cuBLAS).  The residual stream stays fp32; GEMMs take 16-bit operands with
-fp32 accumulation.  The projections, MLP layers and o-proj write 16-bit output (their
+(anima_dit_gelu).  The q/k/v projections run as this library's projection GEMM with the
+attention prologue in its epilogue (anima_qkv_projection, fused_qkv=True; outside the tokens
+layout); the other GEMMs run in PyTorch (cuBLAS).  The residual stream stays fp32; GEMMs take
+16-bit operands with fp32 accumulation.  The projections, MLP layers and o-proj write 16-bit output (their
 consumers are the attention prologue, GELU, the next GEMM, or the fused residual pass, which
 adds them into the fp32 residual stream); the adaLN and final-layer GEMMs write fp32.
 The operand type is fp16 by default: the weights are bf16 values (exact in fp16 unless
@@ -28,8 +30,9 @@ Multi-GPU (N ranks; the attention is split by heads in both modes, rank r owning
   shard="heads"   the layout specified for this step: every rank holds the whole residual
                   stream, projects q/k/v for its heads only, runs their attention, and one
                   all_gather_into_tensor per attention collects every rank's head outputs
-                  before the o-proj.  o-proj, MLP, adaLN and final layer are replicated, so
-                  only the attention's share of the step shrinks with N.
+                  before the o-proj (one transpose copy to [B, S, hidden], one GEMM).  o-proj,
+                  MLP, adaLN and final layer are replicated, so only the attention's share of
+                  the step shrinks with N.
   shard="tokens"  (default) the same head-parallel attention, with everything else split by
                   tokens (sequence parallelism): rank r owns rows [r*R/N, (r+1)*R/N) of the
                   R = B*L token rows.  It projects q/k/v for all heads on its rows, one
@@ -393,12 +396,11 @@ class AnimaDiT:
         o_local = o_local.contiguous()
         with _region("collective"):
             dist.all_gather_into_tensor(full, o_local, group=self.group)
-        full = full.view((self.world,) + tuple(o_local.shape))
-        out = None
-        for r in range(self.world):
-            part = _linear(full[r].reshape(B, S, cols), w_o[:, r * cols:(r + 1) * cols])
-            out = part if out is None else out + part
-        return out
+        # [world, B, S, H/N, hd] -> [B, S, hidden], rank r's heads at columns r*cols (the
+        # order of w_o's input columns), then one GEMM with K = hidden: one transpose copy
+        # instead of `world` GEMMs of K = cols summed in fp32.
+        full = full.view((self.world,) + tuple(o_local.shape)).permute(1, 2, 0, 3, 4)
+        return _linear(full.reshape(B, S, self.world * cols), w_o, self.cfg.gemm_dtype)
 
     def _fused(self, x: torch.Tensor) -> bool:
         """Whether x [B, S, K] can feed anima_qkv_projection (token count a multiple of 32)."""
