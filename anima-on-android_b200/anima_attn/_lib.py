@@ -18,6 +18,7 @@ DTYPE_F32, DTYPE_BF16, DTYPE_F16 = 0, 1, 2
 FLAG_QNORM, FLAG_KNORM, FLAG_ROPE, FLAG_MASK, FLAG_CAUSAL, FLAG_PAIR = 0x1, 0x2, 0x4, 0x8, 0x10, 0x20
 FLAG_SPLIT, FLAG_UNIT, FLAG_WHOLE, FLAG_KV64 = 0x40, 0x80, 0x100, 0x200
 SCHED_UNIT, SCHED_WHOLE, SCHED_CUT = 0, 1, 2
+IPC_HANDLE_BYTES = 64  # ANIMA_IPC_HANDLE_BYTES
 
 ERR_NAMES = {OK: "ok", ERR_ARG: "bad argument", ERR_SHAPE: "unsupported shape",
              ERR_CUDA: "CUDA error", ERR_TIMEOUT: "device-side wait timed out",
@@ -74,6 +75,10 @@ SIGNATURES = {
     "anima_attn_prologue": ([ct.POINTER(PrologueArgs), _P], ct.c_int),
     "anima_attn_fwd": ([ct.POINTER(AttnArgs), _P], ct.c_int),
     "anima_attn_fwd_noalloc": ([ct.POINTER(AttnArgs), _P], ct.c_int),
+    "anima_attn_fwd_gather": ([ct.POINTER(AttnArgs), ct.POINTER(_P), ct.c_int, _P], ct.c_int),
+    "anima_ipc_export": ([_P, _P, ct.POINTER(ct.c_uint64)], ct.c_int),
+    "anima_ipc_open": ([_P, ct.c_uint64, ct.POINTER(_P)], ct.c_int),
+    "anima_ipc_close": ([_P, ct.c_uint64], ct.c_int),
     "anima_attn_workspace_size": ([ct.c_int] * 4 + [ct.c_uint], ct.c_uint64),
     "anima_attn_schedule": ([ct.c_int] * 4 + [ct.c_uint, ct.c_int], ct.c_int),
     "anima_attn_status": ([_P, ct.c_int], ct.c_int),

@@ -196,11 +196,16 @@ class AnimaDiT:
     projections run as anima_qkv_projection (the GEMM with q/k RMSNorm, RoPE and the
     head-major 16-bit store in its epilogue) followed by the attention core, instead of a
     cuBLAS GEMM whose output the attention prologue reads back.
+    ``peer_gather``: heads layout on N > 1 GPUs with fused_qkv: the attention kernel stores
+    its head outputs into every rank's gather buffer over NVLink (anima_attn_fwd_gather) and a
+    one-element all-reduce orders the ranks, instead of an NCCL all-gather.  The buffers are
+    allocated by a collective call on the first step (every rank, before graph capture);
+    ``close()`` releases the peer mappings (every rank, before the process group goes).
     """
 
     def __init__(self, cfg: DiTConfig, weights: Dict[str, torch.Tensor], rank: int = 0,
                  world: int = 1, group=None, attn_fn: Optional[AttnFn] = None,
-                 shard: str = "tokens", fused_qkv: bool = True):
+                 shard: str = "tokens", fused_qkv: bool = True, peer_gather: bool = True):
         if cfg.heads % world:
             raise ValueError("heads must divide evenly over ranks")
         if shard not in ("tokens", "heads"):
@@ -243,6 +248,11 @@ class AnimaDiT:
             attn_fn = _lib_attention
         self.attn_fn = attn_fn
         self.fused_qkv = bool(fused_qkv) and attn_fn is _lib_attention
+        # heads layout over N > 1 GPUs: the attention stores its head outputs straight into
+        # every rank's gather buffer over NVLink (peer.GatherBuffers), replacing the NCCL
+        # all-gather and the transpose before the o-proj
+        self.peer_gather = bool(peer_gather) and self.fused_qkv and world > 1 and not self.seq
+        self._gather = None
         self._freqs_cache = {}
         self._w32 = {}
 
@@ -402,6 +412,24 @@ class AnimaDiT:
         full = full.view((self.world,) + tuple(o_local.shape)).permute(1, 2, 0, 3, 4)
         return _linear(full.reshape(B, S, self.world * cols), w_o, self.cfg.gemm_dtype)
 
+    def _gather_buffers(self, B: int, S: int, device):
+        """The peer gather buffers for [B, S] tokens (collective on first use and on a shape
+        change: every rank reaches it at the same attention)."""
+        from .peer import GatherBuffers
+        shape = (B, S, self.cfg.heads, self.cfg.head_dim)
+        if self._gather is None or tuple(self._gather.bufs[0].shape) != shape:
+            if self._gather is not None:
+                self._gather.close()
+            self._gather = GatherBuffers(shape, self.cfg.gemm_dtype, device, self.group,
+                                         self.rank, self.world)
+        return self._gather
+
+    def close(self) -> None:
+        """Releases the peer mappings of the gather buffers (heads layout, N > 1)."""
+        if self._gather is not None:
+            self._gather.close()
+            self._gather = None
+
     def _fused(self, x: torch.Tensor) -> bool:
         """Whether x [B, S, K] can feed anima_qkv_projection (token count a multiple of 32)."""
         return self.fused_qkv and x.is_cuda and x.shape[1] % 32 == 0
@@ -435,6 +463,17 @@ class AnimaDiT:
                     qh, _, _ = qkv_projection(x16, self.w[p + ".q_proj.weight"], hl, 1, 0, qw,
                                               None, None, cfg.eps, True, False)
                     kh, vh = entry["kh"], entry["vh"]
+            if self.peer_gather and x.is_cuda:
+                g = self._gather_buffers(B, S, x.device)
+                i = 0 if ctx is None else 1  # self- and cross-attention alternate buffers
+                mine = g.bufs[i][:, :, self.rank * hl:(self.rank + 1) * hl]
+                with _region("attention"):
+                    attention_core(qh, kh, vh, B, hl, out=mine, out_dtype=dt,
+                                   peers=g.destinations(i, self.rank * hl * hd))
+                with _region("collective"):
+                    g.barrier()
+                return _linear(g.bufs[i].view(B, S, cfg.hidden), self.w[p + ".output_proj.weight"],
+                               dt)
             with _region("attention"):
                 o = attention_core(qh, kh, vh, B, hl, out_dtype=dt)
             return self._gather_oproj(o, self.w[p + ".output_proj.weight"])

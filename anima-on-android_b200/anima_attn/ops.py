@@ -132,7 +132,7 @@ def attention_core(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, B: int, H:
                    causal: bool = False, out: Optional[torch.Tensor] = None,
                    out_layout: str = "bshd", out_dtype=torch.float32,
                    schedule: str = "auto", pair: bool = False,
-                   kv64: bool = False) -> torch.Tensor:
+                   kv64: bool = False, peers: Optional[list] = None) -> torch.Tensor:
     """tcgen05 flash attention on 16-bit head-major operands.
 
     q [B*H, S_q, 128], k/v [B*H, S_kv, 128] contiguous bf16/fp16.  Returns (or fills)
@@ -145,6 +145,9 @@ def attention_core(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, B: int, H:
     ``pair`` runs the CTA-pair kernel (2-SM MMA, one pair per 512-row unit).
     ``kv64`` runs the 64-key-tile kernel, whose P has tensor-memory columns of its own so a
     query tile's next QK^T overlaps its softmax.
+    ``peers``: device addresses (one per rank, this rank's included) that each receive every
+    output block, with ``out``'s strides and dtype (anima_attn_fwd_gather): the all-gather
+    of head outputs done by the epilogue; ``out`` is then this rank's own destination.
     """
     _check_cuda(q, k, v)
     BH, Sq, D = q.shape
@@ -194,7 +197,12 @@ def attention_core(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, B: int, H:
         ws = _workspace(q.device, int(L.lib.anima_attn_workspace_size(B, H, Sq, Skv, flags)))
     a.workspace = _ptr(ws)
     a.workspace_bytes = 0 if ws is None else ws.numel()
-    L.check(L.lib.anima_attn_fwd(ct.byref(a), ct.c_void_p(_stream())), "anima_attn_fwd")
+    if peers:
+        arr = (ct.c_void_p * len(peers))(*peers)
+        L.check(L.lib.anima_attn_fwd_gather(ct.byref(a), arr, len(peers), ct.c_void_p(_stream())),
+                "anima_attn_fwd_gather")
+    else:
+        L.check(L.lib.anima_attn_fwd(ct.byref(a), ct.c_void_p(_stream())), "anima_attn_fwd")
     return out
 
 

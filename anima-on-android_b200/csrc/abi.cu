@@ -8,6 +8,7 @@
 //    kernels on the library's stream, copies the result back and synchronises.
 //    Calls are serialised by one mutex (one workspace); like the reference they are
 //    safe to call from several threads.
+#include <cstring>
 #include <initializer_list>
 #include <mutex>
 #include <string>
@@ -16,7 +17,8 @@
 #include "common.cuh"
 
 namespace anima {
-int attn_fwd_launch(const AnimaAttnArgs* a, int* status, int sm_count, cudaStream_t st);
+int attn_fwd_launch(const AnimaAttnArgs* a, int* status, int sm_count, cudaStream_t st,
+                    void* const* peers = nullptr, int n_peers = 0);
 int attn_fwd_pair_launch(const AnimaAttnArgs* a, int* status, cudaStream_t st);
 size_t attn_workspace_bytes(int B, int H, int S_q, int S_kv, unsigned flags, int sm_count);
 int attn_schedule_mode(int B, int H, int S_q, int S_kv, unsigned flags, int sm_count);
@@ -514,6 +516,93 @@ int anima_attn_fwd_noalloc(const AnimaAttnArgs* a, void* stream) {
   if (rc != ANIMA_OK)
     set_error(std::string("anima_attn_fwd_noalloc: ") + (why ? why : code_name(rc)));
   return rc;
+}
+
+int anima_attn_fwd_gather(const AnimaAttnArgs* a, void* const* peer_out, int n_peers,
+                          void* stream) {
+  if (!a || !peer_out || n_peers < 1 || n_peers > 8) return ANIMA_ERR_ARG;
+  if (a->flags & ANIMA_FLAG_PAIR) return ANIMA_ERR_ARG;  // the CTA-pair kernel stores locally
+  for (int i = 0; i < n_peers; ++i)
+    if (!peer_out[i] || (reinterpret_cast<uintptr_t>(peer_out[i]) & 15u)) return ANIMA_ERR_ARG;
+  AnimaAttnArgs b = *a;
+  b.out = peer_out[0];  // strides and dtype of every destination; the launch stores to all
+  if (!b.q || !b.k || !b.v) return ANIMA_ERR_ARG;
+  if ((b.flags & ANIMA_FLAG_MASK) && !b.kv_valid_len) return ANIMA_ERR_ARG;
+  const int oe = b.out_dtype == ANIMA_DTYPE_F32 ? 4 : 8;
+  for (int i = 0; i < 3; ++i)
+    if (b.out_stride[i] < 0 || b.out_stride[i] % oe) return ANIMA_ERR_ARG;
+  const uintptr_t al = reinterpret_cast<uintptr_t>(b.q) | reinterpret_cast<uintptr_t>(b.k) |
+                       reinterpret_cast<uintptr_t>(b.v);
+  if (al & 15u) return ANIMA_ERR_ARG;
+  int rc = ANIMA_OK;
+  DeviceState* d = current_device(&rc);
+  if (!d) return rc;
+  rc = attn_fwd_launch(&b, d->status, d->sm_count, static_cast<cudaStream_t>(stream), peer_out,
+                       n_peers);
+  if (rc != ANIMA_OK) set_error(std::string("anima_attn_fwd_gather: ") + code_name(rc));
+  return rc;
+}
+
+// ---------------------------------------------------------------- peer buffers (CUDA IPC)
+typedef CUresult (*AddressRangeFn)(CUdeviceptr*, size_t*, CUdeviceptr);
+
+static AddressRangeFn address_range_fn() {
+  static AddressRangeFn fn = nullptr;
+  if (!fn) {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuMemGetAddressRange", &ptr, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<AddressRangeFn>(ptr);
+  }
+  return fn;
+}
+
+int anima_ipc_export(const void* ptr, void* handle, uint64_t* offset) {
+  if (!ptr || !handle || !offset) return ANIMA_ERR_ARG;
+  AddressRangeFn range = address_range_fn();
+  if (!range) {
+    set_error("anima_ipc_export: cuMemGetAddressRange unavailable");
+    return ANIMA_ERR_CUDA;
+  }
+  CUdeviceptr base = 0;
+  size_t size = 0;
+  if (range(&base, &size, reinterpret_cast<CUdeviceptr>(ptr)) != CUDA_SUCCESS) {
+    set_error("anima_ipc_export: pointer is not device memory of this process");
+    return ANIMA_ERR_ARG;
+  }
+  cudaIpcMemHandle_t h;
+  if (cudaIpcGetMemHandle(&h, reinterpret_cast<void*>(base)) != cudaSuccess) {
+    set_error(std::string("anima_ipc_export: ") + cudaGetErrorString(cudaGetLastError()));
+    return ANIMA_ERR_CUDA;
+  }
+  static_assert(sizeof(cudaIpcMemHandle_t) == ANIMA_IPC_HANDLE_BYTES, "IPC handle size");
+  memcpy(handle, &h, sizeof(h));
+  *offset = reinterpret_cast<uintptr_t>(ptr) - static_cast<uintptr_t>(base);
+  return ANIMA_OK;
+}
+
+int anima_ipc_open(const void* handle, uint64_t offset, void** ptr) {
+  if (!handle || !ptr) return ANIMA_ERR_ARG;
+  cudaIpcMemHandle_t h;
+  memcpy(&h, handle, sizeof(h));
+  void* base = nullptr;
+  if (cudaIpcOpenMemHandle(&base, h, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) {
+    set_error(std::string("anima_ipc_open: ") + cudaGetErrorString(cudaGetLastError()));
+    return ANIMA_ERR_CUDA;
+  }
+  *ptr = static_cast<char*>(base) + offset;
+  return ANIMA_OK;
+}
+
+int anima_ipc_close(void* ptr, uint64_t offset) {
+  if (!ptr) return ANIMA_ERR_ARG;
+  if (cudaIpcCloseMemHandle(static_cast<char*>(ptr) - offset) != cudaSuccess) {
+    set_error(std::string("anima_ipc_close: ") + cudaGetErrorString(cudaGetLastError()));
+    return ANIMA_ERR_CUDA;
+  }
+  return ANIMA_OK;
 }
 
 uint64_t anima_attn_workspace_size(int B, int H, int S_q, int S_kv, unsigned flags) {

@@ -650,7 +650,8 @@ int attn_schedule_mode(int B, int H, int S_q, int S_kv, unsigned flags, int sm_c
   return plan_split(B * H, S_q, S_kv, flags, sm_count).mode;
 }
 
-int attn_fwd_launch(const AnimaAttnArgs* a, int* status, int sm_count, cudaStream_t st) {
+int attn_fwd_launch(const AnimaAttnArgs* a, int* status, int sm_count, cudaStream_t st,
+                    void* const* peers, int n_peers) {
   if (a->D != attn::kD) return ANIMA_ERR_SHAPE;
   if (a->op_dtype != ANIMA_DTYPE_BF16 && a->op_dtype != ANIMA_DTYPE_F16) return ANIMA_ERR_ARG;
   if (a->out_dtype != ANIMA_DTYPE_F32 && a->out_dtype != ANIMA_DTYPE_BF16 &&
@@ -698,10 +699,12 @@ int attn_fwd_launch(const AnimaAttnArgs* a, int* status, int sm_count, cudaStrea
   const int grid = prm.split ? sm_count : (int)units;
   prm.tma_out = 0;
   prm.tma_hs = 0;
+  prm.n_peers = n_peers;
+  for (int i = 0; i < attn::kMaxPeers; ++i) prm.peer_out[i] = i < n_peers ? peers[i] : nullptr;
   if (kv64) return attn64_launch(mq, mk, mv, prm, grid, a->op_dtype, a->out_dtype, st);
   CUtensorMap mo;
   memset(&mo, 0, sizeof(mo));
-  prm.tma_out = make_out_map(&mo, a, &prm.tma_hs) ? 1 : 0;
+  prm.tma_out = n_peers == 0 && make_out_map(&mo, a, &prm.tma_hs) ? 1 : 0;
   const bool bf = a->op_dtype == ANIMA_DTYPE_BF16;
   switch (a->out_dtype) {
     case ANIMA_DTYPE_F32:
@@ -739,7 +742,7 @@ int attn_fwd_launch_noalloc(const AnimaAttnArgs* a, int* status, int sm_count, v
   AnimaAttnArgs b = *a;
   b.workspace = scratch;
   b.workspace_bytes = attn::kNoAllocScratchBytes;
-  return attn_fwd_launch(&b, status, sm_count, st);
+  return attn_fwd_launch(&b, status, sm_count, st, nullptr, 0);
 }
 
 }  // namespace anima

@@ -38,6 +38,8 @@ constexpr int kPartFloats = kUnitRows * kD + 2 * kUnitRows;
 constexpr int kSemBytes = 4096;         // arrival counters at the start of the workspace
 
 
+constexpr int kMaxPeers = 8;  // output destinations of one call (ranks of one NVLink domain)
+
 struct Params {
   int B, H, S_q, S_kv;
   float scale_log2;
@@ -58,6 +60,8 @@ struct Params {
   float* part;         // partial slots [tail_ctas][2][kPartFloats]
   int tma_out;         // 1: output blocks leave by TMA tensor stores (map passed separately)
   int tma_hs;          // output map axes (D, H, S, B) (1) or (D, S, H, B) (0)
+  int n_peers;         // > 0: every output block goes to each peer_out base (same strides)
+  void* peer_out[kMaxPeers];
 };
 
 // Slice of the last round owned by CTA c: key-tile steps [slice_lo(c), slice_lo(c+1)).
@@ -238,6 +242,43 @@ __device__ __forceinline__ void store_block(char* out_w, long long row_bytes, in
   __syncwarp();  // the buffer is free for the next block
 }
 
+// The warp's 32 x 32 block, staged once, stored to every destination base p.peer_out[0 ..
+// n_peers) at byte offset `off` (+ row r * row_bytes + column): the all-gather of the head
+// outputs over NVLink, folded into the epilogue (the other ranks' bases are peer mappings).
+template <int kOut>
+__device__ __forceinline__ void store_block_peers(const Params& p, long long off,
+                                                  long long row_bytes, int nvalid,
+                                                  const float (&v)[32], int c, float inv,
+                                                  float4* stage, int lane) {
+  stage_block<kOut>(v, inv, stage, lane);
+  __syncwarp();
+  if (kOut == ANIMA_DTYPE_F32) {
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const int r = 4 * k + (lane >> 3), q = lane & 7;
+      const float4 x = stage[r * 8 + (q ^ (r & 7))];
+      const long long o = off + r * row_bytes + (c * 32 + q * 4) * 4;
+#pragma unroll
+      for (int i = 0; i < kMaxPeers; ++i)
+        if (i < p.n_peers && r < nvalid)
+          *reinterpret_cast<float4*>(static_cast<char*>(p.peer_out[i]) + o) = x;
+    }
+  } else {
+    const uint4* st = reinterpret_cast<const uint4*>(stage);
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const int r = 8 * k + (lane >> 2), q = lane & 3;
+      const uint4 x = st[r * 4 + (q ^ ((r >> 1) & 3))];
+      const long long o = off + r * row_bytes + (c * 32 + q * 8) * 2;
+#pragma unroll
+      for (int i = 0; i < kMaxPeers; ++i)
+        if (i < p.n_peers && r < nvalid)
+          *reinterpret_cast<uint4*>(static_cast<char*>(p.peer_out[i]) + o) = x;
+    }
+  }
+  __syncwarp();  // the buffer is free for the next block
+}
+
 // Output tile map of a call (om != nullptr): the staged block leaves as one TMA tensor store
 // issued by lane 0, which only waits, before the next block, for the bulk engine to have
 // read the buffer; rows past S_q are clipped by the map.  (x, y, z, w) are the block's map
@@ -278,8 +319,12 @@ __device__ __forceinline__ void segment_epilogue(const Params& p, const Seg& sg,
   // TMA coordinates of this warp's blocks: (32c, head or token, token or head, batch).
   const int h_ = bh % p.H, s_ = grow - lane;
   const int ty = p.tma_hs ? h_ : s_, tz = p.tma_hs ? s_ : h_;
+  const long long off = ((long long)b * p.ob + (long long)(bh % p.H) * p.oh +
+                         (long long)(grow - lane) * p.os) * kEsize;
   auto put = [&](const float (&v)[32], int c, float inv) {
-    if (om != nullptr) {
+    if (p.n_peers > 0) {
+      store_block_peers<kOut>(p, off, row_bytes, nvalid, v, c, inv, stage, lane);
+    } else if (om != nullptr) {
       if (nvalid > 0) store_block_tma<kOut>(om, c * 32, ty, tz, b, v, inv, stage, lane);
     } else {
       store_block<kOut>(out_w, row_bytes, nvalid, v, c, inv, stage, lane);

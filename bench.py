@@ -318,6 +318,15 @@ def _flush_l2(dev):
 L2_BYTES = 126e6  # B200 L2; calls whose inputs are smaller flush it between timed calls
 
 
+def _head_start(steps):
+    """A GPU-side delay queued before a timed loop (about 0.5 ms per step, at most 20 ms), so
+    that the host enqueues every timed call before the GPU reaches the first one and no
+    host-side launch time (Python wrappers, eight ranks sharing the host's cores) falls
+    inside a call's events."""
+    import torch
+    torch.cuda._sleep(int(min(20.0, 0.5 * steps) * 1.0e6))  # ~1e6 cycles per ms at 1-2 GHz
+
+
 def _time_events(fn, steps, warmup, dist, dev, flush=True):
     """Device time per call of fn: CUDA events around each call on the current stream; with
     flush (inputs smaller than L2) a 256 MiB write before every call, outside the events;
@@ -329,6 +338,7 @@ def _time_events(fn, steps, warmup, dist, dev, flush=True):
     _barrier(dist)
     evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
            for _ in range(steps)]
+    _head_start(steps)
     for e0, e1 in evs:
         if flush:
             _flush_l2(dev)
@@ -378,6 +388,7 @@ def run_ours(args, rank, world, local_rank, dist):
             step()
         _barrier(dist)
         t_begin = time.perf_counter()
+        _head_start(args.steps)
         for i in range(args.steps):
             if flush:
                 _flush_l2(dev)  # outside the step's events: the step starts with a cold L2
@@ -646,7 +657,7 @@ def sampler_run(model, x, cc, cu, args, dist, dev, steps):
 
 
 def dit_step_ms(args, rank, world, local_rank, dist, shard, profile=True, sampler_steps=0,
-                fused_qkv=True):
+                fused_qkv=True, peer_gather=True):
     """One Euler+CFG step of the Anima DiT (config 4): latent 16x128x128 (4096 tokens), 28
     blocks, hidden 2048, 16 heads, CFG pair batched (B=2), sigma 0.5 -> 0, cfg 5; attention
     split by head over the ranks in the given layout.  fused_qkv: q/k/v projections through
@@ -668,7 +679,7 @@ def dit_step_ms(args, rank, world, local_rank, dist, shard, profile=True, sample
     else:
         weights = make_weights(cfg, seed=1234, device=dev, rng_device=dev)
     model = AnimaDiT(cfg, weights, rank=rank, world=world, group=group, shard=shard,
-                     fused_qkv=fused_qkv)
+                     fused_qkv=fused_qkv, peer_gather=peer_gather)
     del weights
     side = args.latent
     g = torch.Generator(device=dev).manual_seed(4321)
@@ -735,7 +746,12 @@ def dit_step_ms(args, rank, world, local_rank, dist, shard, profile=True, sample
            "clocks": clocks.summary(t_begin, t_end), "breakdown_eager": breakdown,
            "layout": shard if world > 1 else "one GPU", "sampler": sampler,
            "qkv_projection": ("anima_qkv_projection (GEMM + norm/RoPE epilogue)" if model.fused_qkv
-                              else "cuBLAS GEMM + attention prologue")}
+                              else "cuBLAS GEMM + attention prologue"),
+           "head_gather": (None if world == 1 or shard != "heads" else
+                           "attention epilogue stores to every rank over NVLink + 1-element "
+                           "all-reduce" if model.peer_gather else "NCCL all_gather_into_tensor")}
+    torch.cuda.synchronize()
+    model.close()
     del model
     torch.cuda.empty_cache()
     return res
@@ -759,6 +775,9 @@ def run_dit_section(args, rank, world, local_rank, dist):
     if world == 1:  # the same step with the projections as cuBLAS GEMMs + the prologue
         out["heads_cublas_qkv"] = dit_step_ms(args, rank, world, local_rank, dist, "heads",
                                               fused_qkv=False)
+    else:  # the heads layout with the NCCL all-gather instead of the epilogue's peer stores
+        out["heads_nccl_gather"] = dit_step_ms(args, rank, world, local_rank, dist, "heads",
+                                               profile=False, peer_gather=False)
     out["ms"] = out["heads"]["ms"]
     return out
 

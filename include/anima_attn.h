@@ -162,6 +162,30 @@ int anima_attn_fwd_noalloc(const AnimaAttnArgs* args, void* stream);
  * (0 when the call does not cut its last round; see anima_attn_schedule). */
 uint64_t anima_attn_workspace_size(int B, int H, int S_q, int S_kv, unsigned flags);
 
+/* Attention whose output is all-gathered over NVLink inside its epilogue (replaces the
+ * NCCL all-gather of per-head outputs before the output projection of the head-parallel
+ * DiT step; the reference's step runs on one device and has no counterpart).  Same
+ * arguments as anima_attn_fwd except args->out, which is not used: every output block is
+ * stored to each of peer_out[0 .. n_peers) (1 <= n_peers <= 8, 16-byte aligned, all with
+ * args->out_stride and args->out_dtype).  A rank passes the bases of every rank's gather
+ * buffer [B, S, H_total, 128], its own included, each already offset to the columns of its
+ * heads; the other ranks' bases are peer mappings (anima_ipc_open).  The kernel only
+ * stores; the caller orders the ranks afterwards (e.g. a one-element NCCL all-reduce on
+ * the stream) before anyone reads the gathered buffer, and alternates between two buffers
+ * so that no rank writes one that another is still reading.  ANIMA_FLAG_PAIR is rejected.
+ * Asynchronous on `stream`. */
+int anima_attn_fwd_gather(const AnimaAttnArgs* args, void* const* peer_out, int n_peers,
+                          void* stream);
+
+/* CUDA IPC for the gather buffers (no counterpart in the reference): anima_ipc_export writes
+ * the ANIMA_IPC_HANDLE_BYTES-byte handle of the allocation holding `ptr` and ptr's offset in
+ * it; another process of the node opens it with anima_ipc_open (peer access enabled) and
+ * releases the mapping with anima_ipc_close(ptr, offset). */
+#define ANIMA_IPC_HANDLE_BYTES 64
+int anima_ipc_export(const void* ptr, void* handle, uint64_t* offset);
+int anima_ipc_open(const void* handle, uint64_t offset, void** ptr);
+int anima_ipc_close(void* ptr, uint64_t offset);
+
 /* The schedule anima_attn_fwd(_noalloc) runs for this call when it is given the workspace
  * it asks for: ANIMA_SCHED_UNIT (one CTA per 256-row unit), ANIMA_SCHED_WHOLE (persistent
  * grid of whole units) or ANIMA_SCHED_CUT (persistent grid, last round cut into key-tile

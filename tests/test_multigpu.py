@@ -15,7 +15,7 @@ from conftest import GOLDEN, rel_l2
 pytestmark = pytest.mark.gpu
 
 
-def _rank(rank, world, port, q, shard):
+def _rank(rank, world, port, q, shard, peer_gather=True):
     import datetime
     import sys
     import torch.distributed as dist
@@ -34,7 +34,9 @@ def _rank(rank, world, port, q, shard):
         cu = rng.standard_normal((1, 512, 1024), dtype=np.float32)
         cfg = DiTConfig(blocks=blocks)
         model = AnimaDiT(cfg, make_weights(cfg, seed=wseed, device="cuda"), rank=rank,
-                         world=world, group=dist.group.WORLD, shard=shard)
+                         world=world, group=dist.group.WORLD, shard=shard,
+                         peer_gather=peer_gather)
+        assert model.peer_gather == (peer_gather and shard == "heads")
         T = lambda a: torch.from_numpy(a).cuda()
         args = (float(g["sigma"]), float(g["sigma_next"]))
         with torch.no_grad():
@@ -42,6 +44,8 @@ def _rank(rank, world, port, q, shard):
             graph = StepGraph(model, T(x), *args, T(cc), T(cu), float(g["cfg"]))
             gout = graph().cpu().numpy()
             del graph  # holds NCCL calls: released before the process group
+        torch.cuda.synchronize()
+        model.close()  # peer mappings of the gather buffers
         if rank == 0:
             q.put((rel_l2(out, g["x_next"]), rel_l2(gout, g["x_next"])))
         dist.barrier()
@@ -51,13 +55,18 @@ def _rank(rank, world, port, q, shard):
 
 @pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2,
                     reason="needs two GPUs")
-@pytest.mark.parametrize("shard", ["tokens", "heads"])
-def test_dit_step_two_gpus(shard):
+@pytest.mark.parametrize("shard,peer_gather", [("tokens", True), ("heads", True),
+                                               ("heads", False)])
+def test_dit_step_two_gpus(shard, peer_gather):
+    """heads with peer_gather: the attention kernel stores every head output into both
+    ranks' gather buffers over NVLink (anima_attn_fwd_gather), a one-element all-reduce
+    orders the ranks; without it, an NCCL all_gather_into_tensor."""
     import torch.multiprocessing as mp
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    port = 29700 + os.getpid() % 200 + (0 if shard == "tokens" else 3)
-    procs = [ctx.Process(target=_rank, args=(r, 2, port, q, shard)) for r in range(2)]
+    port = 29700 + os.getpid() % 200 + (0 if shard == "tokens" else 3 if peer_gather else 6)
+    procs = [ctx.Process(target=_rank, args=(r, 2, port, q, shard, peer_gather))
+             for r in range(2)]
     for p in procs:
         p.start()
     r_eager, r_graph = q.get(timeout=600)
@@ -65,3 +74,59 @@ def test_dit_step_two_gpus(shard):
         p.join(timeout=120)
         assert p.exitcode == 0
     assert r_eager <= 1e-2 and r_graph <= 1e-2
+
+
+def _gather_rank(rank, world, port, q):
+    import datetime
+    import torch.distributed as dist
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=120),
+                            device_id=torch.device("cuda", rank))
+    try:
+        import anima_attn
+        from anima_attn.peer import GatherBuffers
+        B, H, hl, S, D = 2, 4, 2, 1000, 128  # ragged S: a partial unit and a partial key tile
+        g = torch.Generator(device="cuda").manual_seed(100 + rank)
+        qh, kh, vh = (torch.randn(B * hl, S, D, device="cuda", generator=g).half()
+                      for _ in range(3))
+        gb = GatherBuffers((B, S, H, D), torch.float16, "cuda", dist.group.WORLD, rank, world)
+        for i in range(2):  # both buffers, twice each
+            for _ in range(2):
+                mine = gb.bufs[i][:, :, rank * hl:(rank + 1) * hl]
+                anima_attn.attention_core(qh, kh, vh, B, hl, out=mine, out_dtype=torch.float16,
+                                          peers=gb.destinations(i, rank * hl * D))
+                gb.barrier()
+        local = anima_attn.attention_core(qh, kh, vh, B, hl, out_dtype=torch.float16)
+        full = torch.empty((world,) + tuple(local.shape), dtype=local.dtype, device="cuda")
+        dist.all_gather_into_tensor(full, local.contiguous())
+        ref = full.permute(1, 2, 0, 3, 4).reshape(B, S, H, D)
+        torch.cuda.synchronize()
+        ok = all(torch.equal(gb.bufs[i], ref) for i in range(2))
+        status = anima_attn.status()
+        gb.close()
+        q.put((rank, ok, status))
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2,
+                    reason="needs two GPUs")
+def test_attention_epilogue_gather_equals_nccl_all_gather():
+    """anima_attn_fwd_gather on two GPUs: each rank's attention stores its 2 heads into both
+    ranks' [B, S, 4, D] buffers (peer mappings by CUDA IPC); after the barrier both buffers
+    equal the NCCL all-gather of the same attention's local outputs, bit for bit."""
+    import torch.multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = 29900 + os.getpid() % 80
+    procs = [ctx.Process(target=_gather_rank, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = sorted(q.get(timeout=600) for _ in range(2))
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    assert res == [(0, True, 0), (1, True, 0)]
