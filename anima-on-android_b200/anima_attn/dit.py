@@ -192,7 +192,8 @@ class AnimaDiT:
     docstring; both split the attention by head.
     ``attn_fn`` replaces the attention op (signature of anima_attn.attention); tests on
     CPU pass a reference implementation, the product uses the B200 kernels.
-    ``fused_qkv``: with the library attention on CUDA, outside the tokens layout, the q/k/v
+    ``fused_qkv``: with the library attention on CUDA, the MLP's first layer and GELU run as
+    one GEMM (anima_gemm_gelu), and outside the tokens layout the q/k/v
     projections run as anima_qkv_projection (the GEMM with q/k RMSNorm, RoPE and the
     head-major 16-bit store in its epilogue) followed by the attention core, instead of a
     cuBLAS GEMM whose output the attention prologue reads back.
@@ -313,7 +314,13 @@ class AnimaDiT:
 
     def _mlp(self, p, h):
         dt = self.cfg.gemm_dtype
-        hid = self._gelu(_linear(h, self.w[p + "mlp.layer1.weight"], dt))
+        w1 = self.w[p + "mlp.layer1.weight"]
+        if self.fused_qkv and h.is_cuda and h.dtype == dt and h.is_contiguous():
+            from .ops import gemm_gelu  # layer 1 + GELU in one GEMM (fp32 accumulator)
+            with _region("gemm"):
+                hid = gemm_gelu(h, w1)
+        else:
+            hid = self._gelu(_linear(h, w1, dt))
         return _linear(hid, self.w[p + "mlp.layer2.weight"], dt)
 
     # ---------------------------------------------------------- tokens mode (rows)

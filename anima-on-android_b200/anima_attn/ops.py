@@ -303,6 +303,26 @@ def qkv_projection(x: torch.Tensor, w: torch.Tensor, H: int, n_tensors: int = 3,
     return tuple(outs)
 
 
+def gemm_gelu(x: torch.Tensor, w: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """GELU(x @ w.T) in one tcgen05 GEMM, the exact GELU applied to the fp32 accumulator
+    (anima_gemm_gelu; the MLP's first layer and activation, src/predict2.py:45).
+
+    x [..., K] and w [N, K] contiguous float16 or bfloat16 of one type; returns [..., N] of
+    that type."""
+    _check_cuda(x, w)
+    if x.dtype not in (torch.float16, torch.bfloat16) or w.dtype != x.dtype:
+        raise ValueError("x and w must share float16 or bfloat16")
+    if not (x.is_contiguous() and w.is_contiguous()) or w.dim() != 2 or x.shape[-1] != w.shape[1]:
+        raise ValueError("x [..., K] and w [N, K] must be contiguous")
+    K, N = w.shape[1], w.shape[0]
+    M = x.numel() // K
+    if out is None:
+        out = torch.empty(x.shape[:-1] + (N,), device=x.device, dtype=x.dtype)
+    L_.check(L_.lib.anima_gemm_gelu(_ptr(x), _ptr(w), _ptr(out), M, N, K, _TORCH_DT[x.dtype],
+                                    ct.c_void_p(_stream())), "anima_gemm_gelu")
+    return out
+
+
 def apply_rope(t: torch.Tensor, freqs: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
     """predict2.apply_rotary_pos_emb (src/predict2.py:31-38) on the GPU.
 

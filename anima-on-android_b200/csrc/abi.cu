@@ -47,6 +47,8 @@ int rope_strided_launch(const float* t, const long long* ts, const float* f, flo
                         cudaStream_t st);
 int act_launch(int which, const float* x, float* y, long long n, int sm_count, cudaStream_t st);
 int qkv_projection_launch(const AnimaQkvProjArgs* a, int* status, int sm_count, cudaStream_t st);
+int gemm_gelu_launch(const void* x, const void* w, void* y, int M, int N, int K, int dtype,
+                     int* status, int sm_count, cudaStream_t st);
 int layernorm_launch(const float* x, float* y, long long m, int d, float eps, int sm_count,
                      cudaStream_t st);
 int softmax_launch(const float* x, float* y, long long outer, int dim, int sm_count,
@@ -515,6 +517,17 @@ int anima_attn_fwd_noalloc(const AnimaAttnArgs* a, void* stream) {
                                static_cast<cudaStream_t>(stream), &why);
   if (rc != ANIMA_OK)
     set_error(std::string("anima_attn_fwd_noalloc: ") + (why ? why : code_name(rc)));
+  return rc;
+}
+
+int anima_gemm_gelu(const void* x, const void* w, void* y, int M, int N, int K, int dtype,
+                    void* stream) {
+  int rc = ANIMA_OK;
+  DeviceState* d = current_device(&rc);
+  if (!d) return rc;
+  rc = gemm_gelu_launch(x, w, y, M, N, K, dtype, d->status, d->sm_count,
+                        static_cast<cudaStream_t>(stream));
+  if (rc != ANIMA_OK) set_error(std::string("anima_gemm_gelu: ") + code_name(rc));
   return rc;
 }
 

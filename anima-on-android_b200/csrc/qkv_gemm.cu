@@ -23,6 +23,8 @@
 //              shared memory (32 consecutive tokens of one head are 32 consecutive rows of
 //              the head-major output)
 // Every wait is bounded (see common.cuh); a CTA that gives up records ANIMA_ERR_TIMEOUT.
+#include <cstring>
+
 #include "attn_shared.cuh"
 
 namespace anima {
@@ -59,16 +61,20 @@ struct Params {
   const float* freqs;     // [L, 64, 2, 2]; nullptr: no RoPE (applied to q and k)
   float eps;
   void* out[3];           // head-major [B*H, L, 128] per tensor
+  void* y;                // GELU epilogue: row-major [M, N] output, row stride ldy elements
+  long long ldy;
   int* status;
 };
 
-// 32 rows (one per lane) x 16 columns from column c0 of 128-column rows of 16-bit values:
-// packed into the warp's staging buffer, then written as whole 32-byte row pieces (two lanes
-// per row).  The swizzle (piece ^ bit 2 of the row) keeps both phases free of bank
+enum { kEpiQkv = 0, kEpiGelu = 1 };
+
+// 32 rows (one per lane) x 16 columns from column c0 of rows of 16-bit values, row_bytes
+// apart: packed into the warp's staging buffer, then written as whole 32-byte row pieces
+// (two lanes per row).  The swizzle (piece ^ bit 2 of the row) keeps both phases free of bank
 // conflicts.  Rows >= nvalid are not written.
 template <int kDt>
-__device__ __forceinline__ void store_half(char* out_w, int nvalid, const float (&v)[16], int c0,
-                                           uint4* st, int lane) {
+__device__ __forceinline__ void store_half(char* out_w, long long row_bytes, int nvalid,
+                                           const float (&v)[16], int c0, uint4* st, int lane) {
 #pragma unroll
   for (int e = 0; e < 2; ++e)
     st[lane * 2 + (e ^ ((lane >> 2) & 1))] = make_uint4(
@@ -79,12 +85,12 @@ __device__ __forceinline__ void store_half(char* out_w, int nvalid, const float 
   for (int k = 0; k < 2; ++k) {
     const int r = 16 * k + (lane >> 1), q = lane & 1;
     const uint4 x = st[r * 2 + (q ^ ((r >> 2) & 1))];
-    if (r < nvalid) *reinterpret_cast<uint4*>(out_w + r * 256 + (c0 + q * 8) * 2) = x;
+    if (r < nvalid) *reinterpret_cast<uint4*>(out_w + r * row_bytes + (c0 + q * 8) * 2) = x;
   }
   __syncwarp();  // the buffer is free for the next piece
 }
 
-template <int kDt>
+template <int kDt, int kEpi>
 __global__ void __launch_bounds__(kThreads, 1)
     qkv_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a,
                     const __grid_constant__ CUtensorMap tmap_b, const Params p) {
@@ -185,6 +191,44 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     umma_commit(&sm.mma_done);
     attn::drain_wait(&sm.mma_done, 0);
+  } else if (warp >= 4 && kEpi == kEpiGelu) {
+    // ------------------------------------------------------------ GELU epilogue
+    // y = GELU(C) (exact, x (1 + erf(x / sqrt 2)) / 2) on the fp32 accumulator, 16 columns
+    // at a time, stored row-major as 16-bit.
+    const int quarter = warp & 3;
+    const uint32_t lane_field = (uint32_t)(quarter * 32) << 16;
+    int tl = 0;
+    for (int t = blockIdx.x; t < p.n_tiles; t += gridDim.x, ++tl) {
+      const int buf = tl & 1;
+      const int m0 = (t / p.n_tiles_n) * kBM, n0 = (t % p.n_tiles_n) * kBN;
+      const int wm = m0 + quarter * 32;
+      const int nvalid = min(32, p.M - wm);
+      const int nchunks = min(kBN, p.N - n0) / 16;  // N is a multiple of 16
+      const bool got = mbar_wait(&sm.acc_full[buf], (uint32_t)(tl >> 1) & 1u, abort, p.status,
+                                 ANIMA_ERR_TIMEOUT);
+      if (!__all_sync(0xffffffffu, got)) break;
+      tc_fence_after();
+      const uint32_t tb = tmem + lane_field + (uint32_t)buf * kBN;
+      char* const yw = static_cast<char*>(p.y) + ((long long)max(wm, 0) * p.ldy + n0) * 2;
+#pragma unroll 1
+      for (int j = 0; j < nchunks; ++j) {
+        uint32_t r[16];
+        tmem_ld16(tb + 16 * j, r);
+        tmem_ld_wait();
+        if (j == nchunks - 1) {  // the last TMEM read of this buffer is done
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&sm.acc_empty[buf]);
+        }
+        float v[16];
+#pragma unroll
+        for (int e = 0; e < 16; ++e) {
+          const float x = __uint_as_float(r[e]);
+          v[e] = 0.5f * x * (1.f + erff(x * 0.70710678118654752f));
+        }
+        store_half<kDt>(yw, p.ldy * 2, nvalid, v, 16 * j, sm.stage[quarter], lane);
+      }
+    }
   } else if (warp >= 4) {
     // ------------------------------------------------------------ epilogue
     // Pass 1 reads each normalised head's 128 columns for the sum of squares; pass 2
@@ -291,8 +335,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           void* const base = hc[hh] == 0 ? p.out[0] : hc[hh] == 1 ? p.out[1] : p.out[2];
           char* const out_w = static_cast<char*>(base) +
                               (((long long)b * p.H + hh_[hh]) * p.L + s0) * 256;
-          store_half<kDt>(out_w, nvalid, a, 16 * j, sm.stage[quarter], lane);
-          store_half<kDt>(out_w, nvalid, d, 64 + 16 * j, sm.stage[quarter], lane);
+          store_half<kDt>(out_w, 256, nvalid, a, 16 * j, sm.stage[quarter], lane);
+          store_half<kDt>(out_w, 256, nvalid, d, 64 + 16 * j, sm.stage[quarter], lane);
         }
         if (any_rope && j < 3) {
 #pragma unroll
@@ -349,10 +393,10 @@ static int make_rows_map(CUtensorMap* map, const void* base, int dtype, int rows
   return r == CUDA_SUCCESS ? ANIMA_OK : ANIMA_ERR_CUDA;
 }
 
-template <int kDt>
+template <int kDt, int kEpi>
 static int qkv_launch_t(const CUtensorMap& ma, const CUtensorMap& mb, const qkv::Params& prm,
                         int grid, cudaStream_t st) {
-  auto kern = qkv::qkv_gemm_kernel<kDt>;
+  auto kern = qkv::qkv_gemm_kernel<kDt, kEpi>;
   static int attr_dev_mask = 0;
   int dev = 0;
   cudaGetDevice(&dev);
@@ -405,8 +449,46 @@ int qkv_projection_launch(const AnimaQkvProjArgs* a, int* status, int sm_count, 
   for (int c = 0; c < 3; ++c) prm.out[c] = outs[c];
   prm.status = status;
   const int grid = (int)(tiles < sm_count ? tiles : sm_count);
-  return a->dtype == ANIMA_DTYPE_BF16 ? qkv_launch_t<ANIMA_DTYPE_BF16>(ma, mb, prm, grid, st)
-                                      : qkv_launch_t<ANIMA_DTYPE_F16>(ma, mb, prm, grid, st);
+  prm.y = nullptr;
+  prm.ldy = 0;
+  return a->dtype == ANIMA_DTYPE_BF16
+             ? qkv_launch_t<ANIMA_DTYPE_BF16, qkv::kEpiQkv>(ma, mb, prm, grid, st)
+             : qkv_launch_t<ANIMA_DTYPE_F16, qkv::kEpiQkv>(ma, mb, prm, grid, st);
+}
+
+// y [M, N] = GELU(x [M, K] W[N, K]^T), 16-bit row-major (the first layer of the DiT block's
+// MLP with its activation, predict2.py:45: the cuBLAS GEMM + GELU pass it replaces read and
+// wrote the hidden layer once more).
+int gemm_gelu_launch(const void* x, const void* w, void* y, int M, int N, int K, int dtype,
+                     int* status, int sm_count, cudaStream_t st) {
+  if (dtype != ANIMA_DTYPE_F16 && dtype != ANIMA_DTYPE_BF16) return ANIMA_ERR_ARG;
+  if (M <= 0 || N <= 0 || K <= 0 || N % 16 != 0 || K % 8 != 0) return ANIMA_ERR_SHAPE;
+  if (!x || !w || !y ||
+      ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(w) |
+        reinterpret_cast<uintptr_t>(y)) & 15u))
+    return ANIMA_ERR_ARG;
+  CUtensorMap ma, mb;
+  int rc;
+  if ((rc = make_rows_map(&ma, x, dtype, M, K, qkv::kBM))) return rc;
+  if ((rc = make_rows_map(&mb, w, dtype, N, K, qkv::kBN))) return rc;
+  qkv::Params prm;
+  memset(&prm, 0, sizeof(prm));
+  prm.M = M;
+  prm.N = N;
+  prm.K = K;
+  prm.L = 1;
+  prm.H = 1;
+  prm.n_tiles_n = (N + qkv::kBN - 1) / qkv::kBN;
+  const long long tiles = (long long)((M + qkv::kBM - 1) / qkv::kBM) * prm.n_tiles_n;
+  if (tiles > 0x7fffffffLL) return ANIMA_ERR_SHAPE;
+  prm.n_tiles = (int)tiles;
+  prm.y = y;
+  prm.ldy = N;
+  prm.status = status;
+  const int grid = (int)(tiles < sm_count ? tiles : sm_count);
+  return dtype == ANIMA_DTYPE_BF16
+             ? qkv_launch_t<ANIMA_DTYPE_BF16, qkv::kEpiGelu>(ma, mb, prm, grid, st)
+             : qkv_launch_t<ANIMA_DTYPE_F16, qkv::kEpiGelu>(ma, mb, prm, grid, st);
 }
 
 }  // namespace anima

@@ -918,9 +918,26 @@ def run_qkv(args):
                      "fused_frac_of_measured_peak": round(fl / (tf * 1e-3) / 1e12 / peak, 3),
                      "cublas_gemm_tflops": tflops(tg), "speedup_vs_unfused": round(tu / tf, 3),
                      "max_abs_diff_vs_unfused": round(diff, 4)}
+    # The MLP's first layer + GELU (B*L x 8192 x 2048): anima_gemm_gelu against the cuBLAS
+    # GEMM followed by the library's GELU pass.
+    x = torch.randn(Bq * L, K, device=dev, generator=g).to(dt)
+    w = (torch.randn(4 * K, K, device=dev, generator=g) / K ** 0.5).to(dt)
+    fused = lambda: ops.gemm_gelu(x, w)
+    unfused = lambda: ops.gelu_(torch.mm(x, w.t()))
+    diff = float((fused().float() - unfused().float()).abs().max())
+    tf, tu = timed(fused), timed(unfused)
+    tg = timed(lambda: torch.mm(x, w.t()))
+    fl = 2.0 * Bq * L * K * 4 * K
+    out["mlp1_gelu"] = {"fused_ms": round(tf, 4), "cublas_plus_gelu_ms": round(tu, 4),
+                        "cublas_gemm_ms": round(tg, 4),
+                        "fused_tflops": round(fl / (tf * 1e-3) / 1e12, 1),
+                        "fused_frac_of_measured_peak": round(fl / (tf * 1e-3) / 1e12 / peak, 3),
+                        "speedup_vs_unfused": round(tu / tf, 3),
+                        "max_abs_diff_vs_unfused": round(diff, 4)}
     if anima_attn.status() != 0:
         raise SystemExit("device-side timeout recorded")
-    return {"workload": f"q/k/v projection + prologue, B={Bq} L={L} K={K} fp16 (DiT shapes)",
+    return {"workload": f"q/k/v projection + prologue, and MLP layer 1 + GELU, B={Bq} L={L} "
+                        f"K={K} fp16 (DiT shapes)",
             "peak_bf16_tflops_measured": peak, "shapes": out}
 
 

@@ -254,6 +254,13 @@ int anima_dit_ln_modulate(const float* x, const float* scale, const float* shift
                           int rows_per_b, int D, float eps, void* stream);
 int anima_dit_gate_residual(float* x, const float* gate, int64_t gate_stride_b, const float* y,
                             int64_t rows, int rows_per_b, int D, void* stream);
+/* anima_gemm_gelu: y [M, N] = GELU(x [M, K] W[N, K]^T), the first layer of the DiT block's
+ *   MLP with its exact GELU (x (1 + erf(x / sqrt 2)) / 2, src/predict2.py:45) applied to the
+ *   fp32 accumulator in the epilogue of one tcgen05 GEMM; x, W and y row-major 16-bit of
+ *   dtype (ANIMA_DTYPE_F16 or BF16), 16-byte aligned, N a multiple of 16 and K of 8.
+ *   Asynchronous on `stream`. */
+int anima_gemm_gelu(const void* x, const void* w, void* y, int M, int N, int K, int dtype,
+                    void* stream);
 /* anima_dit_gate_residual_ln_modulate: the two above back to back in one pass -- x += gate[b]*y
  *   in place, then h = LayerNorm(x) * (1 + scale[b]) + shift[b] as out_dtype (a sub-block's
  *   gated residual followed by the next sub-block's modulated LayerNorm, predict2.py:536-563);
