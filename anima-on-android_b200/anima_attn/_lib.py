@@ -77,6 +77,10 @@ SIGNATURES = {
     "anima_attn_fwd_noalloc": ([ct.POINTER(AttnArgs), _P], ct.c_int),
     "anima_attn_fwd_gather": ([ct.POINTER(AttnArgs), ct.POINTER(_P), ct.c_int, _P], ct.c_int),
     "anima_gemm_gelu": ([_P, _P, _P] + [ct.c_int] * 4 + [_P], ct.c_int),
+    "anima_qkv_projection_scatter": ([ct.POINTER(QkvProjArgs), ct.c_int, ct.c_int, ct.POINTER(_P),
+                                      ct.c_int, _P], ct.c_int),
+    "anima_attn_fwd_scatter_rows": ([ct.POINTER(AttnArgs), ct.POINTER(_P), ct.c_int, ct.c_int,
+                                     ct.c_int64, ct.c_int, _P], ct.c_int),
     "anima_ipc_export": ([_P, _P, ct.POINTER(ct.c_uint64)], ct.c_int),
     "anima_ipc_open": ([_P, ct.c_uint64, ct.POINTER(_P)], ct.c_int),
     "anima_ipc_close": ([_P, ct.c_uint64], ct.c_int),

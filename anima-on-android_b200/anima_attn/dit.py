@@ -40,7 +40,9 @@ Multi-GPU (N ranks; the attention is split by heads in both modes, rank r owning
                   per head, and a second all_to_all_single returns all heads' outputs for its
                   own rows before the o-proj -- the part of the all-gather a rank uses.  The
                   o-proj, MLP, LayerNorm/adaLN passes and final layer run on its rows only.
-                  Cross-attention K/V come from the (replicated, 512-token) context.
+                  Cross-attention K/V come from the (replicated, 512-token) context.  With
+                  peer_a2a (default on CUDA) both exchanges are stores from the producing
+                  kernels into the other ranks' buffers over NVLink (peer.PeerBuffers).
 
 Weights follow the reference's parameter names (state-dict keys of MiniTrainDIT with
 use_adaln_lora=True), so the same seeded weights load into the reference model for the
@@ -197,6 +199,11 @@ class AnimaDiT:
     projections run as anima_qkv_projection (the GEMM with q/k RMSNorm, RoPE and the
     head-major 16-bit store in its epilogue) followed by the attention core, instead of a
     cuBLAS GEMM whose output the attention prologue reads back.
+    ``peer_a2a``: tokens layout with fused_qkv: the projection GEMM stores each head's
+    operand rows into the owning rank's buffers and the attention stores each output row into
+    its token owner's buffer over NVLink (anima_qkv_projection_scatter,
+    anima_attn_fwd_scatter_rows), with one-element all-reduces ordering the ranks, instead of
+    two NCCL all-to-alls and the prologue per attention.
     ``peer_gather``: heads layout on N > 1 GPUs with fused_qkv: the attention kernel stores
     its head outputs into every rank's gather buffer over NVLink (anima_attn_fwd_gather) and a
     one-element all-reduce orders the ranks, instead of an NCCL all-gather.  The buffers are
@@ -206,7 +213,8 @@ class AnimaDiT:
 
     def __init__(self, cfg: DiTConfig, weights: Dict[str, torch.Tensor], rank: int = 0,
                  world: int = 1, group=None, attn_fn: Optional[AttnFn] = None,
-                 shard: str = "tokens", fused_qkv: bool = True, peer_gather: bool = True):
+                 shard: str = "tokens", fused_qkv: bool = True, peer_gather: bool = True,
+                 peer_a2a: bool = True):
         if cfg.heads % world:
             raise ValueError("heads must divide evenly over ranks")
         if shard not in ("tokens", "heads"):
@@ -239,6 +247,9 @@ class AnimaDiT:
                 self.w[sa + "qkv"] = torch.cat([t.view(N, cols, D) for t in (wq, wk, wv)], 1).contiguous()
                 cq = self.w.pop(ca + "q_proj.weight")
                 self.w[ca + "q_by_rank"] = cq.view(N, cols, cq.shape[1]).contiguous()
+                if peer_a2a and self.w[sa + "qkv"].is_cuda:  # (tensor, global head, dim) rows
+                    self.w[sa + "qkv_all"] = torch.cat([wq, wk, wv]).contiguous()
+                    self.w[ca + "q_all"] = cq.contiguous()
             else:
                 self.w[sa + "qkv"] = torch.cat([wq[lo:hi], wk[lo:hi], wv[lo:hi]]).contiguous()
                 self.w[ca + "q_proj.weight"] = self.w[ca + "q_proj.weight"][lo:hi].contiguous()
@@ -254,6 +265,12 @@ class AnimaDiT:
         # all-gather and the transpose before the o-proj
         self.peer_gather = bool(peer_gather) and self.fused_qkv and world > 1 and not self.seq
         self._gather = None
+        # tokens layout: the q/k/v projection stores each head's operand rows into its owner's
+        # buffers and the attention stores each output row into its token owner's buffer,
+        # over NVLink (anima_qkv_projection_scatter, anima_attn_fwd_scatter_rows), in place of
+        # the two NCCL all-to-alls and the prologue on the received projections
+        self.peer_a2a = bool(peer_a2a) and self.fused_qkv and self.seq
+        self._a2a_bufs, self._a2a_key = None, None
         self._freqs_cache = {}
         self._w32 = {}
 
@@ -369,8 +386,64 @@ class AnimaDiT:
             dist.all_to_all_single(out, t, group=self.group)
         return out
 
+    def _a2a_buffers(self, B: int, L: int, device):
+        """The peer buffers of the tokens layout for a [B, L] token grid (collective on first
+        use and on a shape change): q/k/v operands of this rank's heads for self-attention
+        (q0, k0, v0), the query of cross-attention (q1), and this rank's rows of all heads'
+        attention outputs (o0 self, o1 cross)."""
+        from .peer import PeerBuffers
+        cfg, hl, hd, dt = self.cfg, self.h_local, self.cfg.head_dim, self.cfg.gemm_dtype
+        n = B * L // self.world
+        if self._a2a_bufs is None or self._a2a_key != (B, L):
+            if self._a2a_bufs is not None:
+                self._a2a_bufs.close()
+            op = ((B * hl, L, hd), dt)
+            out = ((n, cfg.heads * hd), dt)
+            self._a2a_bufs = PeerBuffers({"q0": op, "k0": op, "v0": op, "q1": op, "o0": out,
+                                          "o1": out}, device, self.group, self.rank, self.world)
+            self._a2a_key = (B, L)
+        return self._a2a_bufs
+
+    def _attention_rows_peer(self, p, h_loc, B, L, ctx, freqs):
+        """_attention_rows with the all-to-alls folded into the projection's and the
+        attention's epilogues: projection GEMM (all heads, this rank's rows) -> each head's
+        rows into its owner's q/k/v buffers -> barrier -> attention on this rank's heads ->
+        each output row into its token owner's buffer -> barrier -> o-proj of this rank's
+        rows."""
+        from .ops import attention_core, qkv_projection_scatter
+        cfg, N, r = self.cfg, self.world, self.rank
+        hl, hd, dt = self.h_local, cfg.head_dim, cfg.gemm_dtype
+        n = h_loc.shape[0]
+        g = self._a2a_buffers(B, L, h_loc.device)
+        h16 = h_loc.to(dt).contiguous()
+        qw = self._norm32(p + ".q_norm.weight")
+        if ctx is None:
+            dest = [(g.ptr("q0", d), g.ptr("k0", d), g.ptr("v0", d)) for d in range(N)]
+            with _region("qkv_fused"):
+                qkv_projection_scatter(h16, self.w[p + ".qkv_all"], B, L, hl, r * n, dest, 3, 0,
+                                       qw, self._norm32(p + ".k_norm.weight"), freqs, cfg.eps)
+            qh, kh, vh, o = g.local["q0"], g.local["k0"], g.local["v0"], "o0"
+        else:
+            dest = [(g.ptr("q1", d), 0, 0) for d in range(N)]
+            with _region("qkv_fused"):
+                qkv_projection_scatter(h16, self.w[p + ".q_all"], B, L, hl, r * n, dest, 1, 0,
+                                       qw, None, None, cfg.eps, True, False)
+            entry = ctx if isinstance(ctx, dict) else self._context_entry(p, ctx, True)
+            qh, kh, vh, o = g.local["q1"], entry["kh"], entry["vh"], "o1"
+        with _region("collective"):
+            g.barrier()
+        with _region("attention"):
+            attention_core(qh, kh, vh, B, hl, out_dtype=dt,
+                           scatter=(g.ptrs(o), n, cfg.heads * hd, r * hl))
+        with _region("collective"):
+            g.barrier()
+        return _linear(g.local[o], self.w[p + ".output_proj.weight"], dt)
+
     def _attention_rows(self, p, h_loc, B, L, ctx, freqs):
         """Head-parallel attention for local token rows h_loc [n, D] -> o-proj [n, D]."""
+        if (self.peer_a2a and h_loc.is_cuda and L % 32 == 0 and h_loc.shape[0] % 32 == 0
+                and (ctx is None or not isinstance(ctx, dict) or "kh" in ctx)):
+            return self._attention_rows_peer(p, h_loc, B, L, ctx, freqs)
         cfg, N = self.cfg, self.world
         hl, hd, dt = self.h_local, cfg.head_dim, cfg.gemm_dtype
         n = h_loc.shape[0]
@@ -432,10 +505,13 @@ class AnimaDiT:
         return self._gather
 
     def close(self) -> None:
-        """Releases the peer mappings of the gather buffers (heads layout, N > 1)."""
+        """Releases the peer mappings of the gather / all-to-all buffers (N > 1)."""
         if self._gather is not None:
             self._gather.close()
             self._gather = None
+        if self._a2a_bufs is not None:
+            self._a2a_bufs.close()
+            self._a2a_bufs, self._a2a_key = None, None
 
     def _fused(self, x: torch.Tensor) -> bool:
         """Whether x [B, S, K] can feed anima_qkv_projection (token count a multiple of 32)."""

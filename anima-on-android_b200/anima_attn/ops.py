@@ -132,7 +132,8 @@ def attention_core(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, B: int, H:
                    causal: bool = False, out: Optional[torch.Tensor] = None,
                    out_layout: str = "bshd", out_dtype=torch.float32,
                    schedule: str = "auto", pair: bool = False,
-                   kv64: bool = False, peers: Optional[list] = None) -> torch.Tensor:
+                   kv64: bool = False, peers: Optional[list] = None,
+                   scatter: Optional[tuple] = None) -> torch.Tensor:
     """tcgen05 flash attention on 16-bit head-major operands.
 
     q [B*H, S_q, 128], k/v [B*H, S_kv, 128] contiguous bf16/fp16.  Returns (or fills)
@@ -148,6 +149,10 @@ def attention_core(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, B: int, H:
     ``peers``: device addresses (one per rank, this rank's included) that each receive every
     output block, with ``out``'s strides and dtype (anima_attn_fwd_gather): the all-gather
     of head outputs done by the epilogue; ``out`` is then this rank's own destination.
+    ``scatter`` = (dest, rows_per_dest, row_stride, head0): the output rows go to the ranks
+    that own them (anima_attn_fwd_scatter_rows): global row b*S_q + s to dest[g //
+    rows_per_dest] at row g % rows_per_dest, columns of heads head0.. of rows row_stride
+    elements long; nothing is returned (``out`` is not used).
     """
     _check_cuda(q, k, v)
     BH, Sq, D = q.shape
@@ -158,6 +163,8 @@ def attention_core(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, B: int, H:
         raise ValueError("operands must be bfloat16 or float16")
     if not (q.is_contiguous() and k.is_contiguous() and v.is_contiguous()):
         raise ValueError("operands must be contiguous")
+    if out is None and scatter is not None:  # strides only; the kernel stores to `scatter`
+        out = torch.empty((1, 1, 1, D), device=q.device, dtype=out_dtype).expand(B, Sq, H, D)
     if out is None:
         shape = (B, Sq, H, D) if out_layout == "bshd" else (B, H, Sq, D)
         out = torch.empty(shape, device=q.device, dtype=out_dtype)
@@ -197,6 +204,14 @@ def attention_core(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, B: int, H:
         ws = _workspace(q.device, int(L.lib.anima_attn_workspace_size(B, H, Sq, Skv, flags)))
     a.workspace = _ptr(ws)
     a.workspace_bytes = 0 if ws is None else ws.numel()
+    if scatter is not None:
+        dest, rows_per_dest, row_stride, head0 = scatter
+        arr = (ct.c_void_p * len(dest))(*dest)
+        L.check(L.lib.anima_attn_fwd_scatter_rows(ct.byref(a), arr, len(dest), int(rows_per_dest),
+                                                  int(row_stride), int(head0),
+                                                  ct.c_void_p(_stream())),
+                "anima_attn_fwd_scatter_rows")
+        return None
     if peers:
         arr = (ct.c_void_p * len(peers))(*peers)
         L.check(L.lib.anima_attn_fwd_gather(ct.byref(a), arr, len(peers), ct.c_void_p(_stream())),
@@ -301,6 +316,49 @@ def qkv_projection(x: torch.Tensor, w: torch.Tensor, H: int, n_tensors: int = 3,
     a.q_out, a.k_out, a.v_out = (_ptr(t) for t in outs)
     L_.check(L_.lib.anima_qkv_projection(ct.byref(a), ct.c_void_p(_stream())), "anima_qkv_projection")
     return tuple(outs)
+
+
+def qkv_projection_scatter(x: torch.Tensor, w: torch.Tensor, B: int, L: int, H: int, row0: int,
+                           dest: list, n_tensors: int = 3, first_tensor: int = 0,
+                           q_norm_w: Optional[torch.Tensor] = None,
+                           k_norm_w: Optional[torch.Tensor] = None,
+                           rope_freqs: Optional[torch.Tensor] = None, eps: float = 1e-6,
+                           norm_q: bool = True, norm_k: bool = True) -> None:
+    """qkv_projection for the token rows x [rows, K] (global rows row0.. of the [B, L] token
+    grid) and all heads of a split over len(dest) ranks with H heads each, every head's
+    operand rows stored into its rank's buffers (anima_qkv_projection_scatter): dest[d] =
+    (q, k, v) device addresses of rank d's head-major [B*H, L, 128] buffers (0 for tensors
+    not computed).  w [n_tensors*len(dest)*H*128, K] in (tensor, global head, dim) row order."""
+    _check_cuda(x, w)
+    if x.dtype not in (torch.float16, torch.bfloat16) or w.dtype != x.dtype:
+        raise ValueError("x and w must share float16 or bfloat16")
+    if x.dim() != 2 or not (x.is_contiguous() and w.is_contiguous()):
+        raise ValueError("x must be [rows, K]; x and w contiguous")
+    rows, K = x.shape
+    if w.shape != (n_tensors * len(dest) * H * 128, K):
+        raise ValueError("w must be [n_tensors*ranks*H*128, K]")
+    qw, kw = _as_weight(q_norm_w, x.device), _as_weight(k_norm_w, x.device)
+    fr = None
+    flags = (L_.FLAG_QNORM if norm_q else 0) | (L_.FLAG_KNORM if norm_k else 0)
+    if rope_freqs is not None:
+        fr = rope_freqs.detach().to(device=x.device, dtype=torch.float32).reshape(-1).contiguous()
+        if fr.numel() != L * 256:
+            raise ValueError("rope_freqs must hold [L, 64, 2, 2] values")
+        flags |= L_.FLAG_ROPE
+    a = L_.QkvProjArgs()
+    a.x, a.w = _ptr(x), _ptr(w)
+    a.dtype = _TORCH_DT[x.dtype]
+    a.B, a.L, a.H, a.K = B, L, H, K
+    a.n_tensors, a.first_tensor = n_tensors, first_tensor
+    a.q_norm_w, a.k_norm_w = _ptr(qw), _ptr(kw)
+    a.eps = float(eps)
+    a.rope_freqs = _ptr(fr)
+    a.flags = flags
+    flat = [int(p) for d3 in dest for p in d3]
+    arr = (ct.c_void_p * len(flat))(*flat)
+    L_.check(L_.lib.anima_qkv_projection_scatter(ct.byref(a), rows, row0, arr, len(dest),
+                                                 ct.c_void_p(_stream())),
+             "anima_qkv_projection_scatter")
 
 
 def gemm_gelu(x: torch.Tensor, w: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:

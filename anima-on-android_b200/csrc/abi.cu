@@ -18,7 +18,11 @@
 
 namespace anima {
 int attn_fwd_launch(const AnimaAttnArgs* a, int* status, int sm_count, cudaStream_t st,
-                    void* const* peers = nullptr, int n_peers = 0);
+                    void* const* peers = nullptr, int n_peers = 0, int peer_rows = 0,
+                    long long peer_row_stride = 0, int peer_head0 = 0);
+int qkv_projection_scatter_launch(const AnimaQkvProjArgs* a, int rows, int row0,
+                                  void* const* dest, int n_dest, int* status, int sm_count,
+                                  cudaStream_t st);
 int attn_fwd_pair_launch(const AnimaAttnArgs* a, int* status, cudaStream_t st);
 size_t attn_workspace_bytes(int B, int H, int S_q, int S_kv, unsigned flags, int sm_count);
 int attn_schedule_mode(int B, int H, int S_q, int S_kv, unsigned flags, int sm_count);
@@ -531,6 +535,49 @@ int anima_gemm_gelu(const void* x, const void* w, void* y, int M, int N, int K, 
   return rc;
 }
 
+int anima_qkv_projection_scatter(const AnimaQkvProjArgs* a, int rows, int row0,
+                                 void* const* dest, int n_dest, void* stream) {
+  if (!a) return ANIMA_ERR_ARG;
+  int rc = ANIMA_OK;
+  DeviceState* d = current_device(&rc);
+  if (!d) return rc;
+  rc = qkv_projection_scatter_launch(a, rows, row0, dest, n_dest, d->status, d->sm_count,
+                                     static_cast<cudaStream_t>(stream));
+  if (rc != ANIMA_OK) set_error(std::string("anima_qkv_projection_scatter: ") + code_name(rc));
+  return rc;
+}
+
+int anima_attn_fwd_scatter_rows(const AnimaAttnArgs* a, void* const* dest, int n_dest,
+                                int rows_per_dest, int64_t dest_row_stride, int head0,
+                                void* stream) {
+  if (!a || !dest || n_dest < 1 || n_dest > 8 || rows_per_dest <= 0 || head0 < 0)
+    return ANIMA_ERR_ARG;
+  if (a->flags & ANIMA_FLAG_PAIR) return ANIMA_ERR_ARG;
+  if (a->S_q <= 0 || a->S_q % 32 != 0 || rows_per_dest % 32 != 0) return ANIMA_ERR_SHAPE;
+  if ((long long)a->B * a->S_q > (long long)n_dest * rows_per_dest) return ANIMA_ERR_SHAPE;
+  const int esz = a->out_dtype == ANIMA_DTYPE_F32 ? 4 : 2;
+  if (dest_row_stride <= 0 || (dest_row_stride * esz) % 16 ||
+      ((long long)head0 + a->H) * 128 > dest_row_stride)
+    return ANIMA_ERR_ARG;
+  for (int i = 0; i < n_dest; ++i)
+    if (!dest[i] || (reinterpret_cast<uintptr_t>(dest[i]) & 15u)) return ANIMA_ERR_ARG;
+  AnimaAttnArgs b = *a;
+  b.out = dest[0];
+  b.out_stride[0] = b.out_stride[1] = b.out_stride[2] = dest_row_stride;  // unused by the kernel
+  if (!b.q || !b.k || !b.v) return ANIMA_ERR_ARG;
+  if ((b.flags & ANIMA_FLAG_MASK) && !b.kv_valid_len) return ANIMA_ERR_ARG;
+  const uintptr_t al = reinterpret_cast<uintptr_t>(b.q) | reinterpret_cast<uintptr_t>(b.k) |
+                       reinterpret_cast<uintptr_t>(b.v);
+  if (al & 15u) return ANIMA_ERR_ARG;
+  int rc = ANIMA_OK;
+  DeviceState* d = current_device(&rc);
+  if (!d) return rc;
+  rc = attn_fwd_launch(&b, d->status, d->sm_count, static_cast<cudaStream_t>(stream), dest,
+                       n_dest, rows_per_dest, dest_row_stride, head0);
+  if (rc != ANIMA_OK) set_error(std::string("anima_attn_fwd_scatter_rows: ") + code_name(rc));
+  return rc;
+}
+
 int anima_attn_fwd_gather(const AnimaAttnArgs* a, void* const* peer_out, int n_peers,
                           void* stream) {
   if (!a || !peer_out || n_peers < 1 || n_peers > 8) return ANIMA_ERR_ARG;
@@ -551,7 +598,7 @@ int anima_attn_fwd_gather(const AnimaAttnArgs* a, void* const* peer_out, int n_p
   DeviceState* d = current_device(&rc);
   if (!d) return rc;
   rc = attn_fwd_launch(&b, d->status, d->sm_count, static_cast<cudaStream_t>(stream), peer_out,
-                       n_peers);
+                       n_peers, 0, 0, 0);
   if (rc != ANIMA_OK) set_error(std::string("anima_attn_fwd_gather: ") + code_name(rc));
   return rc;
 }

@@ -651,7 +651,8 @@ int attn_schedule_mode(int B, int H, int S_q, int S_kv, unsigned flags, int sm_c
 }
 
 int attn_fwd_launch(const AnimaAttnArgs* a, int* status, int sm_count, cudaStream_t st,
-                    void* const* peers, int n_peers) {
+                    void* const* peers, int n_peers, int peer_rows, long long peer_row_stride,
+                    int peer_head0) {
   if (a->D != attn::kD) return ANIMA_ERR_SHAPE;
   if (a->op_dtype != ANIMA_DTYPE_BF16 && a->op_dtype != ANIMA_DTYPE_F16) return ANIMA_ERR_ARG;
   if (a->out_dtype != ANIMA_DTYPE_F32 && a->out_dtype != ANIMA_DTYPE_BF16 &&
@@ -701,6 +702,9 @@ int attn_fwd_launch(const AnimaAttnArgs* a, int* status, int sm_count, cudaStrea
   prm.tma_hs = 0;
   prm.n_peers = n_peers;
   for (int i = 0; i < attn::kMaxPeers; ++i) prm.peer_out[i] = i < n_peers ? peers[i] : nullptr;
+  prm.peer_rows = peer_rows;
+  prm.peer_row_stride = peer_row_stride;
+  prm.peer_head0 = peer_head0;
   if (kv64) return attn64_launch(mq, mk, mv, prm, grid, a->op_dtype, a->out_dtype, st);
   CUtensorMap mo;
   memset(&mo, 0, sizeof(mo));
@@ -742,7 +746,7 @@ int attn_fwd_launch_noalloc(const AnimaAttnArgs* a, int* status, int sm_count, v
   AnimaAttnArgs b = *a;
   b.workspace = scratch;
   b.workspace_bytes = attn::kNoAllocScratchBytes;
-  return attn_fwd_launch(&b, status, sm_count, st, nullptr, 0);
+  return attn_fwd_launch(&b, status, sm_count, st, nullptr, 0, 0, 0, 0);
 }
 
 }  // namespace anima

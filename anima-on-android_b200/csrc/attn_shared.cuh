@@ -60,8 +60,12 @@ struct Params {
   float* part;         // partial slots [tail_ctas][2][kPartFloats]
   int tma_out;         // 1: output blocks leave by TMA tensor stores (map passed separately)
   int tma_hs;          // output map axes (D, H, S, B) (1) or (D, S, H, B) (0)
-  int n_peers;         // > 0: every output block goes to each peer_out base (same strides)
+  int n_peers;         // > 0: output blocks go to peer_out bases instead of out
   void* peer_out[kMaxPeers];
+  int peer_rows;       // 0: every block to every base (all-gather); > 0: row scatter, global
+                       // row g = b * S_q + s to base g / peer_rows at local row g % peer_rows
+  long long peer_row_stride;  // row scatter: elements between a destination's rows
+  int peer_head0;      // row scatter: this call's first head in a destination row
 };
 
 // Slice of the last round owned by CTA c: key-tile steps [slice_lo(c), slice_lo(c+1)).
@@ -322,7 +326,20 @@ __device__ __forceinline__ void segment_epilogue(const Params& p, const Seg& sg,
   const long long off = ((long long)b * p.ob + (long long)(bh % p.H) * p.oh +
                          (long long)(grow - lane) * p.os) * kEsize;
   auto put = [&](const float (&v)[32], int c, float inv) {
-    if (p.n_peers > 0) {
+    if (p.n_peers > 0 && p.peer_rows > 0) {
+      // the all-to-all back to the token owners: the 32 rows of this block belong to one
+      // rank (S_q and peer_rows are multiples of 32)
+      const int g0 = b * p.S_q + s_;
+      const int d = g0 / p.peer_rows, r0 = g0 - d * p.peer_rows;
+      char* base = nullptr;
+#pragma unroll
+      for (int k = 0; k < kMaxPeers; ++k)  // constant indices: no local copy of the params
+        if (k == d) base = static_cast<char*>(p.peer_out[k]);
+      if (nvalid > 0)
+        store_block<kOut>(base + ((long long)r0 * p.peer_row_stride +
+                                  (long long)(p.peer_head0 + h_) * kD) * kEsize,
+                          p.peer_row_stride * kEsize, nvalid, v, c, inv, stage, lane);
+    } else if (p.n_peers > 0) {
       store_block_peers<kOut>(p, off, row_bytes, nvalid, v, c, inv, stage, lane);
     } else if (om != nullptr) {
       if (nvalid > 0) store_block_tma<kOut>(om, c * 32, ty, tz, b, v, inv, stage, lane);

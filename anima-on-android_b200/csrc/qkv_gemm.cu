@@ -51,8 +51,10 @@ struct Smem {
 constexpr size_t kSmemBytes = sizeof(Smem) + 1024;
 static_assert(kSmemBytes <= 227 * 1024, "shared memory budget");
 
+constexpr int kMaxDest = 8;
+
 struct Params {
-  int M, N, K;            // GEMM: tokens B*L, columns n_tensors*H*128, depth
+  int M, N, K;            // GEMM: token rows, columns n_tensors*H*128, depth
   int L, H;               // tokens per sample, heads per tensor
   int n_tiles_n, n_tiles; // column tiles, all tiles
   int tensor0;            // tensor (0 q, 1 k, 2 v) of the first 128-column block
@@ -60,7 +62,12 @@ struct Params {
   unsigned norm_mask;     // bit c: normalise tensor c
   const float* freqs;     // [L, 64, 2, 2]; nullptr: no RoPE (applied to q and k)
   float eps;
-  void* out[3];           // head-major [B*H, L, 128] per tensor
+  // Head-major [B*Hd, L, 128] outputs: global head hg (of H per tensor) goes to destination
+  // hg / Hd as its local head hg % Hd (one destination: this call's own q/k/v; several: the
+  // ranks of a head split, reached through peer mappings).  Rows are tokens row0 + m of
+  // the [B, L] token grid.
+  int row0, Hd, n_dest;
+  void* dest[kMaxDest][3];
   void* y;                // GELU epilogue: row-major [M, N] output, row stride ldy elements
   long long ldy;
   int* status;
@@ -243,8 +250,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int t = blockIdx.x; t < p.n_tiles; t += gridDim.x, ++tl) {
       const int buf = tl & 1;
       const int m0 = (t / p.n_tiles_n) * kBM, n0 = (t % p.n_tiles_n) * kBN;
-      const int wm = m0 + quarter * 32;        // the warp's first token
-      const int b = wm / p.L, s0 = wm - b * p.L;
+      const int wm = m0 + quarter * 32;        // the warp's first token row of x
+      const int gw = p.row0 + wm;              // ... in the [B, L] token grid
+      const int b = gw / p.L, s0 = gw - b * p.L;
       const int nvalid = min(32, p.M - wm);    // rows of the warp inside the GEMM
       bool hval[2], hnorm[2], hrope[2];
       int hc[2], hh_[2];
@@ -332,9 +340,14 @@ __global__ void __launch_bounds__(kThreads, 1)
               d[e] = fc[e].z * x + fc[e].w * y;
             }
           }
-          void* const base = hc[hh] == 0 ? p.out[0] : hc[hh] == 1 ? p.out[1] : p.out[2];
+          const int dd = hh_[hh] / p.Hd, hl = hh_[hh] - dd * p.Hd;
+          void* base = nullptr;
+#pragma unroll
+          for (int k = 0; k < kMaxDest; ++k)  // constant indices: no local copy of the params
+            if (k == dd)
+              base = hc[hh] == 0 ? p.dest[k][0] : hc[hh] == 1 ? p.dest[k][1] : p.dest[k][2];
           char* const out_w = static_cast<char*>(base) +
-                              (((long long)b * p.H + hh_[hh]) * p.L + s0) * 256;
+                              (((long long)b * p.Hd + hl) * p.L + s0) * 256;
           store_half<kDt>(out_w, 256, nvalid, a, 16 * j, sm.stage[quarter], lane);
           store_half<kDt>(out_w, 256, nvalid, d, 64 + 16 * j, sm.stage[quarter], lane);
         }
@@ -446,11 +459,77 @@ int qkv_projection_launch(const AnimaQkvProjArgs* a, int* status, int sm_count, 
   prm.norm_mask = ((a->flags & ANIMA_FLAG_QNORM) ? 1u : 0u) | ((a->flags & ANIMA_FLAG_KNORM) ? 2u : 0u);
   prm.freqs = rope ? a->rope_freqs : nullptr;
   prm.eps = a->eps;
-  for (int c = 0; c < 3; ++c) prm.out[c] = outs[c];
+  prm.row0 = 0;
+  prm.Hd = a->H;
+  prm.n_dest = 1;
+  for (int d = 0; d < qkv::kMaxDest; ++d)
+    for (int c = 0; c < 3; ++c) prm.dest[d][c] = d == 0 ? outs[c] : nullptr;
   prm.status = status;
   const int grid = (int)(tiles < sm_count ? tiles : sm_count);
   prm.y = nullptr;
   prm.ldy = 0;
+  return a->dtype == ANIMA_DTYPE_BF16
+             ? qkv_launch_t<ANIMA_DTYPE_BF16, qkv::kEpiQkv>(ma, mb, prm, grid, st)
+             : qkv_launch_t<ANIMA_DTYPE_F16, qkv::kEpiQkv>(ma, mb, prm, grid, st);
+}
+
+// The projection of `rows` token rows (tokens row0 .. of the [B, L] grid) for all heads of a
+// head split over n_dest ranks (a->H heads each), each head's operand rows stored into the
+// buffers of the rank that owns the head: dest[d * 3 + c] is rank d's head-major
+// [B * a->H, L, 128] buffer of tensor c (q, k, v).  This is the projection GEMM and the
+// all-to-all of its output in one kernel.
+int qkv_projection_scatter_launch(const AnimaQkvProjArgs* a, int rows, int row0,
+                                  void* const* dest, int n_dest, int* status, int sm_count,
+                                  cudaStream_t st) {
+  if (a->dtype != ANIMA_DTYPE_F16 && a->dtype != ANIMA_DTYPE_BF16) return ANIMA_ERR_ARG;
+  if (a->B <= 0 || a->L <= 0 || a->H <= 0 || a->K <= 0 || rows <= 0 || row0 < 0)
+    return ANIMA_ERR_SHAPE;
+  if (a->L % 32 != 0 || a->K % 8 != 0 || row0 % 32 != 0) return ANIMA_ERR_SHAPE;
+  if ((long long)row0 + rows > (long long)a->B * a->L) return ANIMA_ERR_SHAPE;
+  if (n_dest < 1 || n_dest > qkv::kMaxDest || !dest) return ANIMA_ERR_ARG;
+  if (a->n_tensors < 1 || a->first_tensor < 0 || a->first_tensor + a->n_tensors > 3)
+    return ANIMA_ERR_ARG;
+  for (int d = 0; d < n_dest; ++d)
+    for (int c = a->first_tensor; c < a->first_tensor + a->n_tensors; ++c) {
+      const void* q = dest[d * 3 + c];
+      if (!q || (reinterpret_cast<uintptr_t>(q) & 15u)) return ANIMA_ERR_ARG;
+    }
+  if (!a->x || !a->w || ((reinterpret_cast<uintptr_t>(a->x) | reinterpret_cast<uintptr_t>(a->w)) & 15u))
+    return ANIMA_ERR_ARG;
+  const bool rope = (a->flags & ANIMA_FLAG_ROPE) != 0;
+  if (rope && (!a->rope_freqs || (reinterpret_cast<uintptr_t>(a->rope_freqs) & 15u)))
+    return ANIMA_ERR_ARG;
+  const long long H = (long long)a->H * n_dest;  // heads per tensor over all ranks
+  const long long N = (long long)a->n_tensors * H * 128;
+  if (N > 0x7fffffffLL) return ANIMA_ERR_SHAPE;
+  CUtensorMap ma, mb;
+  int rc;
+  if ((rc = make_rows_map(&ma, a->x, a->dtype, rows, a->K, qkv::kBM))) return rc;
+  if ((rc = make_rows_map(&mb, a->w, a->dtype, (int)N, a->K, qkv::kBN))) return rc;
+  qkv::Params prm;
+  memset(&prm, 0, sizeof(prm));
+  prm.M = rows;
+  prm.N = (int)N;
+  prm.K = a->K;
+  prm.L = a->L;
+  prm.H = (int)H;
+  prm.n_tiles_n = (int)((N + qkv::kBN - 1) / qkv::kBN);
+  const long long tiles = (long long)((rows + qkv::kBM - 1) / qkv::kBM) * prm.n_tiles_n;
+  if (tiles > 0x7fffffffLL) return ANIMA_ERR_SHAPE;
+  prm.n_tiles = (int)tiles;
+  prm.tensor0 = a->first_tensor;
+  prm.norm_w[0] = a->q_norm_w;
+  prm.norm_w[1] = a->k_norm_w;
+  prm.norm_mask = ((a->flags & ANIMA_FLAG_QNORM) ? 1u : 0u) | ((a->flags & ANIMA_FLAG_KNORM) ? 2u : 0u);
+  prm.freqs = rope ? a->rope_freqs : nullptr;
+  prm.eps = a->eps;
+  prm.row0 = row0;
+  prm.Hd = a->H;
+  prm.n_dest = n_dest;
+  for (int d = 0; d < n_dest; ++d)
+    for (int c = 0; c < 3; ++c) prm.dest[d][c] = dest[d * 3 + c];
+  prm.status = status;
+  const int grid = (int)(tiles < sm_count ? tiles : sm_count);
   return a->dtype == ANIMA_DTYPE_BF16
              ? qkv_launch_t<ANIMA_DTYPE_BF16, qkv::kEpiQkv>(ma, mb, prm, grid, st)
              : qkv_launch_t<ANIMA_DTYPE_F16, qkv::kEpiQkv>(ma, mb, prm, grid, st);

@@ -657,7 +657,7 @@ def sampler_run(model, x, cc, cu, args, dist, dev, steps):
 
 
 def dit_step_ms(args, rank, world, local_rank, dist, shard, profile=True, sampler_steps=0,
-                fused_qkv=True, peer_gather=True):
+                fused_qkv=True, peer_gather=True, peer_a2a=True):
     """One Euler+CFG step of the Anima DiT (config 4): latent 16x128x128 (4096 tokens), 28
     blocks, hidden 2048, 16 heads, CFG pair batched (B=2), sigma 0.5 -> 0, cfg 5; attention
     split by head over the ranks in the given layout.  fused_qkv: q/k/v projections through
@@ -679,7 +679,7 @@ def dit_step_ms(args, rank, world, local_rank, dist, shard, profile=True, sample
     else:
         weights = make_weights(cfg, seed=1234, device=dev, rng_device=dev)
     model = AnimaDiT(cfg, weights, rank=rank, world=world, group=group, shard=shard,
-                     fused_qkv=fused_qkv, peer_gather=peer_gather)
+                     fused_qkv=fused_qkv, peer_gather=peer_gather, peer_a2a=peer_a2a)
     del weights
     side = args.latent
     g = torch.Generator(device=dev).manual_seed(4321)
@@ -749,7 +749,11 @@ def dit_step_ms(args, rank, world, local_rank, dist, shard, profile=True, sample
                               else "cuBLAS GEMM + attention prologue"),
            "head_gather": (None if world == 1 or shard != "heads" else
                            "attention epilogue stores to every rank over NVLink + 1-element "
-                           "all-reduce" if model.peer_gather else "NCCL all_gather_into_tensor")}
+                           "all-reduce" if model.peer_gather else "NCCL all_gather_into_tensor"),
+           "all_to_all": (None if world == 1 or shard != "tokens" else
+                          "projection and attention epilogues store to the owning ranks over "
+                          "NVLink + 1-element all-reduces" if model.peer_a2a else
+                          "NCCL all_to_all_single x2 per attention")}
     torch.cuda.synchronize()
     model.close()
     del model
@@ -775,9 +779,11 @@ def run_dit_section(args, rank, world, local_rank, dist):
     if world == 1:  # the same step with the projections as cuBLAS GEMMs + the prologue
         out["heads_cublas_qkv"] = dit_step_ms(args, rank, world, local_rank, dist, "heads",
                                               fused_qkv=False)
-    else:  # the heads layout with the NCCL all-gather instead of the epilogue's peer stores
+    else:  # both layouts with NCCL collectives instead of the epilogues' peer stores
         out["heads_nccl_gather"] = dit_step_ms(args, rank, world, local_rank, dist, "heads",
                                                profile=False, peer_gather=False)
+        out["tokens_nccl_a2a"] = dit_step_ms(args, rank, world, local_rank, dist, "tokens",
+                                             profile=False, peer_a2a=False)
     out["ms"] = out["heads"]["ms"]
     return out
 

@@ -232,6 +232,29 @@ typedef struct AnimaQkvProjArgs {
 
 int anima_qkv_projection(const AnimaQkvProjArgs* args, void* stream);
 
+/* The two all-to-alls of a sequence-parallel attention, each folded into the kernel before
+ * it (the reference's step runs on one device and has no counterpart).  A rank owns token
+ * rows [r * rows, (r + 1) * rows) of the B x L grid for everything outside the attention and
+ * heads [r * H, (r + 1) * H) inside it; the other ranks' buffers are peer mappings
+ * (anima_ipc_open); the caller orders the ranks between the two kernels and after the
+ * second (e.g. a one-element NCCL all-reduce on the stream).
+ * anima_qkv_projection_scatter: args as for anima_qkv_projection with args->H the heads
+ *   per rank and args->B, args->L the whole token grid; x holds `rows` token rows starting
+ *   at global row `row0` (a multiple of 32), W all n_dest * H heads of each tensor.  The
+ *   operand rows of head g go to rank g / H: dest[d * 3 + c] is rank d's head-major
+ *   [B * H, L, 128] buffer of tensor c (q, k, v; only the computed tensors are read).
+ * anima_attn_fwd_scatter_rows: args as for anima_attn_fwd (args->out and out_stride unused;
+ *   S_q a multiple of 32); output row s of sample b is global row g = b * S_q + s and goes to
+ *   dest[g / rows_per_dest] at local row g % rows_per_dest (a multiple of 32), as the
+ *   columns of heads head0 .. head0 + H - 1 of a row-major buffer with dest_row_stride
+ *   elements per row.
+ * Asynchronous on `stream`. */
+int anima_qkv_projection_scatter(const AnimaQkvProjArgs* args, int rows, int row0,
+                                 void* const* dest, int n_dest, void* stream);
+int anima_attn_fwd_scatter_rows(const AnimaAttnArgs* args, void* const* dest, int n_dest,
+                                int rows_per_dest, int64_t dest_row_stride, int head0,
+                                void* stream);
+
 /* RoPE on device memory, for callers that apply it outside the fused prologue (replaces
  * predict2.apply_rotary_pos_emb, src/predict2.py:31-38, and the device side of
  * anima_rt_run_rope, anima_rt/include/cpu/rope_kernel.h:30-62, with the same arithmetic).
