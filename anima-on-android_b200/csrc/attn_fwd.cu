@@ -6,7 +6,7 @@
 //
 // Work unit = 256 query rows (two 128-row tiles) of one (batch, head) against its keys,
 // streamed in 128-key tiles.  Three schedules share one kernel (plan_split chooses):
-//   unit         one CTA per unit (masked / causal calls, calls of at most one wave that
+//   unit         one CTA per unit (causal calls, long masked units, calls of at most one wave that
 //                keep most SMs busy, and long units, where the hardware's dynamic hand-out
 //                of CTAs balances best);
 //   whole        a persistent grid of one CTA per SM.  Whole units are dealt round-robin
@@ -113,6 +113,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = sm.tmem_base;
+  // Launched as a programmatic dependent of the kernel before it on the stream (the
+  // prologue): the set-up above overlaps that kernel's tail; no global memory is touched
+  // before the previous grid has completed and its writes are visible.
+  grid_dependency_wait();
 
   if (warp >= 8) {
     regs_dec<kRegsControl>();
@@ -563,8 +567,24 @@ static int launch_t(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensor
       return ANIMA_ERR_CUDA;
     attr_dev_mask |= 1 << (dev & 31);
   }
-  kern<<<grid, attn::kThreads, attn::kSmemBytes, st>>>(mq, mk, mv, mo, prm);
-  return cudaGetLastError() == cudaSuccess ? ANIMA_OK : ANIMA_ERR_CUDA;
+  // Programmatic dependent launch: the CTAs may start (barriers, TMEM, descriptor
+  // prefetch) while the previous kernel on the stream drains; the kernel waits for it
+  // (griddepcontrol.wait) before its first global access.
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)grid);
+  cfg.blockDim = dim3(attn::kThreads);
+  cfg.dynamicSmemBytes = attn::kSmemBytes;
+  cfg.stream = st;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+  if (cudaLaunchKernelEx(&cfg, kern, mq, mk, mv, mo, prm) != cudaSuccess) {
+    cudaGetLastError();
+    return ANIMA_ERR_CUDA;
+  }
+  return ANIMA_OK;
 }
 
 // Schedule of a call: one CTA per unit, or a persistent grid of whole-unit rounds, or
@@ -581,11 +601,24 @@ static SplitPlan plan_split(int bh, int S_q, int S_kv, unsigned flags, int sm_co
                             bool allow_cut = true) {
   const int bn = (flags & ANIMA_FLAG_KV64) ? 64 : attn::kBN;
   SplitPlan sp = {kSchedUnit, 0, 0, 0, 0, 0};
-  if (flags & (ANIMA_FLAG_MASK | ANIMA_FLAG_CAUSAL | ANIMA_FLAG_UNIT) || sm_count < 2)
-    return sp;  // masked / causal units differ in length: the hardware balances them
+  if (flags & (ANIMA_FLAG_CAUSAL | ANIMA_FLAG_UNIT) || sm_count < 2)
+    return sp;  // causal units differ in length along the diagonal: the hardware balances them
   const long long units = (long long)bh * ((S_q + attn::kUnitRows - 1) / attn::kUnitRows);
   const long long n = (S_kv + attn::kBN - 1) / attn::kBN;
   if (units > 0x7fffffffLL) return sp;
+  if (flags & ANIMA_FLAG_MASK) {
+    // Key-padding masks shorten every unit of a sample alike (the DiT's cross-attention:
+    // 512 context keys, 4 tiles, fewer when padded).  Short units pay their start-up
+    // (TMEM allocation, barriers, the first loads) once per unit in one-CTA-per-unit mode,
+    // so calls of more than one wave of units of at most 16 key tiles run persistent whole
+    // units (never cut: the cut's slices assume every unit has n tiles).  Longer masked
+    // units keep one CTA per unit, which balances units of different lengths.
+    if ((flags & ANIMA_FLAG_KV64) || units <= sm_count) return sp;
+    if (n > 16 && !(flags & ANIMA_FLAG_WHOLE)) return sp;
+    sp.mode = kSchedWhole;
+    sp.rounds = (int)((units + sm_count - 1) / sm_count);
+    return sp;
+  }
   const long long rounds = units / sm_count, tail = units - rounds * sm_count;
   // Cutting the last round saves the idle share of the unit grid's last wave, (sm - tail)/sm
   // of one unit's time, and costs segment set-up, partial stores and merges, which do not

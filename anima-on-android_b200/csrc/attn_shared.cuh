@@ -92,9 +92,11 @@ __device__ __forceinline__ int unit_kv_len(const Params& p, int unit) {
   return kv_len;
 }
 // kBN: keys per key tile of the calling kernel.
+// In split mode (persistent grid) a unit has p.n_kv key tiles, or fewer when its sample's
+// keys are masked (masked calls run whole units only, never cut).
 template <int kBN>
 __device__ __forceinline__ int unit_tiles(const Params& p, int unit) {
-  if (p.split) return p.n_kv;
+  if (p.split && !(p.flags & ANIMA_FLAG_MASK)) return p.n_kv;
   int n = (unit_kv_len(p, unit) + kBN - 1) / kBN;
   if (p.flags & ANIMA_FLAG_CAUSAL) {
     const int q0 = (unit % p.nqb) * kUnitRows;
@@ -138,7 +140,7 @@ struct SegIter {
       ++r;
       if (s.unit < p.units) {
         s.k0 = 0;
-        s.k1 = n;
+        s.k1 = unit_tiles<kBN>(p, s.unit);
         s.full = 1;
         s.slot = 0;
         return true;

@@ -428,6 +428,19 @@ __device__ __forceinline__ void umma_commit_pair(uint64_t* bar, uint16_t cta_mas
       : "memory");
 }
 
+// ---------------------------------------------------------------- programmatic dependent launch
+// Waits until the grids this one depends on (launched before it on the stream) have
+// completed and their memory operations are visible; returns at once without such a
+// dependency.
+__device__ __forceinline__ void grid_dependency_wait() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+// Lets the dependent grid (the next kernel on the stream, when launched as a programmatic
+// dependent) start its CTAs once every CTA of this grid has issued this or exited.
+__device__ __forceinline__ void grid_dependents_launch() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 // ---------------------------------------------------------------- register budget
 // Per-warpgroup register reconfiguration; every warp of the warpgroup executes it.
 template <uint32_t kRegs>

@@ -115,6 +115,9 @@ __global__ void __launch_bounds__(256, sizeof(Tin) == 4 ? 3 : 2) prologue_kernel
   const long long warp0 = ((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const long long nwarps = ((long long)gridDim.x * blockDim.x) >> 5;
   const long long total = p.tokens_q + 2 * p.tokens_k;
+  // The attention kernel that follows may begin its set-up; it reads nothing of ours
+  // before this grid has completed.
+  grid_dependents_launch();
 
   for (long long item = warp0; item < total; item += nwarps) {
     int t;
@@ -304,6 +307,7 @@ __global__ void __launch_bounds__(256, sizeof(Tin) == 4 ? 3 : 2)
   const long long warp0 = ((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const long long nwarps = ((long long)gridDim.x * blockDim.x) >> 5;
   const long long total = items_q + 2 * items_k;
+  grid_dependents_launch();  // as in prologue_kernel
 
   for (long long item = warp0; item < total; item += nwarps) {
     int t;

@@ -104,11 +104,13 @@ typedef struct AnimaPrologueArgs {
  *   [B, S_q, H, D] (feeds the o-proj):     {S_q*H*D, D, H*D}
  * kv_valid_len: device int32 [B], used with ANIMA_FLAG_MASK (keys >= valid are masked;
  * a sample with 0 valid keys gets a zero output).
- * Schedule: a call of at most one wave of 256-row units, or a masked or causal call,
- * launches one CTA per unit.  Otherwise the kernel runs persistently, one CTA per SM taking
- * whole units round-robin, which saves the per-CTA start-up and pipeline drain of every
- * unit; where it measured faster, the last partial round is also cut into equal slices of
- * key tiles whose fp32 partials are merged in-kernel, which needs the workspace.
+ * Schedule: a call of at most one wave of 256-row units, or a causal call, launches one
+ * CTA per unit.  Otherwise the kernel runs persistently, one CTA per SM taking whole units
+ * round-robin, which saves the per-CTA start-up and pipeline drain of every unit; where it
+ * measured faster, the last partial round is also cut into equal slices of key tiles whose
+ * fp32 partials are merged in-kernel, which needs the workspace.  Masked calls run whole
+ * units persistently when their units have at most 16 key tiles (cross-attention into a
+ * padded text context), else one CTA per unit; they are never cut.
  * workspace: optional device scratch of workspace_bytes, 256-byte aligned, ZERO-FILLED
  * before its first use; anima_attn_workspace_size() gives the size the cut needs (0 when
  * the call does not cut).  Without it the call runs whole units only.  The kernel leaves

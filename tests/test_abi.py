@@ -120,6 +120,10 @@ SCHEDULES = [
     (2048, 2048, L.FLAG_SPLIT, "cut"), (8192, 8192, L.FLAG_SPLIT, "cut"),
     (4096, 4096, L.FLAG_PAIR, "unit"), (4096, 4096, L.FLAG_KV64, "cut"),
     (4096, 512, L.FLAG_KV64, "whole"),
+    (4096, 512, L.FLAG_MASK, "whole"), (4096, 2048, L.FLAG_MASK, "whole"),  # cross-attention
+    (4096, 512, L.FLAG_MASK | L.FLAG_SPLIT, "whole"),  # masked calls are never cut
+    (4096, 4096, L.FLAG_MASK | L.FLAG_WHOLE, "whole"), (1024, 512, L.FLAG_MASK, "unit"),
+    (4096, 512, L.FLAG_MASK | L.FLAG_KV64, "unit"),
 ]
 SCHED_CODE = {"unit": 0, "whole": 1, "cut": 2}
 

@@ -253,6 +253,33 @@ def test_masked_cross_attention(aa, O):
     _ok(got, ref)
 
 
+def test_masked_persistent_whole_units_match_unit_mode_and_oracle(aa, O):
+    """Masked calls of more than one wave of short units run persistent whole units: here
+    6 x 16 heads x 4 units of 250 rows against 512 keys (384 units on 148 SMs), valid
+    lengths 0 (zero output), 1, 77, 128, 129 and 512 -- units of 0 to 4 key tiles dealt
+    round-robin -- against one CTA per unit and the oracle."""
+    from anima_attn import _lib as L
+    rng = np.random.default_rng(23)
+    B, H, Sq, Skv = 6, 16, 1000, 512
+    assert L.lib.anima_attn_schedule(B, H, Sq, Skv, L.FLAG_MASK, 0) == L.SCHED_WHOLE
+    q = rng.standard_normal((B, H, Sq, 128), dtype=np.float32)
+    k = rng.standard_normal((B, H, Skv, 128), dtype=np.float32)
+    v = rng.standard_normal((B, H, Skv, 128), dtype=np.float32)
+    valid = np.array([0, 1, 77, 128, 129, 512], dtype=np.int32)
+    qh, kh, vh = (_dev(t).reshape(B * H, -1, 128).to(torch.bfloat16) for t in (q, k, v))
+    dvalid = _dev(valid)
+    got = aa.attention_core(qh, kh, vh, B, H, kv_valid_len=dvalid, out_layout="bhsd")
+    one = aa.attention_core(qh, kh, vh, B, H, kv_valid_len=dvalid, out_layout="bhsd",
+                            schedule="unit")
+    torch.cuda.synchronize()
+    assert aa.status() == 0
+    g = got.cpu().numpy()
+    assert not g[0].any()
+    assert np.array_equal(g, one.cpu().numpy())  # same tiles in the same order per row
+    ref = O.sdpa_varlen(q, k, v, valid, threads=16)
+    _ok(g, ref)
+
+
 @pytest.mark.parametrize("Sq,Skv", [(1300, 700), (4000, 3000), (1280, 128), (4096, 4096)])
 def test_schedules_match_each_other_and_oracle(aa, O, Sq, Skv):
     """More than one wave of 256-row units (B*H*ceil(Sq/256) > 148 SMs) in all three
