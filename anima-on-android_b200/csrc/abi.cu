@@ -8,10 +8,20 @@
 //    kernels on the library's stream, copies the result back and synchronises.
 //    Calls are serialised by one mutex (one workspace); like the reference they are
 //    safe to call from several threads.
+#include <sched.h>
+
+#include <algorithm>
+#include <atomic>
+#include <chrono>
+#include <condition_variable>
+#include <cstdlib>
 #include <cstring>
+#include <functional>
 #include <initializer_list>
 #include <mutex>
 #include <string>
+#include <thread>
+#include <vector>
 
 #include "anima_rt.h"
 #include "common.cuh"
@@ -161,6 +171,22 @@ const char* code_name(int rc) {
 
 // ---------------------------------------------------------------- anima_rt state
 constexpr int kRtMaxChunks = 64;
+// Page-locked staging of pageable caller arrays (see "host staging" below): slots of
+// kStageSlot bytes, kStageIn of them for host->device pieces, kStageOut for device->host.
+// Measured at B=2, H=16, L=4096 (16 host threads, pageable fp32 arrays in and out):
+// 4 MiB x (6 + 4) slots 5.2-5.3 ms per anima_rt_run_attention call; 2 MiB x (6 + 4) 6.8,
+// 2 MiB x (12 + 6) 5.7, 4 MiB x (12 + 6) 6.2, 8 MiB x (6 + 4) 6.3, 1 MiB x (16 + 8) 6.6;
+// the driver's own pageable copies 24.2.
+#ifndef ANIMA_STAGE_SLOT_MB
+#define ANIMA_STAGE_SLOT_MB 4
+#endif
+constexpr size_t kStageSlot = size_t(ANIMA_STAGE_SLOT_MB) << 20;
+#ifndef ANIMA_STAGE_IN
+#define ANIMA_STAGE_IN 6
+#define ANIMA_STAGE_OUT 4
+#endif
+constexpr int kStageIn = ANIMA_STAGE_IN, kStageOut = ANIMA_STAGE_OUT;
+constexpr int kStageSlots = kStageIn + kStageOut;
 struct RtState {
   bool inited = false;
   cudaStream_t stream = nullptr;          // kernels
@@ -169,6 +195,9 @@ struct RtState {
   void* ws = nullptr;
   size_t ws_bytes = 0;
   int device = -1;
+  char* ring = nullptr;                      // kStageSlots * kStageSlot page-locked bytes
+  cudaEvent_t ev_slot[kStageSlots] = {};     // last copy that used each slot
+  unsigned next_in = 0, next_out = 0;        // round-robin slot counters
 };
 RtState g_rt;
 std::recursive_mutex g_rt_mu;
@@ -195,6 +224,10 @@ bool rt_prepare(size_t bytes) {
       if (g_rt.ev_done[c]) cudaEventDestroy(g_rt.ev_done[c]);
       g_rt.ev_in[c] = g_rt.ev_done[c] = nullptr;
     }
+    for (cudaEvent_t& e : g_rt.ev_slot) {
+      if (e) cudaEventDestroy(e);
+      e = nullptr;
+    }
     g_rt.ws = nullptr;
     g_rt.ws_bytes = 0;
     g_rt.device = -1;
@@ -206,6 +239,11 @@ bool rt_prepare(size_t bytes) {
     for (int c = 0; c < kRtMaxChunks; ++c)
       if (cudaEventCreateWithFlags(&g_rt.ev_in[c], cudaEventDisableTiming) != cudaSuccess ||
           cudaEventCreateWithFlags(&g_rt.ev_done[c], cudaEventDisableTiming) != cudaSuccess) {
+        cudaGetLastError();
+        return rt_fail("cudaEventCreate failed");
+      }
+    for (cudaEvent_t& e : g_rt.ev_slot)
+      if (cudaEventCreateWithFlags(&e, cudaEventDisableTiming) != cudaSuccess) {
         cudaGetLastError();
         return rt_fail("cudaEventCreate failed");
       }
@@ -246,6 +284,211 @@ bool rt_finish(const char* what) {
   return true;
 }
 
+// ---------------------------------------------------------------- host staging
+// The reference's callers pass ordinary (pageable) numpy arrays.  The CUDA driver copies
+// pageable memory through its own bounce buffer on the calling thread, about 10 GB/s
+// here, and a device->host copy into pageable memory does not return before the copy is
+// done, which stalls the chunk pipeline.  Large pageable arrays are therefore copied
+// through the library's page-locked ring instead: host threads gather a piece of rows
+// into a slot while the copy engine moves the previous slots, and device->host pieces
+// land in slots that the threads scatter into the caller's array.  Page-locked (and
+// device) pointers keep the direct copies.  ANIMA_RT_STAGE=0 turns the staging off.
+
+// Persistent host threads for the gathers and scatters.  run(fn) calls fn(t, T) for
+// t = 0..T-1 on T threads, the caller being thread 0, and returns when all are done.
+// Between jobs a worker spins for up to kSpinUs before it sleeps on the condition
+// variable: the pieces of one call follow each other within microseconds, and a sleeping
+// thread takes tens of microseconds to wake.
+class CopyPool {
+ public:
+  static CopyPool& get() {
+    static CopyPool* pool = new CopyPool();  // never destroyed: idle workers end with the process
+    return *pool;
+  }
+  void run(const std::function<void(int, int)>& fn) {
+    if (nworkers_ == 0) {
+      fn(0, 1);
+      return;
+    }
+    job_.store(&fn, std::memory_order_relaxed);
+    pending_.store(nworkers_, std::memory_order_relaxed);
+    {
+      std::lock_guard<std::mutex> lk(mu_);  // a worker about to sleep sees the new generation
+      gen_.fetch_add(1, std::memory_order_release);
+    }
+    cv_.notify_all();
+    fn(0, nworkers_ + 1);
+    while (pending_.load(std::memory_order_acquire) != 0) std::this_thread::yield();
+  }
+
+ private:
+  static constexpr int kSpinUs = 2000;
+  CopyPool() {
+    int n = 1;
+    cpu_set_t set;
+    if (sched_getaffinity(0, sizeof(set), &set) == 0) n = CPU_COUNT(&set);
+    if (const char* e = std::getenv("ANIMA_RT_COPY_THREADS")) n = std::atoi(e);
+    n = std::max(1, std::min(n, 16));
+    nworkers_ = n - 1;
+    for (int i = 0; i < nworkers_; ++i) std::thread([this, i] { work(i + 1); }).detach();
+  }
+  void work(int id) {
+    unsigned long seen = 0;
+    for (;;) {
+      unsigned long g;
+      const auto t0 = std::chrono::steady_clock::now();
+      while ((g = gen_.load(std::memory_order_acquire)) == seen) {
+        if (std::chrono::steady_clock::now() - t0 > std::chrono::microseconds(kSpinUs)) {
+          std::unique_lock<std::mutex> lk(mu_);
+          cv_.wait(lk, [&] { return gen_.load(std::memory_order_acquire) != seen; });
+        }
+      }
+      seen = g;
+      (*job_.load(std::memory_order_relaxed))(id, nworkers_ + 1);
+      pending_.fetch_sub(1, std::memory_order_acq_rel);
+    }
+  }
+  std::mutex mu_;
+  std::condition_variable cv_;
+  std::atomic<const std::function<void(int, int)>*> job_{nullptr};
+  std::atomic<unsigned long> gen_{0};
+  std::atomic<int> pending_{0};
+  int nworkers_ = 0;
+};
+
+bool staging_enabled() {
+  const char* e = std::getenv("ANIMA_RT_STAGE");
+  return !(e && e[0] == '0');
+}
+
+// True for memory the copy engine reads without the driver's bounce buffer: page-locked
+// host memory (cudaHostAlloc, cudaHostRegister, torch's pin_memory) and device memory.
+bool direct_copyable(const void* p) {
+  cudaPointerAttributes a;
+  if (cudaPointerGetAttributes(&a, p) != cudaSuccess) {
+    cudaGetLastError();
+    return false;
+  }
+  return a.type != cudaMemoryTypeUnregistered;
+}
+
+// Copies below this size go straight to the driver; the ring pays off above it.
+constexpr size_t kStageMin = size_t(1) << 20;
+static_assert(kStageSlot >= kStageMin, "a staged copy fills at least one row per slot");
+
+bool stage_ring() {
+  if (g_rt.ring) return true;
+  void* p = nullptr;
+  if (cudaHostAlloc(&p, kStageSlots * kStageSlot, cudaHostAllocPortable) != cudaSuccess) {
+    cudaGetLastError();
+    return rt_fail("cudaHostAlloc of the staging ring failed");
+  }
+  g_rt.ring = static_cast<char*>(p);
+  return true;
+}
+
+// rows x width bytes with pitches: rows [r0, r0+n) of src to the packed buffer dst, or
+// the packed buffer src to rows of dst, split over the copy threads.
+void copy_rows(char* dst, size_t dpitch, const char* src, size_t spitch, size_t width, size_t n) {
+  CopyPool::get().run([&](int t, int T) {
+    if (dpitch == width && spitch == width) {  // contiguous: split by bytes
+      const size_t total = width * n, lo = total * t / T, hi = total * (t + 1) / T;
+      if (hi > lo) std::memcpy(dst + lo, src + lo, hi - lo);
+      return;
+    }
+    const size_t lo = n * t / T, hi = n * (t + 1) / T;
+    for (size_t r = lo; r < hi; ++r) std::memcpy(dst + r * dpitch, src + r * spitch, width);
+  });
+}
+
+// Host -> device copy of `rows` rows of `width` bytes (pitches in bytes) on stream s.
+// Asynchronous for the caller's array as soon as it returns: every row has been read.
+bool h2d_rows(char* dst, size_t dpitch, const char* src, size_t spitch, size_t width,
+              size_t rows, cudaStream_t s, bool direct, const char* who) {
+  if (!rows || !width) return true;
+  if (direct || !staging_enabled() || width * rows < kStageMin || width > kStageSlot)
+    return rt_check(cudaMemcpy2DAsync(dst, dpitch, src, spitch, width, rows,
+                                      cudaMemcpyHostToDevice, s), who);
+  if (!stage_ring()) return false;
+  const size_t per = kStageSlot / width;
+  for (size_t r0 = 0; r0 < rows; r0 += per) {
+    const size_t n = std::min(per, rows - r0);
+    const int slot = (int)(g_rt.next_in++ % kStageIn);
+    char* buf = g_rt.ring + slot * kStageSlot;
+    // the slot's previous host->device copy has read it
+    if (!rt_check(cudaEventSynchronize(g_rt.ev_slot[slot]), who)) return false;
+    copy_rows(buf, width, src + r0 * spitch, spitch, width, n);
+    if (!rt_check(cudaMemcpy2DAsync(dst + r0 * dpitch, dpitch, buf, width, width, n,
+                                    cudaMemcpyHostToDevice, s), who) ||
+        !rt_check(cudaEventRecord(g_rt.ev_slot[slot], s), who))
+      return false;
+  }
+  return true;
+}
+
+// Device -> host copy of rows on stream s (after whatever s already waits for).  A direct
+// copy is only enqueued; a staged one has landed in `dst` when this returns.
+bool d2h_rows(char* dst, size_t dpitch, const char* src, size_t spitch, size_t width,
+              size_t rows, cudaStream_t s, bool direct, const char* who) {
+  if (!rows || !width) return true;
+  if (direct || !staging_enabled() || width * rows < kStageMin || width > kStageSlot)
+    return rt_check(cudaMemcpy2DAsync(dst, dpitch, src, spitch, width, rows,
+                                      cudaMemcpyDeviceToHost, s), who);
+  if (!stage_ring()) return false;
+  const size_t per = kStageSlot / width;
+  struct Piece { int slot; size_t r0, n; };
+  Piece q[kStageOut];
+  int head = 0, count = 0;
+  auto scatter_oldest = [&]() {
+    const Piece& p = q[head];
+    if (!rt_check(cudaEventSynchronize(g_rt.ev_slot[kStageIn + p.slot]), who)) return false;
+    copy_rows(dst + p.r0 * dpitch, dpitch, g_rt.ring + (kStageIn + p.slot) * kStageSlot,
+              width, width, p.n);
+    head = (head + 1) % kStageOut;
+    --count;
+    return true;
+  };
+  // Up to kStageOut - 1 pieces in flight: the slot a new piece takes was scattered.
+  for (size_t r0 = 0; r0 < rows; r0 += per) {
+    if (count == kStageOut - 1 && !scatter_oldest()) return false;
+    const size_t n = std::min(per, rows - r0);
+    const int slot = (int)(g_rt.next_out++ % kStageOut);
+    if (!rt_check(cudaMemcpy2DAsync(g_rt.ring + (kStageIn + slot) * kStageSlot, width,
+                                    src + r0 * spitch, spitch, width, n,
+                                    cudaMemcpyDeviceToHost, s), who) ||
+        !rt_check(cudaEventRecord(g_rt.ev_slot[kStageIn + slot], s), who))
+      return false;
+    q[(head + count) % kStageOut] = Piece{slot, r0, n};
+    ++count;
+  }
+  while (count > 0)
+    if (!scatter_oldest()) return false;
+  return true;
+}
+
+// A contiguous buffer as rows of 256 KiB (and a direct tail).
+constexpr size_t kStageRow = size_t(256) << 10;
+bool h2d_bytes(void* dst, const void* src, size_t n, cudaStream_t s, const char* who) {
+  const bool direct = n < kStageMin || direct_copyable(src);
+  const size_t rows = direct ? 0 : n / kStageRow, body = rows * kStageRow;
+  if (!h2d_rows(static_cast<char*>(dst), kStageRow, static_cast<const char*>(src), kStageRow,
+                kStageRow, rows, s, false, who))
+    return false;
+  return n == body || rt_check(cudaMemcpyAsync(static_cast<char*>(dst) + body,
+                                               static_cast<const char*>(src) + body, n - body,
+                                               cudaMemcpyHostToDevice, s), who);
+}
+bool d2h_bytes(void* dst, const void* src, size_t n, cudaStream_t s, const char* who) {
+  const bool direct = n < kStageMin || direct_copyable(dst);
+  const size_t rows = direct ? 0 : n / kStageRow, body = rows * kStageRow;
+  if (!d2h_rows(static_cast<char*>(dst), kStageRow, static_cast<const char*>(src), kStageRow,
+                kStageRow, rows, s, false, who))
+    return false;
+  return n == body || rt_check(cudaMemcpyAsync(static_cast<char*>(dst) + body,
+                                               static_cast<const char*>(src) + body, n - body,
+                                               cudaMemcpyDeviceToHost, s), who);
+}
+
 // One host buffer of a compatibility call (nullptr host: an absent optional input).
 struct RtBuf {
   const void* host;
@@ -283,9 +526,7 @@ bool rt_call(const char* who, std::initializer_list<RtBuf> ins, void* out, size_
   for (const RtBuf& b : ins) {
     if (b.host) {
       dev_in[n] = ws + offs[n];
-      if (b.bytes &&
-          !rt_check(cudaMemcpyAsync(ws + offs[n], b.host, b.bytes, cudaMemcpyHostToDevice, st), who))
-        return bail();
+      if (b.bytes && !h2d_bytes(ws + offs[n], b.host, b.bytes, st, who)) return bail();
     }
     ++n;
   }
@@ -297,8 +538,7 @@ bool rt_call(const char* who, std::initializer_list<RtBuf> ins, void* out, size_
     rt_fail(std::string(who) + ": " + code_name(rc));
     return bail();
   }
-  if (!rt_check(cudaMemcpyAsync(out, ws + o_out, out_bytes, cudaMemcpyDeviceToHost, st), who))
-    return bail();
+  if (!d2h_bytes(out, ws + o_out, out_bytes, st, who)) return bail();
   return rt_finish(who);
 }
 
@@ -368,23 +608,45 @@ bool rt_attention(const float* q, const float* k, const float* v, const float* q
     return bail();
   if (k_w && !rt_check(cudaMemcpyAsync(dw + D, k_w, D * 4, cudaMemcpyHostToDevice, sin), who))
     return bail();
-  if (freqs && !rt_check(cudaMemcpyAsync(ws + o_f, freqs, (size_t)S_q * D * 2 * 4,
-                                         cudaMemcpyHostToDevice, sin), who))
-    return bail();
+  if (freqs && !h2d_bytes(ws + o_f, freqs, (size_t)S_q * D * 2 * 4, sin, who)) return bail();
   if (kv_valid && !rt_check(cudaMemcpyAsync(ws + o_valid, kv_valid, (size_t)B * 4,
                                             cudaMemcpyHostToDevice, sin), who))
     return bail();
   const size_t row = (size_t)H * D * 4, crow = (size_t)G * D * 4;  // bytes: pitch, chunk row
+  // Pageable arrays go through the staging ring (h2d_rows / d2h_rows).  A staged output
+  // chunk is collected one chunk late, after the next chunk's inputs are on their way,
+  // so the scatter into `out` overlaps the copy engine's host->device work.
+  const bool q_direct = direct_copyable(q), k_direct = direct_copyable(k),
+             v_direct = direct_copyable(v), out_direct = direct_copyable(out);
+  const bool out_staged = !out_direct && staging_enabled();
+  auto chunk_geom = [&](int c, int& bn, size_t& qo, size_t& ko) {
+    const int b0 = (c / ng) * Bc, h0 = (c % ng) * G;
+    bn = min(Bc, B - b0);
+    qo = ((size_t)b0 * S_q * H + h0) * D;
+    ko = ((size_t)b0 * S_kv * H + h0) * D;
+  };
+  auto copy_out = [&](int c) {  // after chunk c's kernels
+    int bn;
+    size_t qo, ko;
+    chunk_geom(c, bn, qo, ko);
+    if (!rt_check(cudaStreamWaitEvent(sout, g_rt.ev_done[c], 0), who)) return false;
+    return d2h_rows(reinterpret_cast<char*>(out + qo), row,
+                    reinterpret_cast<const char*>(dout + qo), row, crow, (size_t)bn * S_q, sout,
+                    out_direct, who);
+  };
   for (int c = 0; c < nchunks; ++c) {
-    const int b0 = (c / ng) * Bc, h0 = (c % ng) * G, bn = min(Bc, B - b0);
+    const int b0 = (c / ng) * Bc;
+    int bn;
+    size_t qo, ko;
+    chunk_geom(c, bn, qo, ko);
     // ---- copy in
-    const size_t qo = ((size_t)b0 * S_q * H + h0) * D, ko = ((size_t)b0 * S_kv * H + h0) * D;
-    if (!rt_check(cudaMemcpy2DAsync(dq + qo, row, q + qo, row, crow, (size_t)bn * S_q,
-                                    cudaMemcpyHostToDevice, sin), who) ||
-        !rt_check(cudaMemcpy2DAsync(dk + ko, row, k + ko, row, crow, (size_t)bn * S_kv,
-                                    cudaMemcpyHostToDevice, sin), who) ||
-        !rt_check(cudaMemcpy2DAsync(dv + ko, row, v + ko, row, crow, (size_t)bn * S_kv,
-                                    cudaMemcpyHostToDevice, sin), who) ||
+    auto in = [&](float* d, const float* h, size_t off, int S, bool direct) {
+      return h2d_rows(reinterpret_cast<char*>(d + off), row,
+                      reinterpret_cast<const char*>(h + off), row, crow, (size_t)bn * S, sin,
+                      direct, who);
+    };
+    if (!in(dq, q, qo, S_q, q_direct) || !in(dk, k, ko, S_kv, k_direct) ||
+        !in(dv, v, ko, S_kv, v_direct) ||
         !rt_check(cudaEventRecord(g_rt.ev_in[c], sin), who) ||
         !rt_check(cudaStreamWaitEvent(st, g_rt.ev_in[c], 0), who))
       return bail();
@@ -448,13 +710,15 @@ bool rt_attention(const float* q, const float* k, const float* v, const float* q
       rt_fail(std::string(who) + ": attention: " + code_name(rc));
       return bail();
     }
-    // ---- copy out
-    if (!rt_check(cudaEventRecord(g_rt.ev_done[c], st), who) ||
-        !rt_check(cudaStreamWaitEvent(sout, g_rt.ev_done[c], 0), who) ||
-        !rt_check(cudaMemcpy2DAsync(out + qo, row, dout + qo, row, crow, (size_t)bn * S_q,
-                                    cudaMemcpyDeviceToHost, sout), who))
+    // ---- copy out (a staged chunk one chunk late)
+    if (!rt_check(cudaEventRecord(g_rt.ev_done[c], st), who)) return bail();
+    if (!out_staged) {
+      if (!copy_out(c)) return bail();
+    } else if (c > 0 && !copy_out(c - 1)) {
       return bail();
+    }
   }
+  if (out_staged && !copy_out(nchunks - 1)) return bail();
   if (!rt_check(cudaStreamSynchronize(sout), who)) return bail();
   return rt_finish(who);
 }

@@ -440,13 +440,24 @@ def run_ours(args, rank, world, local_rank, dist):
         e2e = {"value": flops_rank * world / s / 1e12, "unit": UNIT, "h2d_bytes_per_step": h2d,
                "d2h_bytes_per_step": pout.numel() * 4, "ms_per_step": s * 1e3, "steps": n,
                "path": "anima_rt_run_attention (C ABI, page-locked host buffers, wall clock)"}
-        s, n = timed((q.ctypes.data, k.ctypes.data, v.ctypes.data, qw.ctypes.data,
-                      kw.ctypes.data, nf.ctypes.data), nout.ctypes.data)
+        host_ptrs = (q.ctypes.data, k.ctypes.data, v.ctypes.data, qw.ctypes.data,
+                     kw.ctypes.data, nf.ctypes.data)
+        s, n = timed(host_ptrs, nout.ctypes.data)
+        # the same call with the library's page-locked staging ring turned off: the CUDA
+        # driver's own pageable copies
+        os.environ["ANIMA_RT_STAGE"] = "0"
+        try:
+            s_drv, _ = timed(host_ptrs, nout.ctypes.data)
+        finally:
+            os.environ.pop("ANIMA_RT_STAGE", None)
         e2e_pageable = {"value": flops_rank * world / s / 1e12, "unit": UNIT,
                         "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": nout.nbytes,
                         "ms_per_step": s * 1e3, "steps": n,
+                        "driver_copies": {"value": flops_rank * world / s_drv / 1e12,
+                                          "ms_per_step": s_drv * 1e3},
                         "path": "anima_rt_run_attention (C ABI, pageable numpy arrays, as the "
-                                "reference's callers pass them; wall clock)"}
+                                "reference's callers pass them, copied through the library's "
+                                "page-locked staging ring; wall clock)"}
 
     peaks = load_peaks()
     achieved = flops_rank / (att_ms * 1e-3) / 1e12

@@ -97,7 +97,11 @@ bool anima_rt_run_gemm_bf16(const float* A, const uint16_t* W, float* C, int M, 
  * SDPA and the transposes.  q [B, S_q, H, D], k/v [B, S_kv, H, D], out [B, S_q, H, D],
  * all fp32 host memory.  kv_valid (host int32 [B], may be NULL) masks keys >= kv_valid[b].
  * flags: 1 = q norm, 2 = k norm, 4 = RoPE, 16 = causal (bit values of ANIMA_FLAG_*).
- * Host buffers in page-locked memory make the copies run at full PCIe speed. */
+ * Host buffers in page-locked memory are copied by the copy engine directly (full PCIe
+ * speed).  Ordinary pageable arrays above 1 MiB are copied through the library's own
+ * page-locked ring by up to 16 host threads (ANIMA_RT_COPY_THREADS; ANIMA_RT_STAGE=0
+ * leaves them to the CUDA driver's single-threaded copies); the same holds for the
+ * other host entries above. */
 bool anima_rt_run_attention(const float* q, const float* k, const float* v, const float* q_w,
                             const float* k_w, const float* freqs, const int* kv_valid,
                             float* out, int B, int S_q, int S_kv, int H, int D, float eps,
