@@ -9,6 +9,7 @@
 //    Calls are serialised by one mutex (one workspace); like the reference they are
 //    safe to call from several threads.
 #include <sched.h>
+#include <unistd.h>
 
 #include <algorithm>
 #include <atomic>
@@ -306,7 +307,7 @@ class CopyPool {
     return *pool;
   }
   void run(const std::function<void(int, int)>& fn) {
-    if (nworkers_ == 0) {
+    if (nworkers_ == 0 || getpid() != pid_) {  // a forked child has no workers
       fn(0, 1);
       return;
     }
@@ -330,6 +331,7 @@ class CopyPool {
     if (const char* e = std::getenv("ANIMA_RT_COPY_THREADS")) n = std::atoi(e);
     n = std::max(1, std::min(n, 16));
     nworkers_ = n - 1;
+    pid_ = getpid();
     for (int i = 0; i < nworkers_; ++i) std::thread([this, i] { work(i + 1); }).detach();
   }
   void work(int id) {
@@ -354,6 +356,7 @@ class CopyPool {
   std::atomic<unsigned long> gen_{0};
   std::atomic<int> pending_{0};
   int nworkers_ = 0;
+  pid_t pid_ = 0;
 };
 
 bool staging_enabled() {
@@ -566,8 +569,33 @@ bool rt_attention(const float* q, const float* k, const float* v, const float* q
   constexpr int kGroups = 2;
   const int G = (H % kGroups == 0) ? H / kGroups : H;       // heads per chunk
   int Bc = (B * (H / G) <= 8) ? 1 : (B * (H / G) + 7) / 8;  // batch rows per chunk
-  while ((B + Bc - 1) / Bc * (H / G) > kRtMaxChunks) ++Bc;
-  const int nb = (B + Bc - 1) / Bc, ng = H / G, nchunks = nb * ng;
+  while ((B + Bc - 1) / Bc * (H / G) > kRtMaxChunks - 2) ++Bc;
+  const int nb = (B + Bc - 1) / Bc, ng = H / G;
+  // Pageable arrays go through the staging ring (h2d_rows / d2h_rows).  A staged output
+  // chunk is collected one chunk late, after the next chunk's inputs are on their way,
+  // so the scatter into `out` overlaps the copy engine's host->device work.
+  const bool q_direct = direct_copyable(q), k_direct = direct_copyable(k),
+             v_direct = direct_copyable(v), out_direct = direct_copyable(out);
+  const bool out_staged = !out_direct && staging_enabled();
+  // Chunks of bn batch rows from b0 x g heads from h0.  The last chunk's kernels and its
+  // device->host copy run after every input has arrived, so with a page-locked `out` it is
+  // made small: the last uniform chunk is split into g/2, g/4 and g/4 heads (B=2, H=16,
+  // L=4096: the tail falls from 8 heads' 16.8 MB copy back to 2 heads'; 4.50-4.55 -> 4.37-4.45 ms
+  // per call, same box, interleaved).  A staged output keeps uniform chunks: there the host threads' scatter is the
+  // bound, and the extra chunk boundaries measured slower (5.18 -> 5.4-5.7 ms).
+  struct Chunk { int b0, bn, h0, g; };
+  std::vector<Chunk> chunks;
+  for (int c = 0; c < nb * ng; ++c) {
+    const int b0 = (c / ng) * Bc;
+    chunks.push_back({b0, min(Bc, B - b0), (c % ng) * G, G});
+  }
+  if (G % 4 == 0 && out_direct) {
+    const Chunk t = chunks.back();
+    chunks.back().g = G / 2;
+    chunks.push_back({t.b0, t.bn, t.h0 + G / 2, G / 4});
+    chunks.push_back({t.b0, t.bn, t.h0 + 3 * G / 4, G / 4});
+  }
+  const int nchunks = (int)chunks.size();
   const size_t nq = (size_t)B * S_q * H * D, nk = (size_t)B * S_kv * H * D;
   size_t off = 0;
   auto carve = [&](size_t bytes) { size_t o = off; off = align_up(off + bytes); return o; };
@@ -584,7 +612,10 @@ bool rt_attention(const float* q, const float* k, const float* v, const float* q
   int drc = ANIMA_OK;
   DeviceState* dev = current_device(&drc);
   if (!dev) return false;
-  const size_t ws_split = attn_workspace_bytes(Bc, G, S_q, S_kv, aflags, dev->sm_count);
+  size_t ws_split = 0;  // the largest any chunk's schedule needs; the chunks run in turn
+  for (const Chunk& ch : chunks)
+    ws_split = std::max(ws_split, attn_workspace_bytes(ch.bn, ch.g, S_q, S_kv, aflags,
+                                                       dev->sm_count));
   const size_t o_split = carve(ws_split);
   if (!rt_prepare(off)) return false;
   char* ws = static_cast<char*>(g_rt.ws);
@@ -612,33 +643,28 @@ bool rt_attention(const float* q, const float* k, const float* v, const float* q
   if (kv_valid && !rt_check(cudaMemcpyAsync(ws + o_valid, kv_valid, (size_t)B * 4,
                                             cudaMemcpyHostToDevice, sin), who))
     return bail();
-  const size_t row = (size_t)H * D * 4, crow = (size_t)G * D * 4;  // bytes: pitch, chunk row
-  // Pageable arrays go through the staging ring (h2d_rows / d2h_rows).  A staged output
-  // chunk is collected one chunk late, after the next chunk's inputs are on their way,
-  // so the scatter into `out` overlaps the copy engine's host->device work.
-  const bool q_direct = direct_copyable(q), k_direct = direct_copyable(k),
-             v_direct = direct_copyable(v), out_direct = direct_copyable(out);
-  const bool out_staged = !out_direct && staging_enabled();
-  auto chunk_geom = [&](int c, int& bn, size_t& qo, size_t& ko) {
-    const int b0 = (c / ng) * Bc, h0 = (c % ng) * G;
-    bn = min(Bc, B - b0);
-    qo = ((size_t)b0 * S_q * H + h0) * D;
-    ko = ((size_t)b0 * S_kv * H + h0) * D;
+  const size_t row = (size_t)H * D * 4;  // bytes: pitch of a token row
+  auto chunk_geom = [&](int c, int& bn, size_t& qo, size_t& ko, size_t& crow) {
+    const Chunk& ch = chunks[c];
+    bn = ch.bn;
+    qo = ((size_t)ch.b0 * S_q * H + ch.h0) * D;
+    ko = ((size_t)ch.b0 * S_kv * H + ch.h0) * D;
+    crow = (size_t)ch.g * D * 4;  // bytes of one token row of the chunk's heads
   };
   auto copy_out = [&](int c) {  // after chunk c's kernels
     int bn;
-    size_t qo, ko;
-    chunk_geom(c, bn, qo, ko);
+    size_t qo, ko, crow;
+    chunk_geom(c, bn, qo, ko, crow);
     if (!rt_check(cudaStreamWaitEvent(sout, g_rt.ev_done[c], 0), who)) return false;
     return d2h_rows(reinterpret_cast<char*>(out + qo), row,
                     reinterpret_cast<const char*>(dout + qo), row, crow, (size_t)bn * S_q, sout,
                     out_direct, who);
   };
   for (int c = 0; c < nchunks; ++c) {
-    const int b0 = (c / ng) * Bc;
+    const int b0 = chunks[c].b0, g = chunks[c].g;
     int bn;
-    size_t qo, ko;
-    chunk_geom(c, bn, qo, ko);
+    size_t qo, ko, crow;
+    chunk_geom(c, bn, qo, ko, crow);
     // ---- copy in
     auto in = [&](float* d, const float* h, size_t off, int S, bool direct) {
       return h2d_rows(reinterpret_cast<char*>(d + off), row,
@@ -667,7 +693,7 @@ bool rt_attention(const float* q, const float* k, const float* v, const float* q
       pa.v_stride[i] = sk3[i];
     }
     pa.B = bn;
-    pa.H = G;
+    pa.H = g;
     pa.S_q = S_q;
     pa.S_kv = S_kv;
     pa.D = D;
@@ -696,7 +722,7 @@ bool rt_attention(const float* q, const float* k, const float* v, const float* q
     aa.out_stride[1] = D;
     aa.out_stride[2] = (int64_t)H * D;
     aa.B = bn;
-    aa.H = G;
+    aa.H = g;
     aa.S_q = S_q;
     aa.S_kv = S_kv;
     aa.D = D;

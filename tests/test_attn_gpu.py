@@ -84,11 +84,12 @@ def test_fused_host_entry_vs_reference_composition(aa):
 
 
 @pytest.mark.parametrize("B,H,Sq,Skv,masked", [(3, 6, 160, 200, True), (9, 1, 96, 96, False),
-                                                (2, 16, 64, 64, False)])
+                                                (2, 16, 64, 64, False), (1, 8, 300, 200, True)])
 def test_host_entry_chunks_vs_oracle(aa, O, B, H, Sq, Skv, masked):
     """anima_rt_run_attention pipelines the call over (batch rows x head group) chunks;
-    odd B and H, a short last chunk (B=9, H=1 -> chunks of 2 rows) and per-sample key
-    padding all map back to the right output rows."""
+    odd B and H, a short last chunk (B=9, H=1 -> chunks of 2 rows), a last chunk split into
+    g/2 + g/4 + g/4 heads (H=16 and H=8) and per-sample key padding all map back to the right
+    output rows."""
     from anima_attn import _lib as L
     rng = np.random.default_rng(B * 100 + H)
     q = rng.standard_normal((B, Sq, H, 128), dtype=np.float32)
@@ -96,7 +97,9 @@ def test_host_entry_chunks_vs_oracle(aa, O, B, H, Sq, Skv, masked):
     v = rng.standard_normal((B, Skv, H, 128), dtype=np.float32)
     qw = (1 + 0.1 * rng.standard_normal(128)).astype(np.float32)
     valid = rng.integers(1, Skv + 1, size=B).astype(np.int32) if masked else None
-    out = np.zeros((B, Sq, H, 128), dtype=np.float32)
+    # a page-locked output where the head count lets the library split the last chunk
+    keep = torch.zeros((B, Sq, H, 128), dtype=torch.float32, pin_memory=(H % 8 == 0))
+    out = keep.numpy()
     ok = L.lib.anima_rt_run_attention(
         q.ctypes.data, k.ctypes.data, v.ctypes.data, qw.ctypes.data, None, None,
         None if valid is None else valid.ctypes.data, out.ctypes.data, B, Sq, Skv, H, 128,
