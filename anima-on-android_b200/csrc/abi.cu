@@ -328,6 +328,9 @@ class CopyPool {
     int n = 1;
     cpu_set_t set;
     if (sched_getaffinity(0, sizeof(set), &set) == 0) n = CPU_COUNT(&set);
+    // One process per GPU (torchrun sets LOCAL_WORLD_SIZE): the processes of this host
+    // share its cores, so each takes its share.
+    if (const char* w = std::getenv("LOCAL_WORLD_SIZE")) n /= std::max(1, std::atoi(w));
     if (const char* e = std::getenv("ANIMA_RT_COPY_THREADS")) n = std::atoi(e);
     n = std::max(1, std::min(n, 16));
     nworkers_ = n - 1;

@@ -99,7 +99,8 @@ bool anima_rt_run_gemm_bf16(const float* A, const uint16_t* W, float* C, int M, 
  * flags: 1 = q norm, 2 = k norm, 4 = RoPE, 16 = causal (bit values of ANIMA_FLAG_*).
  * Host buffers in page-locked memory are copied by the copy engine directly (full PCIe
  * speed).  Ordinary pageable arrays above 1 MiB are copied through the library's own
- * page-locked ring by up to 16 host threads (ANIMA_RT_COPY_THREADS; ANIMA_RT_STAGE=0
+ * page-locked ring by up to 16 host threads (the process's CPUs, divided by torchrun's
+ * LOCAL_WORLD_SIZE when set; ANIMA_RT_COPY_THREADS overrides; ANIMA_RT_STAGE=0
  * leaves them to the CUDA driver's single-threaded copies); the same holds for the
  * other host entries above. */
 bool anima_rt_run_attention(const float* q, const float* k, const float* v, const float* q_w,
