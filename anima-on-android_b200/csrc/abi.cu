@@ -382,12 +382,17 @@ bool direct_copyable(const void* p) {
 constexpr size_t kStageMin = size_t(1) << 20;
 static_assert(kStageSlot >= kStageMin, "a staged copy fills at least one row per slot");
 
+// The ring, allocated on first use.  If the host cannot page-lock it, the copies go to the
+// driver instead (slower, same result) and the allocation is not retried.
 bool stage_ring() {
+  static bool failed = false;
   if (g_rt.ring) return true;
+  if (failed) return false;
   void* p = nullptr;
   if (cudaHostAlloc(&p, kStageSlots * kStageSlot, cudaHostAllocPortable) != cudaSuccess) {
     cudaGetLastError();
-    return rt_fail("cudaHostAlloc of the staging ring failed");
+    failed = true;
+    return false;
   }
   g_rt.ring = static_cast<char*>(p);
   return true;
@@ -412,10 +417,10 @@ void copy_rows(char* dst, size_t dpitch, const char* src, size_t spitch, size_t 
 bool h2d_rows(char* dst, size_t dpitch, const char* src, size_t spitch, size_t width,
               size_t rows, cudaStream_t s, bool direct, const char* who) {
   if (!rows || !width) return true;
-  if (direct || !staging_enabled() || width * rows < kStageMin || width > kStageSlot)
+  if (direct || !staging_enabled() || width * rows < kStageMin || width > kStageSlot ||
+      !stage_ring())
     return rt_check(cudaMemcpy2DAsync(dst, dpitch, src, spitch, width, rows,
                                       cudaMemcpyHostToDevice, s), who);
-  if (!stage_ring()) return false;
   const size_t per = kStageSlot / width;
   for (size_t r0 = 0; r0 < rows; r0 += per) {
     const size_t n = std::min(per, rows - r0);
@@ -437,10 +442,10 @@ bool h2d_rows(char* dst, size_t dpitch, const char* src, size_t spitch, size_t w
 bool d2h_rows(char* dst, size_t dpitch, const char* src, size_t spitch, size_t width,
               size_t rows, cudaStream_t s, bool direct, const char* who) {
   if (!rows || !width) return true;
-  if (direct || !staging_enabled() || width * rows < kStageMin || width > kStageSlot)
+  if (direct || !staging_enabled() || width * rows < kStageMin || width > kStageSlot ||
+      !stage_ring())
     return rt_check(cudaMemcpy2DAsync(dst, dpitch, src, spitch, width, rows,
                                       cudaMemcpyDeviceToHost, s), who);
-  if (!stage_ring()) return false;
   const size_t per = kStageSlot / width;
   struct Piece { int slot; size_t r0, n; };
   Piece q[kStageOut];
@@ -579,7 +584,8 @@ bool rt_attention(const float* q, const float* k, const float* v, const float* q
   // so the scatter into `out` overlaps the copy engine's host->device work.
   const bool q_direct = direct_copyable(q), k_direct = direct_copyable(k),
              v_direct = direct_copyable(v), out_direct = direct_copyable(out);
-  const bool out_staged = !out_direct && staging_enabled();
+  const bool out_staged = !out_direct && staging_enabled() &&
+                          (size_t)G * D * 4 <= kStageSlot && stage_ring();
   // Chunks of bn batch rows from b0 x g heads from h0.  The last chunk's kernels and its
   // device->host copy run after every input has arrived, so with a page-locked `out` it is
   // made small: the last uniform chunk is split into g/2, g/4 and g/4 heads (B=2, H=16,
